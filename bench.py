@@ -1,0 +1,432 @@
+"""Benchmark: batch-1 greedy decode tok/s of Qwen3-0.6B (bf16) at ~1k context.
+
+Workload: seeded random-init Qwen3-0.6B weights; a
+1024-token uniform-random prompt is prefilled (untimed, forced decode steps),
+then every bench step is ONE kernel launch that greedily generates 512 tokens
+from position 1023 (the reference's generate_nosync semantics), i.e. cache
+positions 1023..1534.  Weights (1.19 GB) are streamed from HBM every token, so
+the inputs are far larger than the 126 MB L2 and no flush is needed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's own PyTorch path (HF Qwen3ForCausalLM,
+bf16, qwen_megakernel/bench.py:19-55) on the host CPU cores, on the same
+workload, bounded to a few decode tokens per step.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs an independent
+replica with its own prompt seed; no collective on the data path.  Rank 0
+prints one JSON line with the whole-job throughput (tokens of all ranks over
+the max device time of the ranks).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "batch-1 decode tok/s (Qwen3-0.6B bf16, ctx 1k)"
+PROMPT_LEN = 1024
+GEN_TOKENS = 512
+WEIGHT_BYTES = 1_192_101_888  # per token: 28 layers' linears + norms + embed row + LM head
+KV_BYTES_PER_POS = 114_688  # 28 layers x 8 KV heads x 128 dims x (K, V) x 2 B
+WORKLOAD = (
+    "configs[1]: Qwen3-0.6B (random init, seed 0) batch-1 greedy decode of 512 tokens after a "
+    "1024-token random-id prompt (cache positions 1023..1534), one launch per 512 tokens"
+)
+
+
+def kv_bytes(first_pos: int, n: int) -> int:
+    """Algorithmic KV bytes of n tokens at positions first_pos..first_pos+n-1:
+    a token at position p reads p cached positions and writes one."""
+    return KV_BYTES_PER_POS * sum(p + 1 for p in range(first_pos, first_pos + n))
+
+
+def launch_bytes() -> int:
+    return GEN_TOKENS * WEIGHT_BYTES + kv_bytes(PROMPT_LEN - 1, GEN_TOKENS)
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic_per_token():
+    """DRAM bytes per decoded token from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "decode_kernel_traffic.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["dram_bytes_per_token"])
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = (
+        "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+        "clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"],
+                stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL,
+                text=True,
+            )
+        except OSError:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(smax) if smax else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def init_dist(ws: int, local: int):
+    if ws <= 1:
+        return False
+    import datetime
+
+    import torch.distributed as dist
+
+    backend = "nccl" if torch.cuda.is_available() else "gloo"
+    kw = {}
+    if backend == "nccl":
+        kw["device_id"] = torch.device("cuda", local)
+    dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120), **kw)
+    return True
+
+
+def reduce_max(x: float, distributed: bool) -> float:
+    if not distributed:
+        return x
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend() == "nccl" else torch.device("cpu")
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(distributed: bool):
+    if distributed:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def prompt_for_rank(rank: int) -> list[int]:
+    rng = np.random.Generator(np.random.PCG64(2 + rank))
+    return [int(x) for x in rng.integers(0, 151936, size=PROMPT_LEN)]
+
+
+# ------------------------------------------------------------------ CPU legs
+def cpu_reference_rate(weights_cpu: dict, prompt: list[int], tokens_per_step: int, steps: int, warmup: int):
+    """HF Qwen3ForCausalLM bf16 (the reference's PyTorch path) on the host CPU:
+    prefill the prompt once (untimed), then time greedy decode of
+    `tokens_per_step` tokens per step from the prompt's KV cache."""
+    from oracle.hf_reference import build_hf_model
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    model = build_hf_model(weights_cpu, torch.bfloat16)
+    with torch.no_grad():
+        out = model(input_ids=torch.tensor([prompt[:-1]]), use_cache=True, logits_to_keep=1)
+        base_cache = out.past_key_values
+
+        def one_step():
+            import copy
+
+            cache = copy.deepcopy(base_cache)
+            tok = prompt[-1]
+            for _ in range(tokens_per_step):
+                o = model(input_ids=torch.tensor([[tok]]), past_key_values=cache, use_cache=True)
+                cache = o.past_key_values
+                tok = int(o.logits[0, -1].argmax())
+
+        for _ in range(warmup):
+            one_step()
+        times = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            one_step()
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    return tokens_per_step * steps / total, total * 1000.0 / steps, torch.get_num_threads()
+
+
+def run_reference_arm(args):
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    from qwen_megakernel_b200.weights import random_weights
+
+    t0 = time.time()
+    weights = random_weights(seed=0, device="cpu", max_seq_len=2048)
+    prompt = prompt_for_rank(0)
+    tps = 4
+    value, ms, cores = cpu_reference_rate(weights, prompt, tps, args.steps, max(1, min(args.warmup, 1)))
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "tok/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
+        "config": {
+            "workload": WORKLOAD,
+            "sample": f"{tps} greedy tokens per step from position {PROMPT_LEN - 1} after an untimed prefill",
+        },
+        "cpu_baseline": {
+            "value": round(value, 3),
+            "unit": "tok/s",
+            "cores": cores,
+            "kind": "reference",
+            "sample": f"HF Qwen3ForCausalLM bf16 on CPU, {tps} decode tokens x {args.steps} steps at ctx ~1k",
+        },
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "setup_seconds": round(time.time() - t0, 1),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    ws, rank, local = dist_env()
+    distributed = init_dist(ws, local)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    from qwen_megakernel_b200 import Decoder
+    from qwen_megakernel_b200._native import loaded_library_paths
+    from qwen_megakernel_b200.weights import random_weights
+
+    weights_cpu = random_weights(seed=0, device="cpu", max_seq_len=2048)
+    weights = {
+        k: ([t.to(dev) for t in v] if isinstance(v, list) else v.to(dev)) for k, v in weights_cpu.items()
+    }
+    weights["lm_head_weight"] = weights["embed_weight"]
+    dec = Decoder(weights, max_seq_len=2048)
+    prompt = prompt_for_rank(rank)
+    dec.prefill(prompt[:-1])  # positions 0..1022
+    start = PROMPT_LEN - 1
+    log = torch.empty(GEN_TOKENS, dtype=torch.int32, device=dev)
+    first = torch.tensor([prompt[-1]], dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        dec.decode_steps(GEN_TOKENS, forced_tokens=first, start_position=start, output_log=log)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    dec.check_status()
+
+    sampler = ClockSampler(local)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier(distributed)
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    t_all0 = torch.cuda.Event(enable_timing=True)
+    t_all1 = torch.cuda.Event(enable_timing=True)
+    t_all0.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    t_all1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    barrier(distributed)
+    dec.check_status()
+    local_ms = t_all0.elapsed_time(t_all1)
+    per_launch_ms = [a.elapsed_time(b) for a, b in ev]
+    max_ms = reduce_max(local_ms, distributed)
+
+    # end to end through the public API (host token in, host tokens out)
+    e2e_ev0, e2e_ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dec.generate_from(prompt[-1], GEN_TOKENS, position=start)  # warm
+    barrier(distributed)
+    torch.cuda.synchronize(dev)
+    e2e_ev0.record(stream)
+    t_host0 = time.perf_counter()
+    for _ in range(args.steps):
+        dec.generate_from(prompt[-1], GEN_TOKENS, position=start)
+    e2e_ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_host_ms = (time.perf_counter() - t_host0) * 1000.0
+    e2e_ms = max(e2e_ev0.elapsed_time(e2e_ev1), e2e_host_ms)
+    e2e_max = reduce_max(e2e_ms, distributed)
+    barrier(distributed)
+
+    tokens_total = args.steps * GEN_TOKENS * ws
+    value = tokens_total / (max_ms / 1000.0)
+    e2e_value = tokens_total / (e2e_max / 1000.0)
+
+    cpu_baseline = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        try:
+            v, ms, cores = cpu_reference_rate(weights_cpu, prompt, 8, 2, 1)
+            cpu_baseline = {
+                "value": round(v, 3),
+                "unit": "tok/s",
+                "cores": cores,
+                "kind": "reference",
+                "sample": "HF Qwen3ForCausalLM bf16 on the host CPU (the reference's PyTorch path): "
+                "1023-token prefill untimed, then 2 x 8 greedy decode tokens at ctx ~1k",
+            }
+        except Exception as e:  # the baseline is informative; never fail the bench on it
+            cpu_baseline = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
+                            "sample": f"failed: {type(e).__name__}: {e}"}
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        lb = launch_bytes()
+        mean_launch_ms = statistics.mean(per_launch_ms)
+        achieved = lb / (mean_launch_ms / 1000.0) / 1e9
+        tpt = profiled_traffic_per_token()
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "tok/s",
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(max_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
+            "config": {
+                "workload": WORKLOAD,
+                "batch": 1,
+                "prompt_len": PROMPT_LEN,
+                "gen_tokens_per_step": GEN_TOKENS,
+                "accumulate": "fp32",
+                "parallelism": f"replicas x{ws} (independent decode stream per GPU, no collective)",
+                "l2": "no flush: 1.19 GB of weights streamed per token >> 126 MB L2",
+            },
+            "roofline": {
+                "bound": "hbm",
+                "achieved": round(achieved, 1),
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "traffic": (round(tpt * GEN_TOKENS) if tpt else None),
+                "peak_kind": peak_kind,
+                "algorithmic_bytes_per_launch": lb,
+                "kernel": "qmk::decode_kernel",
+            },
+            "e2e": {
+                "value": round(e2e_value, 2),
+                "unit": "tok/s",
+                "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4 * GEN_TOKENS,
+            },
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "per_token_us": round(max_ms / args.steps / GEN_TOKENS * 1000.0, 2),
+            "native_libraries": [os.path.basename(p) for p in loaded_library_paths()],
+        }
+        if cpu_baseline is not None:
+            line["cpu_baseline"] = cpu_baseline
+        print(json.dumps(line), flush=True)
+
+    if distributed:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,203 @@
+/*
+ * qwen_megakernel.h -- C ABI of the B200 (sm_100a) Qwen3-0.6B decode megakernel.
+ *
+ * Everything here is plain C: raw device pointers, sizes, int/float scalars and
+ * a cudaStream_t.  No torch types cross this boundary.  The shared library
+ * libqwen_megakernel.so exports every function declared below.
+ *
+ * Reference interface this library replaces (AlpinDale/qwen_megakernel):
+ *   - struct LDGLayerWeights          csrc/kernel.cu:76-88, csrc/torch_bindings.cpp:21-33
+ *   - launch_ldg_decode_persistent    csrc/kernel.cu:1507, declared csrc/torch_bindings.cpp:35-43
+ *   - launch_ldg_decode_direct        csrc/kernel.cu:1477, declared csrc/torch_bindings.cpp:45-53
+ *   - launch_ldg_generate_nosync      csrc/kernel.cu:1547, declared csrc/torch_bindings.cpp:83-91
+ * The three reference entry points keep their exact signatures and argument
+ * meaning.  The qmk_* functions are additions (explicit workspace, forced
+ * token streams, optional fp32 logits, error read-back, schedule queries).
+ *
+ * Data layouts (identical to the reference):
+ *   embed_weight / lm_head_weight  bf16 [151936, 1024] row-major (tied)
+ *   layer weights                  bf16 row-major [out, in] (HF nn.Linear)
+ *   cos_table / sin_table          bf16 [rows >= last position + 1, 128]
+ *                                  (rotate-half layout, halves duplicated)
+ *   k_cache / v_cache              bf16 [num_layers, 8, max_seq_len, 128]
+ */
+#ifndef QWEN_MEGAKERNEL_H_
+#define QWEN_MEGAKERNEL_H_
+
+#include <stddef.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Model geometry (Qwen3-0.6B; reference qwen_megakernel/model.py:8-16). */
+#define QMK_HIDDEN 1024
+#define QMK_INTERMEDIATE 3072
+#define QMK_NUM_Q_HEADS 16
+#define QMK_NUM_KV_HEADS 8
+#define QMK_HEAD_DIM 128
+#define QMK_VOCAB 151936
+#define QMK_MAX_LAYERS 64
+
+/* Per-layer weight pointer table: 11 device pointers, 88 bytes, in the
+ * reference order (csrc/kernel.cu:76-88; packed by model.py:97-108). */
+typedef struct LDGLayerWeights {
+  const void *input_layernorm_weight;     /* bf16 [1024]        */
+  const void *q_proj_weight;              /* bf16 [2048, 1024]  */
+  const void *k_proj_weight;              /* bf16 [1024, 1024]  */
+  const void *v_proj_weight;              /* bf16 [1024, 1024]  */
+  const void *q_norm_weight;              /* bf16 [128]         */
+  const void *k_norm_weight;              /* bf16 [128]         */
+  const void *o_proj_weight;              /* bf16 [1024, 2048]  */
+  const void *post_attn_layernorm_weight; /* bf16 [1024]        */
+  const void *gate_proj_weight;           /* bf16 [3072, 1024]  */
+  const void *up_proj_weight;             /* bf16 [3072, 1024]  */
+  const void *down_proj_weight;           /* bf16 [1024, 3072]  */
+} LDGLayerWeights;
+
+/* ------------------------------------------------------------------------- */
+/* Reference entry points (same signatures as the reference).                */
+/* They run on a library-owned workspace, one per device, allocated on first  */
+/* use.  Like the reference's process-global barrier state (kernel.cu:1446-   */
+/* 1473), that workspace is shared: concurrent calls on different streams of */
+/* the same device race.  The scratch-buffer arguments (hidden_buffer ..      */
+/* block_max_idxs) are accepted for ABI compatibility; only `g_normalized`    */
+/* is written (the final RMSNorm output, fp32 [1024], as in the reference).   */
+/* Errors: these return void; query qmk_get_last_error() after the call and  */
+/* qmk_read_default_status() after a stream synchronize.                      */
+/* ------------------------------------------------------------------------- */
+
+/* One decode step: input_token_id at `position`; writes the greedy argmax to
+ * *output_token_id (device int32).  Reference: csrc/kernel.cu:1477. */
+void launch_ldg_decode_direct(
+    int input_token_id, int *output_token_id, const void *embed_weight,
+    const LDGLayerWeights *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight, const void *cos_table, const void *sin_table,
+    void *k_cache, void *v_cache, void *hidden_buffer, void *g_activations,
+    void *g_residual, void *g_q, void *g_k, void *g_v, void *g_attn_out,
+    void *g_mlp_intermediate, void *g_normalized, void *block_max_vals,
+    void *block_max_idxs, int num_layers, int position, int max_seq_len,
+    float attn_scale, cudaStream_t stream);
+
+/* Same step; `cache_len` is accepted and ignored (the reference kernel also
+ * derives it as position + 1).  Reference: csrc/kernel.cu:1507. */
+void launch_ldg_decode_persistent(
+    int input_token_id, int *output_token_id, const void *embed_weight,
+    const LDGLayerWeights *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight, const void *cos_table, const void *sin_table,
+    void *k_cache, void *v_cache, void *hidden_buffer, void *g_activations,
+    void *g_residual, void *g_q, void *g_k, void *g_v, void *g_attn_out,
+    void *g_mlp_intermediate, void *g_normalized, void *block_max_vals,
+    void *block_max_idxs, int num_layers, int position, int cache_len,
+    int max_seq_len, float attn_scale, cudaStream_t stream);
+
+/* num_steps greedy steps with device-side token feedback, no host sync:
+ * step t consumes (t == 0 ? first_token_id : output_log[t-1]) at position
+ * start_position + t and writes output_log[t].  Reference: kernel.cu:1547
+ * (there: 4 launches per token; here: one launch for all steps). */
+void launch_ldg_generate_nosync(
+    int first_token_id, int num_steps, const void *embed_weight,
+    const LDGLayerWeights *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight, const void *cos_table, const void *sin_table,
+    void *k_cache, void *v_cache, void *hidden_buffer, void *g_activations,
+    void *g_residual, void *g_q, void *g_k, void *g_v, void *g_attn_out,
+    void *g_mlp_intermediate, void *g_normalized, void *block_max_vals,
+    void *block_max_idxs, int *output_log, int num_layers, int start_position,
+    int max_seq_len, float attn_scale, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Extended API (no reference counterpart: additions of this library).       */
+/* ------------------------------------------------------------------------- */
+
+/* Error codes (returned by qmk_* functions and written to the status block). */
+#define QMK_OK 0
+#define QMK_ERR_ARGS 1          /* invalid argument (host-side validation)   */
+#define QMK_ERR_CUDA 2          /* a CUDA runtime call failed                */
+#define QMK_ERR_LAUNCH 3        /* cooperative launch refused (co-residency) */
+#define QMK_ERR_TIMEOUT 4       /* a bounded device-side wait expired        */
+#define QMK_ERR_TOKEN 5         /* token id outside [0, vocab) on device     */
+#define QMK_ERR_WORKSPACE 6     /* workspace too small / misaligned          */
+
+/* Host-visible status written by the kernel when it finishes (last CTA).
+ * Lives in pinned, device-mapped host memory supplied by the caller. */
+typedef struct QmkStatus {
+  unsigned int error_code;  /* QMK_* device error of the last launch (0 = ok) */
+  unsigned int error_info;  /* (cta << 16) | (site << 8) | layer              */
+  unsigned int launches;    /* number of launches that completed              */
+  unsigned int epoch;       /* flag epoch after the launch                    */
+} QmkStatus;
+
+typedef struct QmkRunArgs {
+  const void *embed_weight;              /* bf16 [151936, 1024]               */
+  const LDGLayerWeights *layer_weights;  /* device array [num_layers]         */
+  const void *final_norm_weight;         /* bf16 [1024]                       */
+  const void *lm_head_weight;            /* bf16 [151936, 1024]               */
+  const void *cos_table;                 /* bf16 [>= start+steps, 128]        */
+  const void *sin_table;                 /* bf16 [>= start+steps, 128]        */
+  void *k_cache;                         /* bf16 [num_layers,8,max_seq,128]   */
+  void *v_cache;
+  void *workspace;                       /* device, qmk_workspace_bytes()     */
+  size_t workspace_bytes;
+  const int *forced_tokens;              /* device int32 [n_forced] or NULL   */
+  int n_forced;                          /* steps t < n_forced read forced[t] */
+  int first_token;                       /* step-0 token when n_forced == 0   */
+  int start_position;
+  int num_steps;
+  int num_layers;
+  int max_seq_len;
+  float attn_scale;
+  int *output_log;                       /* device int32 [num_steps] or NULL  */
+  int *output_token;                     /* device int32 [1] or NULL          */
+  float *logits;                         /* device fp32 [num_steps,151936] / NULL */
+  float *final_hidden;                   /* device fp32 [1024] or NULL        */
+  QmkStatus *status;                     /* mapped pinned host memory or NULL */
+  unsigned long long timeout_ns;         /* per-wait limit; 0 = 1 s default   */
+  int debug_stall;                       /* test hook, 0 = off; k > 0: CTA k-1 */
+                                         /* waits (step 0, layer 0, O-proj input) */
+                                         /* on a flag no CTA writes, so its       */
+                                         /* bounded wait expires: the launch ends */
+                                         /* with QMK_ERR_TIMEOUT in the status    */
+} QmkRunArgs;
+
+/* Bytes of device workspace one decoder needs (flags, dataflow buffers). */
+size_t qmk_workspace_bytes(void);
+
+/* Zero a workspace (stream-ordered).  Must be called once before first use. */
+int qmk_workspace_init(void *workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Launch the persistent decode kernel for args->num_steps steps (one
+ * cooperative launch).  Returns QMK_OK or a host-side error code; device-side
+ * errors are reported through args->status after the stream completes. */
+int qmk_run(const QmkRunArgs *args, cudaStream_t stream);
+
+/* Host-side error of the last qmk_* / launch_ldg_* call on this thread. */
+int qmk_get_last_error(void);
+const char *qmk_get_last_error_message(void);
+const char *qmk_error_string(int code);
+
+/* Status of the library-owned default workspace of the current device (used
+ * by the three reference entry points).  Valid after a stream synchronize. */
+int qmk_read_default_status(QmkStatus *out);
+
+/* Number of CTAs (one per SM) the kernel launches on `device`. */
+int qmk_num_ctas(int device);
+
+/* KV splits per KV head the kernel uses for a launch whose last position is
+ * `max_position` on `num_ctas` CTAs. */
+int qmk_attention_splits(int num_ctas, int max_position);
+
+/* Host-side description of the static work partition, for tests: fills
+ * out[0..7] for CTA `cta` of `num_ctas` with
+ *   {qkv_row0, qkv_row1, o_row0, o_row1, gu_row0, gu_row1, d_row0, d_row1}
+ * and out[8..11] with {lm_row0, lm_row1, item (or -1), merge_task (or -1)}. */
+int qmk_describe_partition(int num_ctas, int splits, int cta, int *out, int out_len);
+
+/* Library version string. */
+const char *qmk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN_MEGAKERNEL_H_ */

@@ -1,0 +1,1397 @@
+// Persistent decode megakernel for Qwen3-0.6B on B200 (sm_100a), plus the C ABI.
+//
+// Structure (one cooperative launch runs `num_steps` greedy decode steps):
+//   * one CTA per SM (148 on B200), 288 threads: 8 consumer warps + 1 producer warp;
+//   * the producer warp streams every byte the CTA will read (its slice of each
+//     weight matrix, its KV-cache chunk, its LM-head rows) through a 6 x 32 KB
+//     shared-memory ring with 1-D TMA bulk copies (cp.async.bulk) and mbarriers.
+//     Weights do not depend on activations, so the ring runs ahead across every
+//     dependency point and keeps HBM busy while consumers wait;
+//   * there is no grid barrier.  Each phase output element is written exactly
+//     once per (step, layer) as an 8-byte word (fp32 value | epoch flag << 32);
+//     consumers poll the words they need until the flag matches.  A dependency
+//     therefore costs one L2 write->read latency instead of fence + atomic
+//     barrier + re-read.
+//   * per layer: P1 RMSNorm+QKV rows -> P2 QK-norm/RoPE/KV-append + split-KV
+//     attention items -> P2.5 merge of the split partials -> P3 O-proj rows +
+//     residual -> P4 RMSNorm + gate/up rows + SiLU -> P5 down rows + residual;
+//     after the last layer the final RMSNorm + tied LM head + grid-wide argmax.
+//
+// Numerics follow the reference kernel (fp32 activations and accumulation,
+// bf16 weights, bf16 K/V cache, bf16 cos/sin tables), except that the residual
+// stream between layers stays fp32 (the reference rounds it to bf16,
+// csrc/kernel.cu:859), which keeps the result closer to the fp32 evaluation of
+// the HF PyTorch path the reference compares against.
+//
+// Every wait is bounded: an mbarrier or flag wait that exceeds timeout_ns
+// records an error in the workspace control block, poisons the CTA (no further
+// copies or stores), drains its in-flight copies and exits; the last CTA to
+// exit publishes the error to the host-visible status block.
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "qmk_device.cuh"
+#include "qmk_schedule.h"
+#include "qwen_megakernel.h"
+
+namespace qmk {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;
+constexpr float kRmsEps = 1e-6f;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s
+constexpr unsigned kEpochWrap = 0xF0000000u;
+
+enum Site : unsigned {
+  kSiteFull = 1,
+  kSiteEmpty = 2,
+  kSiteX = 3,
+  kSiteQKV = 4,
+  kSitePart = 5,
+  kSiteAtt = 6,
+  kSiteA = 7,
+  kSiteM = 8,
+  kSiteArg = 9,
+  kSiteKVReady = 10,
+  kSiteToken = 11,
+};
+
+struct Params {
+  const __nv_bfloat16 *embed;
+  const LDGLayerWeights *layers;
+  const __nv_bfloat16 *final_norm;
+  const __nv_bfloat16 *lm_head;
+  const __nv_bfloat16 *cos_t;
+  const __nv_bfloat16 *sin_t;
+  __nv_bfloat16 *k_cache;
+  __nv_bfloat16 *v_cache;
+  uint8_t *ws;
+  const int *forced;
+  int n_forced;
+  int first_token;
+  int start_pos;
+  int num_steps;
+  int num_layers;
+  int max_seq_len;
+  float attn_scale;
+  int splits;
+  int *out_log;
+  int *out_token;
+  float *logits;
+  float *final_hidden;
+  QmkStatus *status;
+  unsigned long long timeout_ns;
+  int debug_stall;
+};
+
+// Dynamic shared memory plan (bytes).
+constexpr int kSmRing = 0;
+constexpr int kSmX = kNumSlots * kSlotBytes;   // layer input residual, fp32 [1024]
+constexpr int kSmA = kSmX + 4 * kHidden;       // post-attention residual, fp32 [1024]
+constexpr int kSmAtt = kSmA + 4 * kHidden;     // attention output, fp32 [2048]
+constexpr int kSmU = kSmAtt + 4 * kQSize;      // MLP intermediate / attention scratch, fp32 [3072]
+constexpr int kSmMisc = kSmU + 4 * kInter;
+constexpr int kSmBytes = kSmMisc + 256;
+static_assert(kSmBytes <= 232448, "shared memory plan exceeds the sm_100 per-block limit");
+
+// Attention scratch inside the U region (floats).
+constexpr int kUQ = 0;      // q, 2 heads [256]
+constexpr int kUK = 256;    // k [128]
+constexpr int kUV = 384;    // v [128]
+constexpr int kUKn = 512;   // new k after norm/RoPE, bf16-rounded [128]
+constexpr int kUVn = 640;   // new v, bf16-rounded [128]
+constexpr int kUPW = 768;   // per-warp partials [8][260]
+static_assert(kUPW + kConsumerWarps * kPartWords <= kInter, "attention scratch too large");
+static_assert(kMaxSplits * kMergeWordsPerSplit <= kInter, "merge scratch too large");
+
+struct Ctx {
+  uint8_t *ring;
+  uint64_t *full;
+  uint64_t *empty;
+  volatile int *abort_flag;
+  float *warp_best_v;
+  int *warp_best_i;
+  int *token_slot;
+  Ctrl *ctrl;
+  uint64_t *wX, *wQKV, *wPart, *wAtt, *wA, *wM, *wArg;
+  int cta, ncta;
+  unsigned E0;
+  unsigned long long timeout_ns;
+  int cur_layer;
+};
+
+__device__ __forceinline__ unsigned epoch_of(const Ctx &c, int step, int layer, int num_layers) {
+  return c.E0 + 1u + (unsigned)step * (unsigned)(num_layers + 1) + (unsigned)layer;
+}
+
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ void raise_error(Ctx &c, unsigned code, unsigned site) {
+  *c.abort_flag = 1;
+  if (atomicCAS(&c.ctrl->err_code, 0u, code) == 0u) {
+    atomicExch(&c.ctrl->err_info,
+               ((unsigned)c.cta << 16) | ((site & 0xffu) << 8) | ((unsigned)c.cur_layer & 0xffu));
+  }
+}
+
+// Bounded-wait bookkeeping: call keep_going() once per failed poll.
+struct Waiter {
+  uint64_t deadline = 0;
+  unsigned it = 0;
+  __device__ __forceinline__ bool keep_going(Ctx &c, unsigned site) {
+    ++it;
+    if ((it & 15u) == 0u) {
+      if (*c.abort_flag) return false;
+      const uint64_t now = global_timer_ns();
+      if (deadline == 0) {
+        deadline = now + c.timeout_ns;
+      } else if (now > deadline || it > (1u << 30)) {
+        raise_error(c, QMK_ERR_TIMEOUT, site);
+        return false;
+      }
+      if ((it & 1023u) == 0u && ld_relaxed_u32(&c.ctrl->err_code) != 0u) {
+        *c.abort_flag = 1;  // another CTA failed: stop waiting for it
+        return false;
+      }
+      if (it > 64u) __nanosleep(64);
+    }
+    return true;
+  }
+};
+
+// ------------------------------------------------------------- ring (consumer)
+__device__ __forceinline__ bool wait_full(Ctx &c, uint32_t tile) {
+  bool ok = (*c.abort_flag == 0);
+  if (ok) {
+    const int slot = tile % kNumSlots;
+    const unsigned par = (tile / kNumSlots) & 1u;
+    Waiter w;
+    while (!mbar_try_wait(&c.full[slot], par)) {
+      if (!w.keep_going(c, kSiteFull)) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ void release_tile(Ctx &c, uint32_t tile, bool ok) {
+  __syncwarp();
+  if (ok && (threadIdx.x & 31) == 0) mbar_arrive(&c.empty[tile % kNumSlots]);
+}
+
+__device__ __forceinline__ const uint8_t *slot_ptr(const Ctx &c, uint32_t tile) {
+  return c.ring + (tile % kNumSlots) * kSlotBytes;
+}
+
+// ------------------------------------------------------------- LL staging
+// All 256 consumer threads: poll N = 512*P words of `src` (flag == expected)
+// into fp32 `dst`, then consumer_sync().
+template <int P>
+__device__ void stage_vec(Ctx &c, float *dst, const uint64_t *src, unsigned flag, unsigned site) {
+  const int tid = threadIdx.x;
+  unsigned pending = (1u << P) - 1u;
+  if (*c.abort_flag) pending = 0;
+  Waiter w;
+  while (pending) {
+    uint64_t a[P], b[P];
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      a[k] = 0;
+      b[k] = 0;
+      if (pending & (1u << k)) ll_load2(src + 2 * (k * kConsumerThreads + tid), a[k], b[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      if ((pending & (1u << k)) && ll_flag(a[k]) == flag && ll_flag(b[k]) == flag) {
+        reinterpret_cast<float2 *>(dst)[k * kConsumerThreads + tid] =
+            make_float2(ll_value(a[k]), ll_value(b[k]));
+        pending &= ~(1u << k);
+      }
+    }
+    if (pending && !w.keep_going(c, site)) break;
+  }
+  consumer_sync();
+}
+
+// Poll up to K words per thread at arbitrary addresses: word i (i < n) of the
+// list is fetched by thread i % 256 from addr(i) and stored to dst[i].
+template <int K, typename AddrFn>
+__device__ void stage_list(Ctx &c, float *dst, int n, AddrFn addr, unsigned flag, unsigned site) {
+  const int tid = threadIdx.x;
+  unsigned pending = 0;
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+    if (k * kConsumerThreads + tid < n) pending |= 1u << k;
+  if (*c.abort_flag) pending = 0;
+  Waiter w;
+  while (pending) {
+    uint64_t v[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      v[k] = 0;
+      if (pending & (1u << k)) v[k] = ll_load(addr(k * kConsumerThreads + tid));
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      if ((pending & (1u << k)) && ll_flag(v[k]) == flag) {
+        dst[k * kConsumerThreads + tid] = ll_value(v[k]);
+        pending &= ~(1u << k);
+      }
+    }
+    if (pending && !w.keep_going(c, site)) break;
+  }
+  consumer_sync();
+}
+
+// ------------------------------------------------------------- GEMV pieces
+// Lane l owns columns {256*j + 8*l + e : j < J, e < 8} of a K = 256*J vector.
+template <int J>
+__device__ __forceinline__ void load_act(float (&act)[J * 8], const float *s, int lane) {
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const float4 *p = reinterpret_cast<const float4 *>(s + 256 * j + 8 * lane);
+    const float4 x = p[0], y = p[1];
+    act[j * 8 + 0] = x.x;
+    act[j * 8 + 1] = x.y;
+    act[j * 8 + 2] = x.z;
+    act[j * 8 + 3] = x.w;
+    act[j * 8 + 4] = y.x;
+    act[j * 8 + 5] = y.y;
+    act[j * 8 + 6] = y.z;
+    act[j * 8 + 7] = y.w;
+  }
+}
+
+// act <- RMSNorm(s) * w (fp32, eps 1e-6), for a 1024-vector.  Each warp holds
+// the whole vector across its lanes, so no cross-warp reduction is needed.
+__device__ __forceinline__ void rmsnorm_act(float (&act)[32], const float *s,
+                                            const __nv_bfloat16 *w, int lane) {
+  load_act<4>(act, s, lane);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) ss = fmaf(act[i], act[i], ss);
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)kHidden + kRmsEps);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(w + 256 * j + 8 * lane));
+    const unsigned ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      act[j * 8 + 2 * e] = (act[j * 8 + 2 * e] * r) * bf_lo(ww[e]);
+      act[j * 8 + 2 * e + 1] = (act[j * 8 + 2 * e + 1] * r) * bf_hi(ww[e]);
+    }
+  }
+}
+
+// Lane-partial dot product of one bf16 row (K = 256*J, in shared memory).
+template <int J>
+__device__ __forceinline__ float dot_row(const uint8_t *row, const float (&act)[J * 8], int lane) {
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(row + 512 * j + 16 * lane);
+    s0 = fmaf(bf_lo(w.x), act[j * 8 + 0], s0);
+    s1 = fmaf(bf_hi(w.x), act[j * 8 + 1], s1);
+    s2 = fmaf(bf_lo(w.y), act[j * 8 + 2], s2);
+    s3 = fmaf(bf_hi(w.y), act[j * 8 + 3], s3);
+    s0 = fmaf(bf_lo(w.z), act[j * 8 + 4], s0);
+    s1 = fmaf(bf_hi(w.z), act[j * 8 + 5], s1);
+    s2 = fmaf(bf_lo(w.w), act[j * 8 + 6], s2);
+    s3 = fmaf(bf_hi(w.w), act[j * 8 + 7], s3);
+  }
+  return (s0 + s1) + (s2 + s3);
+}
+
+// Process rows [0, n) of one ring tile holding rows of K = 256*J; warp w takes
+// rows w, w+8, ...; `emit(local_row, value)` is called by every lane.
+template <int J, typename Emit>
+__device__ __forceinline__ void gemv_tile(const uint8_t *base, int n, const float (&act)[J * 8],
+                                          int warp, int lane, Emit emit) {
+  int r = warp;
+  // Two rows in flight for K = 1024; longer rows already expose J independent
+  // 16-byte loads per lane, and pairing them would exceed the register budget.
+  for (; J <= 4 && r + kConsumerWarps < n; r += 2 * kConsumerWarps) {
+    float a = dot_row<J>(base + (size_t)r * (512 * J), act, lane);
+    float b = dot_row<J>(base + (size_t)(r + kConsumerWarps) * (512 * J), act, lane);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    emit(r, a);
+    emit(r + kConsumerWarps, b);
+  }
+  if (r < n) {
+    const float a = warp_sum(dot_row<J>(base + (size_t)r * (512 * J), act, lane));
+    emit(r, a);
+  }
+}
+
+// ------------------------------------------------------------- argmax
+__device__ __forceinline__ bool arg_better(unsigned ka, int ia, unsigned kb, int ib) {
+  return ka > kb || (ka == kb && ia < ib);
+}
+
+// Poll every CTA's (key, index) pair for epoch `flag`; all consumer threads
+// return the grid-wide argmax (largest logit, lowest index on ties).
+__device__ int read_argmax(Ctx &c, unsigned flag) {
+  const int tid = threadIdx.x;
+  unsigned key = 0;
+  int idx = 0x7fffffff;
+  if (tid < c.ncta && *c.abort_flag == 0) {
+    Waiter w;
+    while (true) {
+      uint64_t a, b;
+      ll_load2(c.wArg + 2 * tid, a, b);
+      if (ll_flag(a) == flag && ll_flag(b) == flag) {
+        key = (unsigned)(a & 0xffffffffu);
+        idx = (int)(b & 0xffffffffu);
+        break;
+      }
+      if (!w.keep_going(c, kSiteArg)) break;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned k2 = __shfl_xor_sync(0xffffffffu, key, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (arg_better(k2, i2, key, idx)) {
+      key = k2;
+      idx = i2;
+    }
+  }
+  const int warp = tid >> 5, lane = tid & 31;
+  __shared__ unsigned s_key[kConsumerWarps];
+  __shared__ int s_idx[kConsumerWarps];
+  if (lane == 0) {
+    s_key[warp] = key;
+    s_idx[warp] = idx;
+  }
+  consumer_sync();
+  unsigned bk = s_key[0];
+  int bi = s_idx[0];
+#pragma unroll
+  for (int q = 1; q < kConsumerWarps; ++q) {
+    if (arg_better(s_key[q], s_idx[q], bk, bi)) {
+      bk = s_key[q];
+      bi = s_idx[q];
+    }
+  }
+  consumer_sync();  // s_key/s_idx reusable afterwards
+  if (bi < 0 || bi >= kVocab) bi = 0;
+  return bi;
+}
+
+// ------------------------------------------------------------- producer
+struct Producer {
+  Ctx &c;
+  const Params &p;
+  uint64_t pol;
+  uint32_t tile = 0;
+  bool alive = true;
+
+  __device__ Producer(Ctx &c_, const Params &p_) : c(c_), p(p_) { pol = l2_policy_evict_first(); }
+
+  // Reserve the next ring slot for `bytes`; nullptr if the CTA is aborting.
+  __device__ uint8_t *begin(unsigned bytes) {
+    const int slot = tile % kNumSlots;
+    const unsigned use = tile / kNumSlots;
+    if (use > 0) {
+      Waiter w;
+      while (!mbar_try_wait(&c.empty[slot], (use & 1u) ^ 1u)) {
+        if (!w.keep_going(c, kSiteEmpty)) {
+          alive = false;
+          return nullptr;
+        }
+      }
+    }
+    if (*c.abort_flag) {
+      alive = false;
+      return nullptr;
+    }
+    mbar_arrive_expect_tx(&c.full[slot], bytes);
+    return c.ring + slot * kSlotBytes;
+  }
+  __device__ __forceinline__ uint64_t *bar() { return &c.full[tile % kNumSlots]; }
+
+  __device__ void rows(const __nv_bfloat16 *mat, int row_bytes, Range r, int tile_rows) {
+    for (int r0 = r.begin; r0 < r.end && alive; r0 += tile_rows) {
+      const int n = min(tile_rows, r.end - r0);
+      uint8_t *dst = begin((unsigned)(n * row_bytes));
+      if (!dst) return;
+      bulk_g2s(dst, reinterpret_cast<const uint8_t *>(mat) + (size_t)r0 * row_bytes,
+               (unsigned)(n * row_bytes), bar(), pol);
+      ++tile;
+    }
+  }
+
+  __device__ void qkv(const LDGLayerWeights &w, Range r) {
+    for (int r0 = r.begin; r0 < r.end && alive; r0 += kQKVTileRows) {
+      const int n = min(kQKVTileRows, r.end - r0);
+      uint8_t *dst = begin((unsigned)(n * 2048));
+      if (!dst) return;
+      // Split [r0, r0+n) at the q|k|v boundaries (rows 2048 and 3072).
+      int a = r0;
+      while (a < r0 + n) {
+        const __nv_bfloat16 *m;
+        int seg0, seg1;
+        if (a < kQSize) {
+          m = (const __nv_bfloat16 *)w.q_proj_weight;
+          seg0 = 0;
+          seg1 = kQSize;
+        } else if (a < kQSize + kKVSize) {
+          m = (const __nv_bfloat16 *)w.k_proj_weight;
+          seg0 = kQSize;
+          seg1 = kQSize + kKVSize;
+        } else {
+          m = (const __nv_bfloat16 *)w.v_proj_weight;
+          seg0 = kQSize + kKVSize;
+          seg1 = kQKVRows;
+        }
+        const int b = min(r0 + n, seg1);
+        bulk_g2s(dst + (size_t)(a - r0) * 2048,
+                 reinterpret_cast<const uint8_t *>(m) + (size_t)(a - seg0) * 2048,
+                 (unsigned)((b - a) * 2048), bar(), pol);
+        a = b;
+      }
+      ++tile;
+    }
+  }
+
+  __device__ void gate_up(const LDGLayerWeights &w, Range r) {
+    for (int r0 = r.begin; r0 < r.end && alive; r0 += kGUTileRows) {
+      const int n = min(kGUTileRows, r.end - r0);
+      uint8_t *dst = begin((unsigned)(2 * n * 2048));
+      if (!dst) return;
+      bulk_g2s(dst, reinterpret_cast<const uint8_t *>(w.gate_proj_weight) + (size_t)r0 * 2048,
+               (unsigned)(n * 2048), bar(), pol);
+      bulk_g2s(dst + kGUTileRows * 2048,
+               reinterpret_cast<const uint8_t *>(w.up_proj_weight) + (size_t)r0 * 2048,
+               (unsigned)(n * 2048), bar(), pol);
+      ++tile;
+    }
+  }
+
+  // K/V rows [chunk) of (layer, kv head g).  Positions written earlier in this
+  // launch are read only after their writer published kv_ready.
+  __device__ void kv(int step, int layer, int g, Range ch) {
+    if (ch.end <= ch.begin || !alive) return;
+    if (ch.end > p.start_pos && step > 0) {
+      const unsigned e_prev = epoch_of(c, step - 1, layer, p.num_layers);
+      const unsigned e_cur = epoch_of(c, step, layer, p.num_layers);
+      const unsigned *flag = &c.ctrl->kv_ready[layer * kNumKVHeads + g];
+      Waiter w;
+      while (true) {
+        const unsigned v = ld_acquire_u32(flag);
+        if (v == e_prev || v == e_cur) break;
+        if (!w.keep_going(c, kSiteKVReady)) {
+          alive = false;
+          return;
+        }
+      }
+      fence_proxy_async_global();
+    }
+    const size_t head_off = ((size_t)layer * kNumKVHeads + g) * (size_t)p.max_seq_len;
+    for (int j0 = ch.begin; j0 < ch.end && alive; j0 += kKVTilePos) {
+      const int n = min(kKVTilePos, ch.end - j0);
+      uint8_t *dst = begin((unsigned)(2 * n * kHeadDim * 2));
+      if (!dst) return;
+      const size_t off = (head_off + j0) * kHeadDim;
+      bulk_g2s(dst, p.k_cache + off, (unsigned)(n * kHeadDim * 2), bar(), pol);
+      bulk_g2s(dst + kKVTileVOffset, p.v_cache + off, (unsigned)(n * kHeadDim * 2), bar(), pol);
+      ++tile;
+    }
+  }
+
+  __device__ void run() {
+    const int item = item_of_cta(c.cta, p.splits);
+    for (int t = 0; t < p.num_steps && alive; ++t) {
+      const int pos = p.start_pos + t;
+      for (int l = 0; l < p.num_layers && alive; ++l) {
+        c.cur_layer = l;
+        const LDGLayerWeights w = p.layers[l];
+        qkv(w, qkv_rows(c.cta, c.ncta));
+        if (item >= 0) kv(t, l, item / p.splits, kv_chunk(pos, item % p.splits, p.splits));
+        rows((const __nv_bfloat16 *)w.o_proj_weight, kQSize * 2, o_rows(c.cta, c.ncta), kOTileRows);
+        gate_up(w, gu_rows(c.cta, c.ncta));
+        rows((const __nv_bfloat16 *)w.down_proj_weight, kInter * 2, d_rows(c.cta, c.ncta), kDTileRows);
+      }
+      rows(p.lm_head, kHidden * 2, lm_rows(c.cta, c.ncta), kLMTileRows);
+    }
+    // Drain: the last tile issued into each slot must land before the CTA exits.
+    for (int s = 0; s < kNumSlots; ++s) {
+      if (tile > (uint32_t)s) {
+        const uint32_t last = s + ((tile - 1u - s) / kNumSlots) * kNumSlots;
+        const unsigned par = (last / kNumSlots) & 1u;
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&c.full[s], par)) {
+          if (global_timer_ns() - t0 > c.timeout_ns) {
+            raise_error(c, QMK_ERR_TIMEOUT, kSiteFull);
+            break;
+          }
+        }
+      }
+    }
+  }
+};
+
+// ------------------------------------------------------------- consumer
+struct Consumer {
+  Ctx &c;
+  const Params &p;
+  uint8_t *smem;
+  float *sX, *sA, *sAtt, *sU;
+  uint32_t tile = 0;
+  int warp, lane, tid;
+
+  __device__ Consumer(Ctx &c_, const Params &p_, uint8_t *smem_) : c(c_), p(p_), smem(smem_) {
+    sX = reinterpret_cast<float *>(smem + kSmX);
+    sA = reinterpret_cast<float *>(smem + kSmA);
+    sAtt = reinterpret_cast<float *>(smem + kSmAtt);
+    sU = reinterpret_cast<float *>(smem + kSmU);
+    tid = threadIdx.x;
+    warp = tid >> 5;
+    lane = tid & 31;
+  }
+
+  __device__ __forceinline__ bool live() const { return *c.abort_flag == 0; }
+
+  // P1: RMSNorm(x) then q|k|v rows of this CTA.
+  __device__ void phase_qkv(const LDGLayerWeights &w, unsigned E) {
+    float act[32];
+    rmsnorm_act(act, sX, (const __nv_bfloat16 *)w.input_layernorm_weight, lane);
+    const Range R = qkv_rows(c.cta, c.ncta);
+    for (int r0 = R.begin; r0 < R.end; r0 += kQKVTileRows) {
+      const int n = min(kQKVTileRows, R.end - r0);
+      const bool ok = wait_full(c, tile);
+      if (ok) {
+        uint64_t *out = c.wQKV + r0;
+        gemv_tile<4>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
+          if (lane == 0) ll_store(out + r, ll_pack(v, E));
+        });
+      }
+      release_tile(c, tile, ok);
+      ++tile;
+    }
+  }
+
+  // P2: one split-KV attention item for KV head g (q heads 2g, 2g+1).
+  __device__ void phase_attention(const LDGLayerWeights &w, int layer, int step, unsigned E) {
+    const int item = item_of_cta(c.cta, p.splits);
+    if (item < 0) return;
+    const int g = item / p.splits, s = item % p.splits;
+    const bool last = (s == p.splits - 1);
+    const int pos = p.start_pos + step;
+    const Range ch = kv_chunk(pos, s, p.splits);
+    float *sQ = sU + kUQ;
+    float *sPW = sU + kUPW;
+
+    // q rows [256g, 256g+256), k rows 2048+128g.., v rows 3072+128g.. -> sU[0..512)
+    stage_list<2>(
+        c, sU, 512,
+        [&](int i) -> const uint64_t * {
+          const int row = (i < 256) ? (g * 256 + i)
+                                    : (i < 384) ? (kQSize + g * 128 + (i - 256))
+                                                : (kQSize + kKVSize + g * 128 + (i - 384));
+          return c.wQKV + row;
+        },
+        E, kSiteQKV);
+
+    // Per-head RMSNorm + RoPE (rotate-half).  Lane l holds dims 4l..4l+3; the
+    // rotation partner dims (d +- 64) sit in lane l ^ 16.
+    const int d0 = 4 * lane;
+    const __nv_bfloat16 *cosp = p.cos_t + (size_t)pos * kHeadDim;
+    const __nv_bfloat16 *sinp = p.sin_t + (size_t)pos * kHeadDim;
+    if (warp < 2 || (warp == 2 && last)) {
+      float *vec = (warp < 2) ? (sQ + warp * kHeadDim) : (sU + kUK);
+      const __nv_bfloat16 *nw = (const __nv_bfloat16 *)((warp < 2) ? w.q_norm_weight : w.k_norm_weight);
+      float x[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[e] = vec[d0 + e];
+      float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+      ss = warp_sum(ss);
+      const float r = rsqrtf(ss / (float)kHeadDim + kRmsEps);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[e] = (x[e] * r) * __bfloat162float(nw[d0 + e]);
+      float y[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
+        const float cv = __bfloat162float(cosp[d0 + e]);
+        const float sv = __bfloat162float(sinp[d0 + e]);
+        y[e] = (lane < 16) ? (x[e] * cv - partner * sv) : (x[e] * cv + partner * sv);
+      }
+      if (warp < 2) {
+        const float qs = p.attn_scale * kLog2e;  // scores in log2 units
+#pragma unroll
+        for (int e = 0; e < 4; ++e) vec[d0 + e] = y[e] * qs;
+      } else {
+        // New K/V row of this position: bf16 into the cache and (rounded) into smem.
+        const size_t off =
+            (((size_t)layer * kNumKVHeads + g) * (size_t)p.max_seq_len + pos) * kHeadDim + d0;
+        unsigned kbits[4], vbits[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat16 kb = __float2bfloat16(y[e]);
+          const __nv_bfloat16 vb = __float2bfloat16(sU[kUV + d0 + e]);
+          kbits[e] = __bfloat16_as_ushort(kb);
+          vbits[e] = __bfloat16_as_ushort(vb);
+          sU[kUKn + d0 + e] = __bfloat162float(kb);
+          sU[kUVn + d0 + e] = __bfloat162float(vb);
+        }
+        if (live()) {
+          *reinterpret_cast<uint2 *>(p.k_cache + off) =
+              make_uint2(kbits[0] | (kbits[1] << 16), kbits[2] | (kbits[3] << 16));
+          *reinterpret_cast<uint2 *>(p.v_cache + off) =
+              make_uint2(vbits[0] | (vbits[1] << 16), vbits[2] | (vbits[3] << 16));
+        }
+      }
+    }
+    consumer_sync();
+    if (last && tid == 0 && live()) {
+      __threadfence();
+      st_release_u32(&c.ctrl->kv_ready[layer * kNumKVHeads + g], E);
+    }
+
+    float q0[4], q1[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      q0[e] = sQ[d0 + e];
+      q1[e] = sQ[kHeadDim + d0 + e];
+    }
+    float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
+    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+    auto accumulate = [&](const float (&kf)[4], const float (&vf)[4]) {
+      float s0 = q0[0] * kf[0] + q0[1] * kf[1] + q0[2] * kf[2] + q0[3] * kf[3];
+      float s1 = q1[0] * kf[0] + q1[1] * kf[1] + q1[2] * kf[2] + q1[3] * kf[3];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      }
+      const float n0 = fmaxf(m0, s0), n1 = fmaxf(m1, s1);
+      const float c0 = exp2f(m0 - n0), c1 = exp2f(m1 - n1);
+      const float p0 = exp2f(s0 - n0), p1 = exp2f(s1 - n1);
+      l0 = l0 * c0 + p0;
+      l1 = l1 * c1 + p1;
+      m0 = n0;
+      m1 = n1;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        o0[e] = o0[e] * c0 + p0 * vf[e];
+        o1[e] = o1[e] * c1 + p1 * vf[e];
+      }
+    };
+    for (int j0 = ch.begin; j0 < ch.end; j0 += kKVTilePos) {
+      const int n = min(kKVTilePos, ch.end - j0);
+      const bool ok = wait_full(c, tile);
+      if (ok) {
+        const uint8_t *kt = slot_ptr(c, tile);
+        const uint8_t *vt = kt + kKVTileVOffset;
+        for (int j = warp; j < n; j += kConsumerWarps) {
+          const uint2 kw = *reinterpret_cast<const uint2 *>(kt + (size_t)j * 256 + 8 * lane);
+          const uint2 vw = *reinterpret_cast<const uint2 *>(vt + (size_t)j * 256 + 8 * lane);
+          const float kf[4] = {bf_lo(kw.x), bf_hi(kw.x), bf_lo(kw.y), bf_hi(kw.y)};
+          const float vf[4] = {bf_lo(vw.x), bf_hi(vw.x), bf_lo(vw.y), bf_hi(vw.y)};
+          accumulate(kf, vf);
+        }
+      }
+      release_tile(c, tile, ok);
+      ++tile;
+    }
+    if (last && warp == 0) {
+      float kf[4], vf[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        kf[e] = sU[kUKn + d0 + e];
+        vf[e] = sU[kUVn + d0 + e];
+      }
+      accumulate(kf, vf);
+    }
+    // Cross-warp merge of the online-softmax states -> PART words.
+    float *pw = sPW + warp * kPartWords;
+    if (lane == 0) {
+      pw[0] = m0;
+      pw[1] = l0;
+      pw[2] = m1;
+      pw[3] = l1;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      pw[4 + d0 + e] = o0[e];
+      pw[4 + kHeadDim + d0 + e] = o1[e];
+    }
+    consumer_sync();
+    {
+      const int hh = tid >> 7, d = tid & 127;
+      float M = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < kConsumerWarps; ++q) M = fmaxf(M, sPW[q * kPartWords + 2 * hh]);
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int q = 0; q < kConsumerWarps; ++q) {
+          const float mq = sPW[q * kPartWords + 2 * hh];
+          if (mq != -INFINITY) {
+            const float f = exp2f(mq - M);
+            L += sPW[q * kPartWords + 2 * hh + 1] * f;
+            O += sPW[q * kPartWords + 4 + hh * kHeadDim + d] * f;
+          }
+        }
+      }
+      if (live()) {
+        uint64_t *part = c.wPart + (size_t)item * kPartWords;
+        ll_store(part + 4 + hh * kHeadDim + d, ll_pack(O, E));
+        if (d == 0) {
+          ll_store(part + 2 * hh, ll_pack(M, E));
+          ll_store(part + 2 * hh + 1, ll_pack(L, E));
+        }
+      }
+    }
+    consumer_sync();  // sU scratch is reused by the next phase
+  }
+
+  // P2.5: merge the split partials of (q head h, 64 dims) -> ATT words.
+  __device__ void phase_merge(unsigned E) {
+    const int j = merge_task_of_cta(c.cta, c.ncta);
+    if (j < 0) return;
+    const int h = j >> 1, half = j & 1, g = h >> 1, hl = h & 1;
+    const int S = p.splits;
+    const int n = S * kMergeWordsPerSplit;
+    stage_list<(kMaxSplits * kMergeWordsPerSplit + kConsumerThreads - 1) / kConsumerThreads>(
+        c, sU, n,
+        [&](int i) -> const uint64_t * {
+          const int s = i / kMergeWordsPerSplit, k = i % kMergeWordsPerSplit;
+          const int word = (k < 2) ? (2 * hl + k) : (4 + hl * kHeadDim + half * kMergeDims + (k - 2));
+          return c.wPart + (size_t)(g * S + s) * kPartWords + word;
+        },
+        E, kSitePart);
+    if (tid < kMergeDims) {
+      float M = -INFINITY;
+      for (int s = 0; s < S; ++s) M = fmaxf(M, sU[s * kMergeWordsPerSplit]);
+      float L = 0.f, O = 0.f;
+      for (int s = 0; s < S; ++s) {
+        const float ms = sU[s * kMergeWordsPerSplit];
+        if (ms != -INFINITY) {
+          const float f = exp2f(ms - M);
+          L += sU[s * kMergeWordsPerSplit + 1] * f;
+          O += sU[s * kMergeWordsPerSplit + 2 + tid] * f;
+        }
+      }
+      if (live()) ll_store(c.wAtt + h * kHeadDim + half * kMergeDims + tid, ll_pack(O / L, E));
+    }
+    consumer_sync();
+  }
+
+  // P3: O-projection rows + residual -> A words.
+  __device__ void phase_o(const LDGLayerWeights &w, unsigned E, bool stall) {
+    // Test hook: 0xFFFFFFFF is never an epoch, so this wait can only expire.
+    stage_vec<4>(c, sAtt, c.wAtt, stall ? 0xFFFFFFFFu : E, kSiteAtt);
+    float act[64];
+    load_act<8>(act, sAtt, lane);
+    const Range R = o_rows(c.cta, c.ncta);
+    for (int r0 = R.begin; r0 < R.end; r0 += kOTileRows) {
+      const int n = min(kOTileRows, R.end - r0);
+      const bool ok = wait_full(c, tile);
+      if (ok) {
+        gemv_tile<8>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
+          if (lane == 0) ll_store(c.wA + r0 + r, ll_pack(v + sX[r0 + r], E));
+        });
+      }
+      release_tile(c, tile, ok);
+      ++tile;
+    }
+  }
+
+  // P4: RMSNorm(a) then gate/up rows, SiLU(gate) * up -> M words.
+  __device__ void phase_gate_up(const LDGLayerWeights &w, unsigned E) {
+    stage_vec<2>(c, sA, c.wA, E, kSiteA);
+    float act[32];
+    rmsnorm_act(act, sA, (const __nv_bfloat16 *)w.post_attn_layernorm_weight, lane);
+    const Range R = gu_rows(c.cta, c.ncta);
+    for (int r0 = R.begin; r0 < R.end; r0 += kGUTileRows) {
+      const int n = min(kGUTileRows, R.end - r0);
+      const bool ok = wait_full(c, tile);
+      if (ok) {
+        const uint8_t *gt = slot_ptr(c, tile);
+        const uint8_t *ut = gt + kGUTileRows * 2048;
+        for (int r = warp; r < n; r += kConsumerWarps) {
+          float gs = dot_row<4>(gt + (size_t)r * 2048, act, lane);
+          float us = dot_row<4>(ut + (size_t)r * 2048, act, lane);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            gs += __shfl_xor_sync(0xffffffffu, gs, o);
+            us += __shfl_xor_sync(0xffffffffu, us, o);
+          }
+          if (lane == 0) {
+            const float silu = gs / (1.0f + expf(-gs));
+            ll_store(c.wM + r0 + r, ll_pack(silu * us, E));
+          }
+        }
+      }
+      release_tile(c, tile, ok);
+      ++tile;
+    }
+  }
+
+  // P5: down rows + residual -> X words (next layer's input).
+  __device__ void phase_down(const LDGLayerWeights &w, unsigned E) {
+    stage_vec<6>(c, sU, c.wM, E, kSiteM);
+    float act[96];
+    load_act<12>(act, sU, lane);
+    const Range R = d_rows(c.cta, c.ncta);
+    for (int r0 = R.begin; r0 < R.end; r0 += kDTileRows) {
+      const int n = min(kDTileRows, R.end - r0);
+      const bool ok = wait_full(c, tile);
+      if (ok) {
+        gemv_tile<12>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
+          if (lane == 0) ll_store(c.wX + r0 + r, ll_pack(v + sA[r0 + r], E));
+        });
+      }
+      release_tile(c, tile, ok);
+      ++tile;
+    }
+    consumer_sync();  // sU (MLP intermediate) is reused by the next phase
+  }
+
+  // Final RMSNorm + LM head rows + CTA argmax -> ARG words.
+  __device__ void phase_lm_head(int step, unsigned E_x, unsigned E) {
+    stage_vec<2>(c, sX, c.wX, E_x, kSiteX);
+    float act[32];
+    rmsnorm_act(act, sX, p.final_norm, lane);
+    if (p.final_hidden && c.cta == 0 && warp == 0 && step == p.num_steps - 1 && live()) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) p.final_hidden[256 * j + 8 * lane + e] = act[j * 8 + e];
+    }
+    float best = -INFINITY;
+    int best_i = 0x7fffffff;
+    float *logits = p.logits ? (p.logits + (size_t)step * kVocab) : nullptr;
+    const Range R = lm_rows(c.cta, c.ncta);
+    for (int r0 = R.begin; r0 < R.end; r0 += kLMTileRows) {
+      const int n = min(kLMTileRows, R.end - r0);
+      const bool ok = wait_full(c, tile);
+      if (ok) {
+        gemv_tile<4>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
+          const int row = r0 + r;
+          if (v > best || (v == best && row < best_i)) {
+            best = v;
+            best_i = row;
+          }
+          if (logits && lane == 0) logits[row] = v;
+        });
+      }
+      release_tile(c, tile, ok);
+      ++tile;
+    }
+    if (lane == 0) {
+      c.warp_best_v[warp] = best;
+      c.warp_best_i[warp] = best_i;
+    }
+    consumer_sync();
+    if (tid == 0) {
+      unsigned bk = 0;
+      int bi = 0x7fffffff;
+      for (int q = 0; q < kConsumerWarps; ++q) {
+        const float v = c.warp_best_v[q];
+        const int i = c.warp_best_i[q];
+        if (i == 0x7fffffff) continue;
+        const unsigned k = float_order_key(v);
+        if (arg_better(k, i, bk, bi)) {
+          bk = k;
+          bi = i;
+        }
+      }
+      if (bi == 0x7fffffff) bi = R.begin;  // CTA without rows (not on B200)
+      if (live()) {
+        ll_store(c.wArg + 2 * c.cta, ll_pack_u(bk, E));
+        ll_store(c.wArg + 2 * c.cta + 1, ll_pack_u((unsigned)bi, E));
+      }
+    }
+    consumer_sync();
+  }
+
+  // Token consumed by step t.
+  __device__ int step_token(int t) {
+    int tok;
+    if (t < p.n_forced) {
+      tok = __ldg(p.forced + t);
+    } else if (t == 0) {
+      tok = p.first_token;
+    } else {
+      tok = read_argmax(c, epoch_of(c, t - 1, p.num_layers, p.num_layers));
+    }
+    if (tok < 0 || tok >= kVocab) {
+      if (tid == 0) raise_error(c, QMK_ERR_TOKEN, kSiteToken);
+      tok = 0;
+    }
+    return tok;
+  }
+
+  __device__ void run() {
+    const int L = p.num_layers;
+    for (int t = 0; t < p.num_steps; ++t) {
+      // CTA 0 records the previous step's argmax (needed even when forced).
+      if (t > 0 && c.cta == 0) {
+        const int prev = read_argmax(c, epoch_of(c, t - 1, L, L));
+        if (tid == 0 && live() && p.out_log) p.out_log[t - 1] = prev;
+      }
+      const int tok = step_token(t);
+      // Layer-0 input: the embedding row (bf16 -> fp32).
+      {
+        const __nv_bfloat16 *erow = p.embed + (size_t)tok * kHidden;
+        const uint2 v = __ldg(reinterpret_cast<const uint2 *>(erow) + tid);
+        sX[4 * tid + 0] = bf_lo(v.x);
+        sX[4 * tid + 1] = bf_hi(v.x);
+        sX[4 * tid + 2] = bf_lo(v.y);
+        sX[4 * tid + 3] = bf_hi(v.y);
+        consumer_sync();
+      }
+      for (int l = 0; l < L; ++l) {
+        c.cur_layer = l;
+        const LDGLayerWeights w = p.layers[l];
+        const unsigned E = epoch_of(c, t, l, L);
+        if (l > 0) stage_vec<2>(c, sX, c.wX, epoch_of(c, t, l - 1, L), kSiteX);
+        phase_qkv(w, E);
+        phase_attention(w, l, t, E);
+        phase_merge(E);
+        phase_o(w, E, p.debug_stall == c.cta + 1 && t == 0 && l == 0);
+        phase_gate_up(w, E);
+        phase_down(w, E);
+      }
+      phase_lm_head(t, epoch_of(c, t, L - 1, L), epoch_of(c, t, L, L));
+    }
+    if (c.cta == 0) {
+      const int last = read_argmax(c, epoch_of(c, p.num_steps - 1, L, L));
+      if (tid == 0 && live()) {
+        if (p.out_log) p.out_log[p.num_steps - 1] = last;
+        if (p.out_token) *p.out_token = last;
+      }
+      if (tid == 0 && !live() && p.out_token) *p.out_token = -1;
+    }
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ int s_abort;
+  __shared__ unsigned s_epoch;
+  Ctx c;
+  c.ring = smem + kSmRing;
+  c.full = reinterpret_cast<uint64_t *>(smem + kSmMisc);
+  c.empty = c.full + kNumSlots;
+  c.warp_best_v = reinterpret_cast<float *>(smem + kSmMisc + 16 * kNumSlots);
+  c.warp_best_i = reinterpret_cast<int *>(smem + kSmMisc + 16 * kNumSlots + 4 * kConsumerWarps);
+  c.abort_flag = &s_abort;
+  c.ctrl = reinterpret_cast<Ctrl *>(p.ws);
+  c.wX = reinterpret_cast<uint64_t *>(p.ws + kOffX);
+  c.wQKV = reinterpret_cast<uint64_t *>(p.ws + kOffQKV);
+  c.wPart = reinterpret_cast<uint64_t *>(p.ws + kOffPart);
+  c.wAtt = reinterpret_cast<uint64_t *>(p.ws + kOffAtt);
+  c.wA = reinterpret_cast<uint64_t *>(p.ws + kOffA);
+  c.wM = reinterpret_cast<uint64_t *>(p.ws + kOffM);
+  c.wArg = reinterpret_cast<uint64_t *>(p.ws + kOffArg);
+  c.cta = blockIdx.x;
+  c.ncta = gridDim.x;
+  c.timeout_ns = p.timeout_ns;
+  c.cur_layer = 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kNumSlots; ++s) {
+      mbar_init(&c.full[s], 1);
+      mbar_init(&c.empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+    s_abort = 0;
+    s_epoch = ld_relaxed_u32(&c.ctrl->epoch);
+  }
+  __syncthreads();
+  c.E0 = s_epoch;
+
+  if (threadIdx.x >= kConsumerThreads) {
+    if ((threadIdx.x & 31) == 0) {
+      Producer prod(c, p);
+      prod.run();
+    }
+  } else {
+    Consumer cons(c, p, smem);
+    cons.run();
+  }
+  __syncthreads();
+
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned done = atomicAdd(&c.ctrl->exit_count, 1u);
+    if (done == (unsigned)c.ncta - 1u) {
+      __threadfence();
+      const unsigned used = (unsigned)p.num_steps * (unsigned)(p.num_layers + 1) + 1u;
+      unsigned next = c.E0 + used;
+      if (next > kEpochWrap) next = 0;
+      const unsigned code = ld_relaxed_u32(&c.ctrl->err_code);
+      const unsigned info = ld_relaxed_u32(&c.ctrl->err_info);
+      const unsigned launches = c.ctrl->launches + 1u;
+      c.ctrl->epoch = next;
+      c.ctrl->err_code = 0;
+      c.ctrl->err_info = 0;
+      c.ctrl->launches = launches;
+      c.ctrl->exit_count = 0;
+      if (p.status) {
+        volatile QmkStatus *st = p.status;
+        st->error_code = code;
+        st->error_info = info;
+        st->epoch = next;
+        st->launches = launches;
+        __threadfence_system();
+      }
+    }
+  }
+}
+
+}  // namespace qmk
+
+// =============================================================================
+// Host side: C ABI
+// =============================================================================
+
+namespace {
+
+thread_local int g_last_error = QMK_OK;
+thread_local char g_last_msg[512] = "";
+
+int set_error(int code, const char *fmt, ...) {
+  g_last_error = code;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_msg, sizeof(g_last_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int clear_error() {
+  g_last_error = QMK_OK;
+  g_last_msg[0] = '\0';
+  return QMK_OK;
+}
+
+struct DeviceState {
+  bool attr_set = false;
+  int num_sms = 0;
+  void *default_ws = nullptr;
+  QmkStatus *default_status_host = nullptr;
+  QmkStatus *default_status_dev = nullptr;
+};
+
+constexpr int kMaxDevices = 64;
+DeviceState g_devices[kMaxDevices];
+std::mutex g_mutex;
+
+int current_device(int *dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return set_error(QMK_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (*dev < 0 || *dev >= kMaxDevices) return set_error(QMK_ERR_CUDA, "device %d out of range", *dev);
+  return QMK_OK;
+}
+
+// Kernel attributes + SM count for the current device (once per device).
+int prepare_device(int dev) {
+  DeviceState &ds = g_devices[dev];
+  if (ds.attr_set) return QMK_OK;
+  cudaError_t e = cudaFuncSetAttribute(qmk::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       qmk::kSmBytes - 0);
+  if (e != cudaSuccess)
+    return set_error(QMK_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem %d): %s", qmk::kSmBytes,
+                     cudaGetErrorString(e));
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return set_error(QMK_ERR_CUDA, "SM count: %s", cudaGetErrorString(e));
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qmk::decode_kernel, qmk::kThreads,
+                                                    qmk::kSmBytes);
+  if (e != cudaSuccess) return set_error(QMK_ERR_CUDA, "occupancy query: %s", cudaGetErrorString(e));
+  if (per_sm < 1) return set_error(QMK_ERR_LAUNCH, "decode kernel does not fit on one SM");
+  ds.num_sms = sms;
+  ds.attr_set = true;
+  return QMK_OK;
+}
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+size_t qmk_workspace_bytes(void) { return (size_t)qmk::kWorkspaceBytes; }
+
+const char *qmk_version(void) { return "qwen_megakernel_b200 0.1 (sm_100a)"; }
+
+const char *qmk_error_string(int code) {
+  switch (code) {
+    case QMK_OK: return "ok";
+    case QMK_ERR_ARGS: return "invalid argument";
+    case QMK_ERR_CUDA: return "CUDA runtime error";
+    case QMK_ERR_LAUNCH: return "cooperative launch refused";
+    case QMK_ERR_TIMEOUT: return "device-side wait timed out";
+    case QMK_ERR_TOKEN: return "token id out of range";
+    case QMK_ERR_WORKSPACE: return "workspace too small or misaligned";
+    default: return "unknown error";
+  }
+}
+
+int qmk_get_last_error(void) { return g_last_error; }
+const char *qmk_get_last_error_message(void) { return g_last_msg; }
+
+int qmk_attention_splits(int num_ctas, int max_position) {
+  return qmk::attention_splits(num_ctas, max_position);
+}
+
+int qmk_describe_partition(int num_ctas, int splits, int cta, int *out, int out_len) {
+  if (!out || out_len < 12 || num_ctas < qmk::kMinCtas || num_ctas > qmk::kMaxCtas || cta < 0 ||
+      cta >= num_ctas || splits < 1 || splits > qmk::kMaxSplits || qmk::kNumKVHeads * splits > num_ctas)
+    return set_error(QMK_ERR_ARGS, "qmk_describe_partition: bad arguments");
+  const qmk::Range a = qmk::qkv_rows(cta, num_ctas), b = qmk::o_rows(cta, num_ctas),
+                   g = qmk::gu_rows(cta, num_ctas), d = qmk::d_rows(cta, num_ctas),
+                   lm = qmk::lm_rows(cta, num_ctas);
+  out[0] = a.begin; out[1] = a.end;
+  out[2] = b.begin; out[3] = b.end;
+  out[4] = g.begin; out[5] = g.end;
+  out[6] = d.begin; out[7] = d.end;
+  out[8] = lm.begin; out[9] = lm.end;
+  out[10] = qmk::item_of_cta(cta, splits);
+  out[11] = qmk::merge_task_of_cta(cta, num_ctas);
+  return clear_error();
+}
+
+int qmk_num_ctas(int device) {
+  int sms = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) {
+    set_error(QMK_ERR_CUDA, "SM count: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  return sms < qmk::kMaxCtas ? sms : qmk::kMaxCtas;
+}
+
+int qmk_workspace_init(void *workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!workspace || workspace_bytes < (size_t)qmk::kWorkspaceBytes || !aligned(workspace, 256))
+    return set_error(QMK_ERR_WORKSPACE, "workspace needs %lld bytes, 256-byte aligned",
+                     (long long)qmk::kWorkspaceBytes);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, (size_t)qmk::kWorkspaceBytes, stream);
+  if (e != cudaSuccess) return set_error(QMK_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  return clear_error();
+}
+
+int qmk_run(const QmkRunArgs *a, cudaStream_t stream) {
+  if (!a) return set_error(QMK_ERR_ARGS, "qmk_run: null args");
+  if (!a->embed_weight || !a->layer_weights || !a->final_norm_weight || !a->lm_head_weight ||
+      !a->cos_table || !a->sin_table || !a->k_cache || !a->v_cache)
+    return set_error(QMK_ERR_ARGS, "qmk_run: null weight/table/cache pointer");
+  if (!a->workspace || a->workspace_bytes < (size_t)qmk::kWorkspaceBytes || !aligned(a->workspace, 256))
+    return set_error(QMK_ERR_WORKSPACE, "qmk_run: workspace needs %lld bytes, 256-byte aligned",
+                     (long long)qmk::kWorkspaceBytes);
+  if (a->num_layers < 1 || a->num_layers > qmk::kMaxLayers)
+    return set_error(QMK_ERR_ARGS, "qmk_run: num_layers=%d outside [1, %d]", a->num_layers, qmk::kMaxLayers);
+  if (a->num_steps < 1) return set_error(QMK_ERR_ARGS, "qmk_run: num_steps=%d < 1", a->num_steps);
+  if (a->max_seq_len < 1) return set_error(QMK_ERR_ARGS, "qmk_run: max_seq_len=%d < 1", a->max_seq_len);
+  if (a->start_position < 0 || (long long)a->start_position + a->num_steps > a->max_seq_len)
+    return set_error(QMK_ERR_ARGS,
+                     "qmk_run: positions [%d, %lld) exceed max_seq_len=%d", a->start_position,
+                     (long long)a->start_position + a->num_steps, a->max_seq_len);
+  if ((long long)a->num_steps * (a->num_layers + 1) >= (1LL << 27))
+    return set_error(QMK_ERR_ARGS, "qmk_run: num_steps=%d too large for one launch", a->num_steps);
+  if (a->n_forced < 0 || (a->n_forced > 0 && !a->forced_tokens))
+    return set_error(QMK_ERR_ARGS, "qmk_run: n_forced=%d without forced_tokens", a->n_forced);
+  if (a->n_forced == 0 && (a->first_token < 0 || a->first_token >= QMK_VOCAB))
+    return set_error(QMK_ERR_ARGS, "qmk_run: token id %d outside [0, %d)", a->first_token, QMK_VOCAB);
+  if (!(a->attn_scale == a->attn_scale) || a->attn_scale <= 0.f)
+    return set_error(QMK_ERR_ARGS, "qmk_run: attn_scale must be positive");
+  const void *ptrs[] = {a->embed_weight, a->final_norm_weight, a->lm_head_weight, a->cos_table,
+                        a->sin_table,    a->k_cache,           a->v_cache};
+  for (const void *q : ptrs)
+    if (!aligned(q, 16)) return set_error(QMK_ERR_ARGS, "qmk_run: tensor not 16-byte aligned");
+  if (!aligned(a->layer_weights, 8)) return set_error(QMK_ERR_ARGS, "qmk_run: layer table misaligned");
+
+  int dev = 0;
+  if (current_device(&dev) != QMK_OK) return g_last_error;
+  int ncta;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (prepare_device(dev) != QMK_OK) return g_last_error;
+    ncta = g_devices[dev].num_sms;
+  }
+  if (ncta > qmk::kMaxCtas) ncta = qmk::kMaxCtas;
+  if (ncta < qmk::kMinCtas)
+    return set_error(QMK_ERR_LAUNCH, "qmk_run: %d SMs < %d required", ncta, qmk::kMinCtas);
+
+  qmk::Params p;
+  p.embed = (const __nv_bfloat16 *)a->embed_weight;
+  p.layers = a->layer_weights;
+  p.final_norm = (const __nv_bfloat16 *)a->final_norm_weight;
+  p.lm_head = (const __nv_bfloat16 *)a->lm_head_weight;
+  p.cos_t = (const __nv_bfloat16 *)a->cos_table;
+  p.sin_t = (const __nv_bfloat16 *)a->sin_table;
+  p.k_cache = (__nv_bfloat16 *)a->k_cache;
+  p.v_cache = (__nv_bfloat16 *)a->v_cache;
+  p.ws = (uint8_t *)a->workspace;
+  p.forced = a->forced_tokens;
+  p.n_forced = a->n_forced < a->num_steps ? a->n_forced : a->num_steps;
+  p.first_token = a->first_token;
+  p.start_pos = a->start_position;
+  p.num_steps = a->num_steps;
+  p.num_layers = a->num_layers;
+  p.max_seq_len = a->max_seq_len;
+  p.attn_scale = a->attn_scale;
+  p.splits = qmk::attention_splits(ncta, a->start_position + a->num_steps - 1);
+  p.out_log = a->output_log;
+  p.out_token = a->output_token;
+  p.logits = a->logits;
+  p.final_hidden = a->final_hidden;
+  p.status = a->status;
+  p.timeout_ns = a->timeout_ns ? a->timeout_ns : qmk::kDefaultTimeoutNs;
+  p.debug_stall = (a->debug_stall > 0 && a->debug_stall <= ncta) ? a->debug_stall : 0;
+
+  void *kargs[] = {&p};
+  cudaError_t e = cudaLaunchCooperativeKernel((const void *)qmk::decode_kernel, dim3(ncta),
+                                              dim3(qmk::kThreads), kargs, qmk::kSmBytes, stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(e == cudaErrorCooperativeLaunchTooLarge ? QMK_ERR_LAUNCH : QMK_ERR_CUDA,
+                     "cooperative launch of %d x %d: %s", ncta, qmk::kThreads, cudaGetErrorString(e));
+  }
+  return clear_error();
+}
+
+// ---- library-owned default workspace (reference entry points) ----
+
+static int default_state(DeviceState **out) {
+  int dev = 0;
+  if (current_device(&dev) != QMK_OK) return g_last_error;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState &ds = g_devices[dev];
+  if (!ds.default_ws) {
+    void *ws = nullptr;
+    cudaError_t e = cudaMalloc(&ws, (size_t)qmk::kWorkspaceBytes);
+    if (e != cudaSuccess) return set_error(QMK_ERR_CUDA, "cudaMalloc(workspace): %s", cudaGetErrorString(e));
+    e = cudaMemset(ws, 0, (size_t)qmk::kWorkspaceBytes);
+    if (e != cudaSuccess) return set_error(QMK_ERR_CUDA, "cudaMemset(workspace): %s", cudaGetErrorString(e));
+    void *host = nullptr;
+    e = cudaHostAlloc(&host, sizeof(QmkStatus), cudaHostAllocMapped);
+    if (e != cudaSuccess) return set_error(QMK_ERR_CUDA, "cudaHostAlloc(status): %s", cudaGetErrorString(e));
+    memset(host, 0, sizeof(QmkStatus));
+    void *devp = nullptr;
+    e = cudaHostGetDevicePointer(&devp, host, 0);
+    if (e != cudaSuccess) return set_error(QMK_ERR_CUDA, "cudaHostGetDevicePointer: %s", cudaGetErrorString(e));
+    ds.default_ws = ws;
+    ds.default_status_host = (QmkStatus *)host;
+    ds.default_status_dev = (QmkStatus *)devp;
+  }
+  *out = &ds;
+  return QMK_OK;
+}
+
+int qmk_read_default_status(QmkStatus *out) {
+  if (!out) return set_error(QMK_ERR_ARGS, "qmk_read_default_status: null");
+  DeviceState *ds = nullptr;
+  if (default_state(&ds) != QMK_OK) return g_last_error;
+  const volatile QmkStatus *st = ds->default_status_host;
+  out->error_code = st->error_code;
+  out->error_info = st->error_info;
+  out->launches = st->launches;
+  out->epoch = st->epoch;
+  return clear_error();
+}
+
+static void reference_launch(int first_token, int num_steps, const void *embed_weight,
+                             const LDGLayerWeights *layer_weights, const void *final_norm_weight,
+                             const void *lm_head_weight, const void *cos_table, const void *sin_table,
+                             void *k_cache, void *v_cache, void *g_normalized, int *output_log,
+                             int *output_token, int num_layers, int start_position, int max_seq_len,
+                             float attn_scale, cudaStream_t stream) {
+  DeviceState *ds = nullptr;
+  if (default_state(&ds) != QMK_OK) return;
+  QmkRunArgs a;
+  memset(&a, 0, sizeof(a));
+  a.embed_weight = embed_weight;
+  a.layer_weights = layer_weights;
+  a.final_norm_weight = final_norm_weight;
+  a.lm_head_weight = lm_head_weight;
+  a.cos_table = cos_table;
+  a.sin_table = sin_table;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.workspace = ds->default_ws;
+  a.workspace_bytes = (size_t)qmk::kWorkspaceBytes;
+  a.first_token = first_token;
+  a.start_position = start_position;
+  a.num_steps = num_steps;
+  a.num_layers = num_layers;
+  a.max_seq_len = max_seq_len;
+  a.attn_scale = attn_scale;
+  a.output_log = output_log;
+  a.output_token = output_token;
+  a.final_hidden = (float *)g_normalized;
+  a.status = ds->default_status_dev;
+  qmk_run(&a, stream);
+}
+
+void launch_ldg_decode_direct(int input_token_id, int *output_token_id, const void *embed_weight,
+                              const LDGLayerWeights *layer_weights, const void *final_norm_weight,
+                              const void *lm_head_weight, const void *cos_table, const void *sin_table,
+                              void *k_cache, void *v_cache, void *hidden_buffer, void *g_activations,
+                              void *g_residual, void *g_q, void *g_k, void *g_v, void *g_attn_out,
+                              void *g_mlp_intermediate, void *g_normalized, void *block_max_vals,
+                              void *block_max_idxs, int num_layers, int position, int max_seq_len,
+                              float attn_scale, cudaStream_t stream) {
+  (void)hidden_buffer; (void)g_activations; (void)g_residual; (void)g_q; (void)g_k; (void)g_v;
+  (void)g_attn_out; (void)g_mlp_intermediate; (void)block_max_vals; (void)block_max_idxs;
+  reference_launch(input_token_id, 1, embed_weight, layer_weights, final_norm_weight, lm_head_weight,
+                   cos_table, sin_table, k_cache, v_cache, g_normalized, nullptr, output_token_id,
+                   num_layers, position, max_seq_len, attn_scale, stream);
+}
+
+void launch_ldg_decode_persistent(int input_token_id, int *output_token_id, const void *embed_weight,
+                                  const LDGLayerWeights *layer_weights, const void *final_norm_weight,
+                                  const void *lm_head_weight, const void *cos_table,
+                                  const void *sin_table, void *k_cache, void *v_cache,
+                                  void *hidden_buffer, void *g_activations, void *g_residual, void *g_q,
+                                  void *g_k, void *g_v, void *g_attn_out, void *g_mlp_intermediate,
+                                  void *g_normalized, void *block_max_vals, void *block_max_idxs,
+                                  int num_layers, int position, int cache_len, int max_seq_len,
+                                  float attn_scale, cudaStream_t stream) {
+  (void)cache_len;
+  launch_ldg_decode_direct(input_token_id, output_token_id, embed_weight, layer_weights,
+                           final_norm_weight, lm_head_weight, cos_table, sin_table, k_cache, v_cache,
+                           hidden_buffer, g_activations, g_residual, g_q, g_k, g_v, g_attn_out,
+                           g_mlp_intermediate, g_normalized, block_max_vals, block_max_idxs,
+                           num_layers, position, max_seq_len, attn_scale, stream);
+}
+
+void launch_ldg_generate_nosync(int first_token_id, int num_steps, const void *embed_weight,
+                                const LDGLayerWeights *layer_weights, const void *final_norm_weight,
+                                const void *lm_head_weight, const void *cos_table, const void *sin_table,
+                                void *k_cache, void *v_cache, void *hidden_buffer, void *g_activations,
+                                void *g_residual, void *g_q, void *g_k, void *g_v, void *g_attn_out,
+                                void *g_mlp_intermediate, void *g_normalized, void *block_max_vals,
+                                void *block_max_idxs, int *output_log, int num_layers,
+                                int start_position, int max_seq_len, float attn_scale,
+                                cudaStream_t stream) {
+  (void)hidden_buffer; (void)g_activations; (void)g_residual; (void)g_q; (void)g_k; (void)g_v;
+  (void)g_attn_out; (void)g_mlp_intermediate; (void)block_max_vals; (void)block_max_idxs;
+  reference_launch(first_token_id, num_steps, embed_weight, layer_weights, final_norm_weight,
+                   lm_head_weight, cos_table, sin_table, k_cache, v_cache, g_normalized, output_log,
+                   nullptr, num_layers, start_position, max_seq_len, attn_scale, stream);
+}
+
+}  // extern "C"

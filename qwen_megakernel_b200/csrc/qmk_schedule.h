@@ -1,0 +1,128 @@
+// Static work partition of the decode megakernel, shared by host and device.
+//
+// One CTA per SM.  Every phase of a layer splits its output rows into
+// contiguous per-CTA ranges; attention is split into (kv head, KV split)
+// items; the split-KV partials are merged by 32 merge tasks (one per
+// (q head, half of head_dim)).  Producer (TMA) and consumer warps walk the
+// same ranges, so the tile stream they agree on is defined here once.
+#pragma once
+
+#ifdef __CUDACC__
+#define QMK_HD __host__ __device__ __forceinline__
+#else
+#define QMK_HD inline
+#endif
+
+namespace qmk {
+
+constexpr int kHidden = 1024;
+constexpr int kInter = 3072;
+constexpr int kNumQHeads = 16;
+constexpr int kNumKVHeads = 8;
+constexpr int kHeadDim = 128;
+constexpr int kQSize = kNumQHeads * kHeadDim;    // 2048
+constexpr int kKVSize = kNumKVHeads * kHeadDim;  // 1024
+constexpr int kQKVRows = kQSize + 2 * kKVSize;   // 4096
+constexpr int kVocab = 151936;
+constexpr int kMaxLayers = 64;
+
+constexpr int kMaxCtas = 160;
+constexpr int kMinCtas = 64;
+constexpr int kMaxSplits = 18;
+constexpr int kMergeTasks = 32;                     // 16 q heads x 2 halves
+constexpr int kMergeDims = kHeadDim / 2;            // 64 dims per merge task
+constexpr int kPartWords = 4 + 2 * kHeadDim;        // m0,l0,m1,l1,o0[128],o1[128]
+constexpr int kMergeWordsPerSplit = 2 + kMergeDims; // m, l, o[64]
+
+// Tile geometry of the shared-memory ring (all tiles <= kSlotBytes).
+constexpr int kSlotBytes = 32768;
+constexpr int kNumSlots = 6;
+constexpr int kQKVTileRows = 16;   // 16 x 2 KB
+constexpr int kOTileRows = 8;      //  8 x 4 KB
+constexpr int kGUTileRows = 8;     //  8 x 2 KB gate + 8 x 2 KB up
+constexpr int kDTileRows = 5;      //  5 x 6 KB
+constexpr int kLMTileRows = 16;    // 16 x 2 KB
+constexpr int kKVTilePos = 64;     // 64 x 256 B K + 64 x 256 B V
+constexpr int kKVTileVOffset = kKVTilePos * kHeadDim * 2;  // 16 KB
+
+struct Range {
+  int begin;
+  int end;
+};
+
+// Rows [c*n/N, (c+1)*n/N): balanced to within one row.
+QMK_HD Range split_rows(int n, int cta, int ncta) {
+  Range r;
+  r.begin = (int)(((long long)n * cta) / ncta);
+  r.end = (int)(((long long)n * (cta + 1)) / ncta);
+  return r;
+}
+
+QMK_HD Range qkv_rows(int cta, int ncta) { return split_rows(kQKVRows, cta, ncta); }
+QMK_HD Range o_rows(int cta, int ncta) { return split_rows(kHidden, cta, ncta); }
+QMK_HD Range gu_rows(int cta, int ncta) { return split_rows(kInter, cta, ncta); }
+QMK_HD Range d_rows(int cta, int ncta) { return split_rows(kHidden, cta, ncta); }
+QMK_HD Range lm_rows(int cta, int ncta) { return split_rows(kVocab, cta, ncta); }
+
+// Attention items: item i = g * splits + s lives on CTA i.
+QMK_HD int item_of_cta(int cta, int splits) {
+  return (cta < kNumKVHeads * splits) ? cta : -1;
+}
+
+// Merge task j lives on CTA ncta-1-j: q head j/2, dims [(j%2)*64, +64).
+QMK_HD int merge_task_of_cta(int cta, int ncta) {
+  int j = ncta - 1 - cta;
+  return (j >= 0 && j < kMergeTasks) ? j : -1;
+}
+
+// Previous positions [0, prev) of a KV head are cut into `splits` chunks.
+QMK_HD Range kv_chunk(int prev, int s, int splits) {
+  Range r;
+  r.begin = (int)(((long long)prev * s) / splits);
+  r.end = (int)(((long long)prev * (s + 1)) / splits);
+  return r;
+}
+
+// Splits per KV head for a launch whose largest "previous positions" count is
+// max_prev: ~64 positions per split, at most kMaxSplits and at most ncta/8.
+QMK_HD int attention_splits(int ncta, int max_prev) {
+  int s = (max_prev + 63) / 64;
+  int cap = ncta / kNumKVHeads;
+  if (cap > kMaxSplits) cap = kMaxSplits;
+  if (s > cap) s = cap;
+  if (s < 1) s = 1;
+  return s;
+}
+
+// Workspace layout (bytes).  Control block first, then the 8-byte dataflow
+// ("LL": value | flag << 32) buffers.
+constexpr int kCtrlBytes = 8192;
+constexpr int kWordsX = kHidden;
+constexpr int kWordsQKV = kQKVRows;
+constexpr int kWordsPart = kNumKVHeads * kMaxSplits * kPartWords;
+constexpr int kWordsAtt = kQSize;
+constexpr int kWordsA = kHidden;
+constexpr int kWordsM = kInter;
+constexpr int kWordsArg = 2 * kMaxCtas;
+constexpr long long kOffX = kCtrlBytes;
+constexpr long long kOffQKV = kOffX + 8LL * kWordsX;
+constexpr long long kOffPart = kOffQKV + 8LL * kWordsQKV;
+constexpr long long kOffAtt = kOffPart + 8LL * kWordsPart;
+constexpr long long kOffA = kOffAtt + 8LL * kWordsAtt;
+constexpr long long kOffM = kOffA + 8LL * kWordsA;
+constexpr long long kOffArg = kOffM + 8LL * kWordsM;
+constexpr long long kWorkspaceBytes = ((kOffArg + 8LL * kWordsArg) + 4095) / 4096 * 4096;
+
+// Control block (first kCtrlBytes of the workspace).
+struct Ctrl {
+  unsigned epoch;       // flag epoch base for the next launch
+  unsigned exit_count;  // CTAs that finished the current launch
+  unsigned err_code;    // first device error of the current launch
+  unsigned err_info;
+  unsigned launches;
+  unsigned pad[27];
+  unsigned kv_ready[kMaxLayers * kNumKVHeads];  // epoch of the last K/V row written
+};
+static_assert(sizeof(Ctrl) <= kCtrlBytes, "control block too large");
+
+}  // namespace qmk
