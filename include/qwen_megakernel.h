@@ -158,6 +158,16 @@ typedef struct QmkRunArgs {
                                          /* on a flag no CTA writes, so its       */
                                          /* bounded wait expires: the launch ends */
                                          /* with QMK_ERR_TIMEOUT in the status    */
+  unsigned long long *trace;             /* optional device buffer of            */
+                                         /* qmk_trace_words() uint64 globaltimer */
+                                         /* stamps per CTA for step trace_step   */
+  int trace_step;
+  unsigned int poll_backoff_ns;          /* tuning: sleep between failed polls */
+                                         /* of dataflow words (0 = spin; <= 4096) */
+  unsigned int tuning;                   /* tuning flags (0 = default); bits 0-1: */
+                                         /* store kind of dataflow words (0 red.max */
+                                         /* atomic, 1 st.relaxed, 2 st.relaxed +   */
+                                         /* fence per phase, 3 atom.exch)          */
 } QmkRunArgs;
 
 /* Bytes of device workspace one decoder needs (flags, dataflow buffers). */
@@ -192,6 +202,11 @@ int qmk_attention_splits(int num_ctas, int max_position);
  *   {qkv_row0, qkv_row1, o_row0, o_row1, gu_row0, gu_row1, d_row0, d_row1}
  * and out[8..11] with {lm_row0, lm_row1, item (or -1), merge_task (or -1)}. */
 int qmk_describe_partition(int num_ctas, int splits, int cta, int *out, int out_len);
+
+/* uint64 words per CTA of the optional timeline trace (QmkRunArgs.trace):
+ * per layer 16 slots (phase input-ready / done stamps, producer issue
+ * window), then the LM-head slots. */
+int qmk_trace_words(void);
 
 /* Library version string. */
 const char *qmk_version(void);

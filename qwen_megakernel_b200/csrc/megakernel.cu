@@ -39,9 +39,11 @@
 
 namespace qmk {
 
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 7;  // + 1 producer warp = 8 warps: 255 registers per thread
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
+
+__device__ __forceinline__ void consumer_sync() { named_sync<kConsumerThreads>(); }
 constexpr float kRmsEps = 1e-6f;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s
@@ -87,6 +89,10 @@ struct Params {
   QmkStatus *status;
   unsigned long long timeout_ns;
   int debug_stall;
+  unsigned long long *trace;  // optional [ncta][kTraceStride] globaltimer stamps
+  int trace_step;
+  unsigned poll_backoff_ns;
+  unsigned tuning;
 };
 
 // Dynamic shared memory plan (bytes).
@@ -109,6 +115,20 @@ constexpr int kUPW = 768;   // per-warp partials [8][260]
 static_assert(kUPW + kConsumerWarps * kPartWords <= kInter, "attention scratch too large");
 static_assert(kMaxSplits * kMergeWordsPerSplit <= kInter, "merge scratch too large");
 
+// Optional timeline trace (one step): per CTA, per layer 16 slots
+//   0 P1 input ready   1 P1 done   2 P2 q/k/v ready  3 P2 done
+//   4 P2.5 ready       5 P2.5 done 6 P3 ATT ready    7 P3 done
+//   8 P4 A ready       9 P4 done  10 P5 M ready     11 P5 done
+//  12 producer: first tile of the layer issued  13 producer: last tile issued
+// and after the last layer (slot base num_layers*16): 0 LM input ready,
+// 1 LM done, 3 producer LM first tile, 4 producer LM last tile, 5 step start.
+// Then, per ring tile k of the step (k < kTraceTiles): [kTraceTileBase + 2k]
+// consumer warp 0 starts waiting for it, [+2k+1] it has landed, and
+// [kTraceTileBase + 2*kTraceTiles + k] the producer issued its copy.
+constexpr int kTraceTiles = 512;
+constexpr int kTraceTileBase = (kMaxLayers + 1) * 16;
+constexpr int kTraceStride = kTraceTileBase + 3 * kTraceTiles;
+
 struct Ctx {
   uint8_t *ring;
   uint64_t *full;
@@ -123,10 +143,28 @@ struct Ctx {
   unsigned E0;
   unsigned long long timeout_ns;
   int cur_layer;
+  unsigned long long *trace;  // this CTA's trace row, or nullptr
+  uint32_t trace_tile0;       // ring tile index at the start of the traced step
+  unsigned poll_backoff_ns;   // sleep between failed dataflow polls (0: spin)
+  unsigned tuning;            // QmkRunArgs.tuning
 };
 
 __device__ __forceinline__ unsigned epoch_of(const Ctx &c, int step, int layer, int num_layers) {
   return c.E0 + 1u + (unsigned)step * (unsigned)(num_layers + 1) + (unsigned)layer;
+}
+
+// Hardware approximations (ex2.approx / rcp.approx, ~2 ulp) for the softmax
+// and SiLU: they sit on dependent chains where libm's accurate sequences
+// cost several times the latency.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned *p) {
@@ -135,12 +173,44 @@ __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned *p) {
   return v;
 }
 
-__device__ void raise_error(Ctx &c, unsigned code, unsigned site) {
-  *c.abort_flag = 1;
-  if (atomicCAS(&c.ctrl->err_code, 0u, code) == 0u) {
-    atomicExch(&c.ctrl->err_info,
-               ((unsigned)c.cta << 16) | ((site & 0xffu) << 8) | ((unsigned)c.cur_layer & 0xffu));
+__device__ __forceinline__ void trace_stamp(const Ctx &c, bool active, int slot) {
+  if (active && c.trace) c.trace[slot] = global_timer_ns();
+}
+
+// Slow paths stay out of line: the kernel cycles through all of its phases
+// every layer, so code that is rarely executed should not sit in the hot
+// instruction stream.
+__device__ __noinline__ void raise_error_at(volatile int *abort_flag, Ctrl *ctrl, unsigned code,
+                                            unsigned site, int cta, int layer) {
+  *abort_flag = 1;
+  if (atomicCAS(&ctrl->err_code, 0u, code) == 0u) {
+    atomicExch(&ctrl->err_info, ((unsigned)cta << 16) | ((site & 0xffu) << 8) | ((unsigned)layer & 0xffu));
   }
+}
+
+__device__ __forceinline__ void raise_error(Ctx &c, unsigned code, unsigned site) {
+  raise_error_at(c.abort_flag, c.ctrl, code, site, c.cta, c.cur_layer);
+}
+
+// Every 16th failed poll: abort / deadline / foreign-error checks.  Returns
+// the (possibly newly set) deadline, or 0 when the wait must give up.
+__device__ __noinline__ uint64_t wait_checkpoint(volatile int *abort_flag, Ctrl *ctrl, uint64_t deadline,
+                                                 unsigned it, unsigned long long timeout_ns, unsigned site,
+                                                 int cta, int layer) {
+  if (*abort_flag) return 0;
+  const uint64_t now = global_timer_ns();
+  if (deadline == 0) {
+    deadline = now + timeout_ns;
+  } else if (now > deadline || it > (1u << 30)) {
+    raise_error_at(abort_flag, ctrl, QMK_ERR_TIMEOUT, site, cta, layer);
+    return 0;
+  }
+  if ((it & 1023u) == 0u && ld_relaxed_u32(&ctrl->err_code) != 0u) {
+    *abort_flag = 1;  // another CTA failed: stop waiting for it
+    return 0;
+  }
+  if (it > 64u) __nanosleep(64);
+  return deadline;
 }
 
 // Bounded-wait bookkeeping: call keep_going() once per failed poll.
@@ -149,28 +219,18 @@ struct Waiter {
   unsigned it = 0;
   __device__ __forceinline__ bool keep_going(Ctx &c, unsigned site) {
     ++it;
-    if ((it & 15u) == 0u) {
-      if (*c.abort_flag) return false;
-      const uint64_t now = global_timer_ns();
-      if (deadline == 0) {
-        deadline = now + c.timeout_ns;
-      } else if (now > deadline || it > (1u << 30)) {
-        raise_error(c, QMK_ERR_TIMEOUT, site);
-        return false;
-      }
-      if ((it & 1023u) == 0u && ld_relaxed_u32(&c.ctrl->err_code) != 0u) {
-        *c.abort_flag = 1;  // another CTA failed: stop waiting for it
-        return false;
-      }
-      if (it > 64u) __nanosleep(64);
-    }
-    return true;
+    if ((it & 15u) != 0u) return true;
+    deadline = wait_checkpoint(c.abort_flag, c.ctrl, deadline, it, c.timeout_ns, site, c.cta, c.cur_layer);
+    return deadline != 0;
   }
 };
 
 // ------------------------------------------------------------- ring (consumer)
 __device__ __forceinline__ bool wait_full(Ctx &c, uint32_t tile) {
   bool ok = (*c.abort_flag == 0);
+  const uint32_t k = tile - c.trace_tile0;
+  const bool stamp = c.trace && threadIdx.x == 0 && k < (uint32_t)kTraceTiles;
+  if (stamp) c.trace[kTraceTileBase + 2 * k] = global_timer_ns();
   if (ok) {
     const int slot = tile % kNumSlots;
     const unsigned par = (tile / kNumSlots) & 1u;
@@ -182,6 +242,7 @@ __device__ __forceinline__ bool wait_full(Ctx &c, uint32_t tile) {
       }
     }
   }
+  if (stamp) c.trace[kTraceTileBase + 2 * k + 1] = global_timer_ns();
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -195,12 +256,18 @@ __device__ __forceinline__ const uint8_t *slot_ptr(const Ctx &c, uint32_t tile) 
 }
 
 // ------------------------------------------------------------- LL staging
-// All 256 consumer threads: poll N = 512*P words of `src` (flag == expected)
-// into fp32 `dst`, then consumer_sync().
-template <int P>
+// All consumer threads: poll the N words of `src` (flag == expected) into
+// fp32 `dst`, two words per 16-byte load, then consumer_sync().
+template <int N>
 __device__ void stage_vec(Ctx &c, float *dst, const uint64_t *src, unsigned flag, unsigned site) {
+  constexpr int kPairs = N / 2;
+  constexpr int P = (kPairs + kConsumerThreads - 1) / kConsumerThreads;
+  static_assert(N % 2 == 0 && P <= 32, "stage_vec size");
   const int tid = threadIdx.x;
-  unsigned pending = (1u << P) - 1u;
+  unsigned pending = 0;
+#pragma unroll
+  for (int k = 0; k < P; ++k)
+    if (k * kConsumerThreads + tid < kPairs) pending |= 1u << k;
   if (*c.abort_flag) pending = 0;
   Waiter w;
   while (pending) {
@@ -219,13 +286,17 @@ __device__ void stage_vec(Ctx &c, float *dst, const uint64_t *src, unsigned flag
         pending &= ~(1u << k);
       }
     }
-    if (pending && !w.keep_going(c, site)) break;
+    if (pending) {
+      if (!w.keep_going(c, site)) break;
+      if (c.poll_backoff_ns) __nanosleep(c.poll_backoff_ns);
+    }
   }
   consumer_sync();
 }
 
 // Poll up to K words per thread at arbitrary addresses: word i (i < n) of the
-// list is fetched by thread i % 256 from addr(i) and stored to dst[i].
+// list is fetched by consumer thread i % kConsumerThreads from addr(i) and
+// stored to dst[i].
 template <int K, typename AddrFn>
 __device__ void stage_list(Ctx &c, float *dst, int n, AddrFn addr, unsigned flag, unsigned site) {
   const int tid = threadIdx.x;
@@ -249,7 +320,10 @@ __device__ void stage_list(Ctx &c, float *dst, int n, AddrFn addr, unsigned flag
         pending &= ~(1u << k);
       }
     }
-    if (pending && !w.keep_going(c, site)) break;
+    if (pending) {
+      if (!w.keep_going(c, site)) break;
+      if (c.poll_backoff_ns) __nanosleep(c.poll_backoff_ns);
+    }
   }
   consumer_sync();
 }
@@ -273,10 +347,17 @@ __device__ __forceinline__ void load_act(float (&act)[J * 8], const float *s, in
   }
 }
 
+// Norm weights of lane l's columns (see load_act<4>), fetched before the
+// dataflow wait so their L2 latency overlaps it.
+__device__ __forceinline__ void load_norm_w(uint4 (&wv)[4], const __nv_bfloat16 *w, int lane) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) wv[j] = __ldg(reinterpret_cast<const uint4 *>(w + 256 * j + 8 * lane));
+}
+
 // act <- RMSNorm(s) * w (fp32, eps 1e-6), for a 1024-vector.  Each warp holds
 // the whole vector across its lanes, so no cross-warp reduction is needed.
-__device__ __forceinline__ void rmsnorm_act(float (&act)[32], const float *s,
-                                            const __nv_bfloat16 *w, int lane) {
+__device__ __forceinline__ void rmsnorm_act(float (&act)[32], const float *s, const uint4 (&wv)[4],
+                                            int lane) {
   load_act<4>(act, s, lane);
   float ss = 0.f;
 #pragma unroll
@@ -285,8 +366,7 @@ __device__ __forceinline__ void rmsnorm_act(float (&act)[32], const float *s,
   const float r = rsqrtf(ss / (float)kHidden + kRmsEps);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(w + 256 * j + 8 * lane));
-    const unsigned ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    const unsigned ww[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       act[j * 8 + 2 * e] = (act[j * 8 + 2 * e] * r) * bf_lo(ww[e]);
@@ -315,27 +395,29 @@ __device__ __forceinline__ float dot_row(const uint8_t *row, const float (&act)[
 }
 
 // Process rows [0, n) of one ring tile holding rows of K = 256*J; warp w takes
-// rows w, w+8, ...; `emit(local_row, value)` is called by every lane.
-template <int J, typename Emit>
+// rows w, w+W, ... (W consumer warps) and keeps R of them in flight so their
+// load -> FMA -> shuffle-reduction chains overlap.  `emit(local_row, value)`
+// is called by every lane.
+template <int J, int R, typename Emit>
 __device__ __forceinline__ void gemv_tile(const uint8_t *base, int n, const float (&act)[J * 8],
                                           int warp, int lane, Emit emit) {
-  int r = warp;
-  // Two rows in flight for K = 1024; longer rows already expose J independent
-  // 16-byte loads per lane, and pairing them would exceed the register budget.
-  for (; J <= 4 && r + kConsumerWarps < n; r += 2 * kConsumerWarps) {
-    float a = dot_row<J>(base + (size_t)r * (512 * J), act, lane);
-    float b = dot_row<J>(base + (size_t)(r + kConsumerWarps) * (512 * J), act, lane);
+  for (int r0 = warp; r0 < n; r0 += R * kConsumerWarps) {
+    float acc[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const int r = r0 + i * kConsumerWarps;
+      acc[i] = (r < n) ? dot_row<J>(base + (size_t)r * (512 * J), act, lane) : 0.f;
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      a += __shfl_xor_sync(0xffffffffu, a, o);
-      b += __shfl_xor_sync(0xffffffffu, b, o);
+#pragma unroll
+      for (int i = 0; i < R; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
     }
-    emit(r, a);
-    emit(r + kConsumerWarps, b);
-  }
-  if (r < n) {
-    const float a = warp_sum(dot_row<J>(base + (size_t)r * (512 * J), act, lane));
-    emit(r, a);
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const int r = r0 + i * kConsumerWarps;
+      if (r < n) emit(r, acc[i]);
+    }
   }
 }
 
@@ -422,6 +504,10 @@ struct Producer {
       return nullptr;
     }
     mbar_arrive_expect_tx(&c.full[slot], bytes);
+    if (c.trace) {
+      const uint32_t k = tile - c.trace_tile0;
+      if (k < (uint32_t)kTraceTiles) c.trace[kTraceTileBase + 2 * kTraceTiles + k] = global_timer_ns();
+    }
     return c.ring + slot * kSlotBytes;
   }
   __device__ __forceinline__ uint64_t *bar() { return &c.full[tile % kNumSlots]; }
@@ -519,16 +605,22 @@ struct Producer {
     const int item = item_of_cta(c.cta, p.splits);
     for (int t = 0; t < p.num_steps && alive; ++t) {
       const int pos = p.start_pos + t;
+      c.trace = (p.trace && t == p.trace_step) ? p.trace + (size_t)c.cta * kTraceStride : nullptr;
+      c.trace_tile0 = tile;
       for (int l = 0; l < p.num_layers && alive; ++l) {
         c.cur_layer = l;
         const LDGLayerWeights w = p.layers[l];
+        trace_stamp(c, true, l * 16 + 12);
         qkv(w, qkv_rows(c.cta, c.ncta));
         if (item >= 0) kv(t, l, item / p.splits, kv_chunk(pos, item % p.splits, p.splits));
         rows((const __nv_bfloat16 *)w.o_proj_weight, kQSize * 2, o_rows(c.cta, c.ncta), kOTileRows);
         gate_up(w, gu_rows(c.cta, c.ncta));
         rows((const __nv_bfloat16 *)w.down_proj_weight, kInter * 2, d_rows(c.cta, c.ncta), kDTileRows);
+        trace_stamp(c, true, l * 16 + 13);
       }
+      trace_stamp(c, true, p.num_layers * 16 + 3);
       rows(p.lm_head, kHidden * 2, lm_rows(c.cta, c.ncta), kLMTileRows);
+      trace_stamp(c, true, p.num_layers * 16 + 4);
     }
     // Drain: the last tile issued into each slot must land before the CTA exits.
     for (int s = 0; s < kNumSlots; ++s) {
@@ -568,23 +660,48 @@ struct Consumer {
 
   __device__ __forceinline__ bool live() const { return *c.abort_flag == 0; }
 
+  // Store of one dataflow word.  Default: an L2 atomic max (red.max.u64) --
+  // plain stores could sit in the SM's write path for microseconds before
+  // other SMs saw them, atomics are performed at L2 right away.  Tuning bits
+  // 0-1 of QmkRunArgs.tuning select alternatives for measurement:
+  // 1 st.relaxed.gpu, 2 st.relaxed.gpu + fence at the end of the phase,
+  // 3 atom.exch.b64.
+  __device__ __forceinline__ void put(uint64_t *q, uint64_t w) const {
+    switch (c.tuning & 3u) {
+      case 0: ll_store_redmax(q, w); break;
+      case 3: ll_store_exch(q, w); break;
+      default: ll_store(q, w); break;
+    }
+  }
+  __device__ __forceinline__ void flush() const {
+    if ((c.tuning & 3u) == 2u) __threadfence();
+  }
+
   // P1: RMSNorm(x) then q|k|v rows of this CTA.
-  __device__ void phase_qkv(const LDGLayerWeights &w, unsigned E) {
+  // x_flag: epoch of the X words to stage, or 0 when sX already holds the
+  // layer input (the embedding row of layer 0).
+  __device__ void phase_qkv(const LDGLayerWeights &w, unsigned E, int l, unsigned x_flag) {
+    uint4 wn[4];
+    load_norm_w(wn, (const __nv_bfloat16 *)w.input_layernorm_weight, lane);
+    if (x_flag) stage_vec<kHidden>(c, sX, c.wX, x_flag, kSiteX);
+    trace_stamp(c, tid == 0, l * 16 + 0);
     float act[32];
-    rmsnorm_act(act, sX, (const __nv_bfloat16 *)w.input_layernorm_weight, lane);
+    rmsnorm_act(act, sX, wn, lane);
     const Range R = qkv_rows(c.cta, c.ncta);
     for (int r0 = R.begin; r0 < R.end; r0 += kQKVTileRows) {
       const int n = min(kQKVTileRows, R.end - r0);
       const bool ok = wait_full(c, tile);
       if (ok) {
         uint64_t *out = c.wQKV + r0;
-        gemv_tile<4>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
-          if (lane == 0) ll_store(out + r, ll_pack(v, E));
+        gemv_tile<4, 4>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
+          if (lane == 0) put(out + r, ll_pack(v, E));
         });
       }
       release_tile(c, tile, ok);
       ++tile;
     }
+    flush();
+    trace_stamp(c, tid == 0, l * 16 + 1);
   }
 
   // P2: one split-KV attention item for KV head g (q heads 2g, 2g+1).
@@ -598,8 +715,20 @@ struct Consumer {
     float *sQ = sU + kUQ;
     float *sPW = sU + kUPW;
 
+    // Operands that do not depend on this step's activations are fetched
+    // before the dataflow wait: QK-norm weights and the position's cos/sin.
+    const int d0 = 4 * lane;
+    const bool rope_warp = warp < 2 || (warp == 2 && last);
+    uint2 nwv = make_uint2(0u, 0u), cvv = make_uint2(0u, 0u), svv = make_uint2(0u, 0u);
+    if (rope_warp) {
+      const __nv_bfloat16 *nw = (const __nv_bfloat16 *)((warp < 2) ? w.q_norm_weight : w.k_norm_weight);
+      nwv = __ldg(reinterpret_cast<const uint2 *>(nw + d0));
+      cvv = __ldg(reinterpret_cast<const uint2 *>(p.cos_t + (size_t)pos * kHeadDim + d0));
+      svv = __ldg(reinterpret_cast<const uint2 *>(p.sin_t + (size_t)pos * kHeadDim + d0));
+    }
+
     // q rows [256g, 256g+256), k rows 2048+128g.., v rows 3072+128g.. -> sU[0..512)
-    stage_list<2>(
+    stage_list<(512 + kConsumerThreads - 1) / kConsumerThreads>(
         c, sU, 512,
         [&](int i) -> const uint64_t * {
           const int row = (i < 256) ? (g * 256 + i)
@@ -608,15 +737,15 @@ struct Consumer {
           return c.wQKV + row;
         },
         E, kSiteQKV);
+    trace_stamp(c, tid == 0, layer * 16 + 2);
 
     // Per-head RMSNorm + RoPE (rotate-half).  Lane l holds dims 4l..4l+3; the
     // rotation partner dims (d +- 64) sit in lane l ^ 16.
-    const int d0 = 4 * lane;
-    const __nv_bfloat16 *cosp = p.cos_t + (size_t)pos * kHeadDim;
-    const __nv_bfloat16 *sinp = p.sin_t + (size_t)pos * kHeadDim;
-    if (warp < 2 || (warp == 2 && last)) {
+    if (rope_warp) {
       float *vec = (warp < 2) ? (sQ + warp * kHeadDim) : (sU + kUK);
-      const __nv_bfloat16 *nw = (const __nv_bfloat16 *)((warp < 2) ? w.q_norm_weight : w.k_norm_weight);
+      const float nwf[4] = {bf_lo(nwv.x), bf_hi(nwv.x), bf_lo(nwv.y), bf_hi(nwv.y)};
+      const float cvf[4] = {bf_lo(cvv.x), bf_hi(cvv.x), bf_lo(cvv.y), bf_hi(cvv.y)};
+      const float svf[4] = {bf_lo(svv.x), bf_hi(svv.x), bf_lo(svv.y), bf_hi(svv.y)};
       float x[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) x[e] = vec[d0 + e];
@@ -624,14 +753,12 @@ struct Consumer {
       ss = warp_sum(ss);
       const float r = rsqrtf(ss / (float)kHeadDim + kRmsEps);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) x[e] = (x[e] * r) * __bfloat162float(nw[d0 + e]);
+      for (int e = 0; e < 4; ++e) x[e] = (x[e] * r) * nwf[e];
       float y[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
-        const float cv = __bfloat162float(cosp[d0 + e]);
-        const float sv = __bfloat162float(sinp[d0 + e]);
-        y[e] = (lane < 16) ? (x[e] * cv - partner * sv) : (x[e] * cv + partner * sv);
+        y[e] = (lane < 16) ? (x[e] * cvf[e] - partner * svf[e]) : (x[e] * cvf[e] + partner * svf[e]);
       }
       if (warp < 2) {
         const float qs = p.attn_scale * kLog2e;  // scores in log2 units
@@ -673,26 +800,45 @@ struct Consumer {
     }
     float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
     float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
-    auto accumulate = [&](const float (&kf)[4], const float (&vf)[4]) {
-      float s0 = q0[0] * kf[0] + q0[1] * kf[1] + q0[2] * kf[2] + q0[3] * kf[3];
-      float s1 = q1[0] * kf[0] + q1[1] * kf[1] + q1[2] * kf[2] + q1[3] * kf[3];
+    // Online softmax over cache positions; two positions per step so their
+    // dot-product reductions and exponentials overlap.  `wb` = 0 disables
+    // the second position.
+    auto accumulate2 = [&](const float (&ka)[4], const float (&va)[4], const float (&kb)[4],
+                           const float (&vb)[4], bool has_b) {
+      float sa0 = q0[0] * ka[0] + q0[1] * ka[1] + q0[2] * ka[2] + q0[3] * ka[3];
+      float sa1 = q1[0] * ka[0] + q1[1] * ka[1] + q1[2] * ka[2] + q1[3] * ka[3];
+      float sb0 = q0[0] * kb[0] + q0[1] * kb[1] + q0[2] * kb[2] + q0[3] * kb[3];
+      float sb1 = q1[0] * kb[0] + q1[1] * kb[1] + q1[2] * kb[2] + q1[3] * kb[3];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
-        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        sa0 += __shfl_xor_sync(0xffffffffu, sa0, o);
+        sa1 += __shfl_xor_sync(0xffffffffu, sa1, o);
+        sb0 += __shfl_xor_sync(0xffffffffu, sb0, o);
+        sb1 += __shfl_xor_sync(0xffffffffu, sb1, o);
       }
-      const float n0 = fmaxf(m0, s0), n1 = fmaxf(m1, s1);
-      const float c0 = exp2f(m0 - n0), c1 = exp2f(m1 - n1);
-      const float p0 = exp2f(s0 - n0), p1 = exp2f(s1 - n1);
-      l0 = l0 * c0 + p0;
-      l1 = l1 * c1 + p1;
+      if (!has_b) {
+        sb0 = -INFINITY;
+        sb1 = -INFINITY;
+      }
+      const float n0 = fmaxf(m0, fmaxf(sa0, sb0)), n1 = fmaxf(m1, fmaxf(sa1, sb1));
+      const float c0 = fast_exp2(m0 - n0), c1 = fast_exp2(m1 - n1);
+      const float pa0 = fast_exp2(sa0 - n0), pa1 = fast_exp2(sa1 - n1);
+      const float pb0 = fast_exp2(sb0 - n0), pb1 = fast_exp2(sb1 - n1);
+      l0 = l0 * c0 + pa0 + pb0;
+      l1 = l1 * c1 + pa1 + pb1;
       m0 = n0;
       m1 = n1;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        o0[e] = o0[e] * c0 + p0 * vf[e];
-        o1[e] = o1[e] * c1 + p1 * vf[e];
+        o0[e] = o0[e] * c0 + pa0 * va[e] + pb0 * vb[e];
+        o1[e] = o1[e] * c1 + pa1 * va[e] + pb1 * vb[e];
       }
+    };
+    auto load_kv = [&](const uint8_t *kt, const uint8_t *vt, int j, float (&kf)[4], float (&vf)[4]) {
+      const uint2 kw = *reinterpret_cast<const uint2 *>(kt + (size_t)j * 256 + 8 * lane);
+      const uint2 vw = *reinterpret_cast<const uint2 *>(vt + (size_t)j * 256 + 8 * lane);
+      kf[0] = bf_lo(kw.x); kf[1] = bf_hi(kw.x); kf[2] = bf_lo(kw.y); kf[3] = bf_hi(kw.y);
+      vf[0] = bf_lo(vw.x); vf[1] = bf_hi(vw.x); vf[2] = bf_lo(vw.y); vf[3] = bf_hi(vw.y);
     };
     for (int j0 = ch.begin; j0 < ch.end; j0 += kKVTilePos) {
       const int n = min(kKVTilePos, ch.end - j0);
@@ -700,12 +846,13 @@ struct Consumer {
       if (ok) {
         const uint8_t *kt = slot_ptr(c, tile);
         const uint8_t *vt = kt + kKVTileVOffset;
-        for (int j = warp; j < n; j += kConsumerWarps) {
-          const uint2 kw = *reinterpret_cast<const uint2 *>(kt + (size_t)j * 256 + 8 * lane);
-          const uint2 vw = *reinterpret_cast<const uint2 *>(vt + (size_t)j * 256 + 8 * lane);
-          const float kf[4] = {bf_lo(kw.x), bf_hi(kw.x), bf_lo(kw.y), bf_hi(kw.y)};
-          const float vf[4] = {bf_lo(vw.x), bf_hi(vw.x), bf_lo(vw.y), bf_hi(vw.y)};
-          accumulate(kf, vf);
+        for (int j = warp; j < n; j += 2 * kConsumerWarps) {
+          const int jb = j + kConsumerWarps;
+          const bool has_b = jb < n;
+          float ka[4], va[4], kb[4], vb[4];
+          load_kv(kt, vt, j, ka, va);
+          load_kv(kt, vt, has_b ? jb : j, kb, vb);
+          accumulate2(ka, va, kb, vb, has_b);
         }
       }
       release_tile(c, tile, ok);
@@ -718,7 +865,7 @@ struct Consumer {
         kf[e] = sU[kUKn + d0 + e];
         vf[e] = sU[kUVn + d0 + e];
       }
-      accumulate(kf, vf);
+      accumulate2(kf, vf, kf, vf, false);
     }
     // Cross-warp merge of the online-softmax states -> PART words.
     float *pw = sPW + warp * kPartWords;
@@ -734,8 +881,8 @@ struct Consumer {
       pw[4 + kHeadDim + d0 + e] = o1[e];
     }
     consumer_sync();
-    {
-      const int hh = tid >> 7, d = tid & 127;
+    for (int i = tid; i < 2 * kHeadDim; i += kConsumerThreads) {
+      const int hh = i >> 7, d = i & 127;
       float M = -INFINITY;
 #pragma unroll
       for (int q = 0; q < kConsumerWarps; ++q) M = fmaxf(M, sPW[q * kPartWords + 2 * hh]);
@@ -745,7 +892,7 @@ struct Consumer {
         for (int q = 0; q < kConsumerWarps; ++q) {
           const float mq = sPW[q * kPartWords + 2 * hh];
           if (mq != -INFINITY) {
-            const float f = exp2f(mq - M);
+            const float f = fast_exp2(mq - M);
             L += sPW[q * kPartWords + 2 * hh + 1] * f;
             O += sPW[q * kPartWords + 4 + hh * kHeadDim + d] * f;
           }
@@ -753,18 +900,20 @@ struct Consumer {
       }
       if (live()) {
         uint64_t *part = c.wPart + (size_t)item * kPartWords;
-        ll_store(part + 4 + hh * kHeadDim + d, ll_pack(O, E));
+        put(part + 4 + hh * kHeadDim + d, ll_pack(O, E));
         if (d == 0) {
-          ll_store(part + 2 * hh, ll_pack(M, E));
-          ll_store(part + 2 * hh + 1, ll_pack(L, E));
+          put(part + 2 * hh, ll_pack(M, E));
+          put(part + 2 * hh + 1, ll_pack(L, E));
         }
       }
     }
     consumer_sync();  // sU scratch is reused by the next phase
+    flush();
+    trace_stamp(c, tid == 0, layer * 16 + 3);
   }
 
   // P2.5: merge the split partials of (q head h, 64 dims) -> ATT words.
-  __device__ void phase_merge(unsigned E) {
+  __device__ void phase_merge(unsigned E, int l) {
     const int j = merge_task_of_cta(c.cta, c.ncta);
     if (j < 0) return;
     const int h = j >> 1, half = j & 1, g = h >> 1, hl = h & 1;
@@ -778,6 +927,7 @@ struct Consumer {
           return c.wPart + (size_t)(g * S + s) * kPartWords + word;
         },
         E, kSitePart);
+    trace_stamp(c, tid == 0, l * 16 + 4);
     if (tid < kMergeDims) {
       float M = -INFINITY;
       for (int s = 0; s < S; ++s) M = fmaxf(M, sU[s * kMergeWordsPerSplit]);
@@ -785,20 +935,23 @@ struct Consumer {
       for (int s = 0; s < S; ++s) {
         const float ms = sU[s * kMergeWordsPerSplit];
         if (ms != -INFINITY) {
-          const float f = exp2f(ms - M);
+          const float f = fast_exp2(ms - M);
           L += sU[s * kMergeWordsPerSplit + 1] * f;
           O += sU[s * kMergeWordsPerSplit + 2 + tid] * f;
         }
       }
-      if (live()) ll_store(c.wAtt + h * kHeadDim + half * kMergeDims + tid, ll_pack(O / L, E));
+      if (live()) put(c.wAtt + h * kHeadDim + half * kMergeDims + tid, ll_pack(O * fast_rcp(L), E));
     }
     consumer_sync();
+    flush();
+    trace_stamp(c, tid == 0, l * 16 + 5);
   }
 
   // P3: O-projection rows + residual -> A words.
-  __device__ void phase_o(const LDGLayerWeights &w, unsigned E, bool stall) {
+  __device__ void phase_o(const LDGLayerWeights &w, unsigned E, bool stall, int l) {
     // Test hook: 0xFFFFFFFF is never an epoch, so this wait can only expire.
-    stage_vec<4>(c, sAtt, c.wAtt, stall ? 0xFFFFFFFFu : E, kSiteAtt);
+    stage_vec<kQSize>(c, sAtt, c.wAtt, stall ? 0xFFFFFFFFu : E, kSiteAtt);
+    trace_stamp(c, tid == 0, l * 16 + 6);
     float act[64];
     load_act<8>(act, sAtt, lane);
     const Range R = o_rows(c.cta, c.ncta);
@@ -806,20 +959,25 @@ struct Consumer {
       const int n = min(kOTileRows, R.end - r0);
       const bool ok = wait_full(c, tile);
       if (ok) {
-        gemv_tile<8>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
-          if (lane == 0) ll_store(c.wA + r0 + r, ll_pack(v + sX[r0 + r], E));
+        gemv_tile<8, 2>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
+          if (lane == 0) put(c.wA + r0 + r, ll_pack(v + sX[r0 + r], E));
         });
       }
       release_tile(c, tile, ok);
       ++tile;
     }
+    flush();
+    trace_stamp(c, tid == 0, l * 16 + 7);
   }
 
   // P4: RMSNorm(a) then gate/up rows, SiLU(gate) * up -> M words.
-  __device__ void phase_gate_up(const LDGLayerWeights &w, unsigned E) {
-    stage_vec<2>(c, sA, c.wA, E, kSiteA);
+  __device__ void phase_gate_up(const LDGLayerWeights &w, unsigned E, int l) {
+    uint4 wn[4];
+    load_norm_w(wn, (const __nv_bfloat16 *)w.post_attn_layernorm_weight, lane);
+    stage_vec<kHidden>(c, sA, c.wA, E, kSiteA);
+    trace_stamp(c, tid == 0, l * 16 + 8);
     float act[32];
-    rmsnorm_act(act, sA, (const __nv_bfloat16 *)w.post_attn_layernorm_weight, lane);
+    rmsnorm_act(act, sA, wn, lane);
     const Range R = gu_rows(c.cta, c.ncta);
     for (int r0 = R.begin; r0 < R.end; r0 += kGUTileRows) {
       const int n = min(kGUTileRows, R.end - r0);
@@ -827,28 +985,42 @@ struct Consumer {
       if (ok) {
         const uint8_t *gt = slot_ptr(c, tile);
         const uint8_t *ut = gt + kGUTileRows * 2048;
-        for (int r = warp; r < n; r += kConsumerWarps) {
-          float gs = dot_row<4>(gt + (size_t)r * 2048, act, lane);
-          float us = dot_row<4>(ut + (size_t)r * 2048, act, lane);
+        // Two (gate, up) row pairs in flight per warp.
+        for (int ra = warp; ra < n; ra += 2 * kConsumerWarps) {
+          const int rb = ra + kConsumerWarps;
+          const bool has_b = rb < n;
+          float gs0 = dot_row<4>(gt + (size_t)ra * 2048, act, lane);
+          float us0 = dot_row<4>(ut + (size_t)ra * 2048, act, lane);
+          float gs1 = has_b ? dot_row<4>(gt + (size_t)rb * 2048, act, lane) : 0.f;
+          float us1 = has_b ? dot_row<4>(ut + (size_t)rb * 2048, act, lane) : 0.f;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) {
-            gs += __shfl_xor_sync(0xffffffffu, gs, o);
-            us += __shfl_xor_sync(0xffffffffu, us, o);
+            gs0 += __shfl_xor_sync(0xffffffffu, gs0, o);
+            us0 += __shfl_xor_sync(0xffffffffu, us0, o);
+            gs1 += __shfl_xor_sync(0xffffffffu, gs1, o);
+            us1 += __shfl_xor_sync(0xffffffffu, us1, o);
           }
           if (lane == 0) {
-            const float silu = gs / (1.0f + expf(-gs));
-            ll_store(c.wM + r0 + r, ll_pack(silu * us, E));
+            const float silu0 = gs0 * fast_rcp(1.0f + fast_exp2(-gs0 * kLog2e));
+            put(c.wM + r0 + ra, ll_pack(silu0 * us0, E));
+            if (has_b) {
+              const float silu1 = gs1 * fast_rcp(1.0f + fast_exp2(-gs1 * kLog2e));
+              put(c.wM + r0 + rb, ll_pack(silu1 * us1, E));
+            }
           }
         }
       }
       release_tile(c, tile, ok);
       ++tile;
     }
+    flush();
+    trace_stamp(c, tid == 0, l * 16 + 9);
   }
 
   // P5: down rows + residual -> X words (next layer's input).
-  __device__ void phase_down(const LDGLayerWeights &w, unsigned E) {
-    stage_vec<6>(c, sU, c.wM, E, kSiteM);
+  __device__ void phase_down(const LDGLayerWeights &w, unsigned E, int l) {
+    stage_vec<kInter>(c, sU, c.wM, E, kSiteM);
+    trace_stamp(c, tid == 0, l * 16 + 10);
     float act[96];
     load_act<12>(act, sU, lane);
     const Range R = d_rows(c.cta, c.ncta);
@@ -856,21 +1028,26 @@ struct Consumer {
       const int n = min(kDTileRows, R.end - r0);
       const bool ok = wait_full(c, tile);
       if (ok) {
-        gemv_tile<12>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
-          if (lane == 0) ll_store(c.wX + r0 + r, ll_pack(v + sA[r0 + r], E));
+        gemv_tile<12, 1>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
+          if (lane == 0) put(c.wX + r0 + r, ll_pack(v + sA[r0 + r], E));
         });
       }
       release_tile(c, tile, ok);
       ++tile;
     }
     consumer_sync();  // sU (MLP intermediate) is reused by the next phase
+    flush();
+    trace_stamp(c, tid == 0, l * 16 + 11);
   }
 
   // Final RMSNorm + LM head rows + CTA argmax -> ARG words.
   __device__ void phase_lm_head(int step, unsigned E_x, unsigned E) {
-    stage_vec<2>(c, sX, c.wX, E_x, kSiteX);
+    uint4 wn[4];
+    load_norm_w(wn, p.final_norm, lane);
+    stage_vec<kHidden>(c, sX, c.wX, E_x, kSiteX);
+    trace_stamp(c, tid == 0, p.num_layers * 16 + 0);
     float act[32];
-    rmsnorm_act(act, sX, p.final_norm, lane);
+    rmsnorm_act(act, sX, wn, lane);
     if (p.final_hidden && c.cta == 0 && warp == 0 && step == p.num_steps - 1 && live()) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
@@ -885,7 +1062,7 @@ struct Consumer {
       const int n = min(kLMTileRows, R.end - r0);
       const bool ok = wait_full(c, tile);
       if (ok) {
-        gemv_tile<4>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
+        gemv_tile<4, 4>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
           const int row = r0 + r;
           if (v > best || (v == best && row < best_i)) {
             best = v;
@@ -917,11 +1094,13 @@ struct Consumer {
       }
       if (bi == 0x7fffffff) bi = R.begin;  // CTA without rows (not on B200)
       if (live()) {
-        ll_store(c.wArg + 2 * c.cta, ll_pack_u(bk, E));
-        ll_store(c.wArg + 2 * c.cta + 1, ll_pack_u((unsigned)bi, E));
+        put(c.wArg + 2 * c.cta, ll_pack_u(bk, E));
+        put(c.wArg + 2 * c.cta + 1, ll_pack_u((unsigned)bi, E));
       }
     }
     consumer_sync();
+    flush();
+    trace_stamp(c, tid == 0, p.num_layers * 16 + 1);
   }
 
   // Token consumed by step t.
@@ -944,6 +1123,9 @@ struct Consumer {
   __device__ void run() {
     const int L = p.num_layers;
     for (int t = 0; t < p.num_steps; ++t) {
+      c.trace = (p.trace && t == p.trace_step) ? p.trace + (size_t)c.cta * kTraceStride : nullptr;
+      c.trace_tile0 = tile;
+      trace_stamp(c, tid == 0, L * 16 + 5);
       // CTA 0 records the previous step's argmax (needed even when forced).
       if (t > 0 && c.cta == 0) {
         const int prev = read_argmax(c, epoch_of(c, t - 1, L, L));
@@ -953,24 +1135,25 @@ struct Consumer {
       // Layer-0 input: the embedding row (bf16 -> fp32).
       {
         const __nv_bfloat16 *erow = p.embed + (size_t)tok * kHidden;
-        const uint2 v = __ldg(reinterpret_cast<const uint2 *>(erow) + tid);
-        sX[4 * tid + 0] = bf_lo(v.x);
-        sX[4 * tid + 1] = bf_hi(v.x);
-        sX[4 * tid + 2] = bf_lo(v.y);
-        sX[4 * tid + 3] = bf_hi(v.y);
+        for (int i = tid; i < kHidden / 4; i += kConsumerThreads) {
+          const uint2 v = __ldg(reinterpret_cast<const uint2 *>(erow) + i);
+          sX[4 * i + 0] = bf_lo(v.x);
+          sX[4 * i + 1] = bf_hi(v.x);
+          sX[4 * i + 2] = bf_lo(v.y);
+          sX[4 * i + 3] = bf_hi(v.y);
+        }
         consumer_sync();
       }
       for (int l = 0; l < L; ++l) {
         c.cur_layer = l;
         const LDGLayerWeights w = p.layers[l];
         const unsigned E = epoch_of(c, t, l, L);
-        if (l > 0) stage_vec<2>(c, sX, c.wX, epoch_of(c, t, l - 1, L), kSiteX);
-        phase_qkv(w, E);
+        phase_qkv(w, E, l, l > 0 ? epoch_of(c, t, l - 1, L) : 0u);
         phase_attention(w, l, t, E);
-        phase_merge(E);
-        phase_o(w, E, p.debug_stall == c.cta + 1 && t == 0 && l == 0);
-        phase_gate_up(w, E);
-        phase_down(w, E);
+        phase_merge(E, l);
+        phase_o(w, E, p.debug_stall == c.cta + 1 && t == 0 && l == 0, l);
+        phase_gate_up(w, E, l);
+        phase_down(w, E, l);
       }
       phase_lm_head(t, epoch_of(c, t, L - 1, L), epoch_of(c, t, L, L));
     }
@@ -1008,6 +1191,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   c.ncta = gridDim.x;
   c.timeout_ns = p.timeout_ns;
   c.cur_layer = 0;
+  c.trace = nullptr;
+  c.trace_tile0 = 0;
+  c.poll_backoff_ns = p.poll_backoff_ns;
+  c.tuning = p.tuning;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kNumSlots; ++s) {
@@ -1039,7 +1226,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       __threadfence();
       const unsigned used = (unsigned)p.num_steps * (unsigned)(p.num_layers + 1) + 1u;
       unsigned next = c.E0 + used;
-      if (next > kEpochWrap) next = 0;
+      if (next > kEpochWrap) {
+        // Epochs restart from 1.  Dataflow words are written with atomic max
+        // on the epoch, so the old high-epoch words must be cleared first;
+        // every other CTA has finished, nothing reads them concurrently.
+        next = 0;
+        uint64_t *ll = reinterpret_cast<uint64_t *>(p.ws + kOffX);
+        const long long nwords = (kOffArg + 8LL * kWordsArg - kOffX) / 8;
+        for (long long i = 0; i < nwords; ++i) ll[i] = 0ull;
+        __threadfence();
+      }
       const unsigned code = ld_relaxed_u32(&c.ctrl->err_code);
       const unsigned info = ld_relaxed_u32(&c.ctrl->err_info);
       const unsigned launches = c.ctrl->launches + 1u;
@@ -1136,6 +1332,8 @@ extern "C" {
 size_t qmk_workspace_bytes(void) { return (size_t)qmk::kWorkspaceBytes; }
 
 const char *qmk_version(void) { return "qwen_megakernel_b200 0.1 (sm_100a)"; }
+
+int qmk_trace_words(void) { return qmk::kTraceStride; }
 
 const char *qmk_error_string(int code) {
   switch (code) {
@@ -1261,6 +1459,10 @@ int qmk_run(const QmkRunArgs *a, cudaStream_t stream) {
   p.status = a->status;
   p.timeout_ns = a->timeout_ns ? a->timeout_ns : qmk::kDefaultTimeoutNs;
   p.debug_stall = (a->debug_stall > 0 && a->debug_stall <= ncta) ? a->debug_stall : 0;
+  p.trace = a->trace;
+  p.trace_step = a->trace_step;
+  p.poll_backoff_ns = a->poll_backoff_ns > 4096u ? 4096u : a->poll_backoff_ns;
+  p.tuning = a->tuning;
 
   void *kargs[] = {&p};
   cudaError_t e = cudaLaunchCooperativeKernel((const void *)qmk::decode_kernel, dim3(ncta),

@@ -84,6 +84,16 @@ __device__ __forceinline__ uint64_t ll_pack_u(unsigned v, unsigned flag) {
 __device__ __forceinline__ void ll_store(uint64_t *p, uint64_t w) {
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+// The same word written as an L2 atomic: max works because the epoch in the
+// high half only grows, so the new word is always the larger one.
+__device__ __forceinline__ void ll_store_redmax(uint64_t *p, uint64_t w) {
+  asm volatile("red.relaxed.gpu.global.max.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void ll_store_exch(uint64_t *p, uint64_t w) {
+  uint64_t old;
+  asm volatile("atom.relaxed.gpu.global.exch.b64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(w) : "memory");
+  (void)old;
+}
 __device__ __forceinline__ uint64_t ll_load(const uint64_t *p) {
   uint64_t w;
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
@@ -109,8 +119,12 @@ __device__ __forceinline__ unsigned ld_volatile_u32(const unsigned *p) {
   return *reinterpret_cast<const volatile unsigned *>(p);
 }
 
-// Consumer-warp named barrier (warps 0..7; the producer warp never joins).
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Named barrier 1 over the first `kThreads` threads of the CTA (the
+// consumer warps; the producer warp never joins it).
+template <int kThreads>
+__device__ __forceinline__ void named_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+}
 
 // ------------------------------------------------------------------ math
 __device__ __forceinline__ float bf_lo(unsigned u) { return __uint_as_float(u << 16); }

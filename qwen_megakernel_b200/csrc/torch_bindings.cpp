@@ -10,35 +10,63 @@
 //
 // Added operators (no reference counterpart):
 //   run(...)             -> qmk_run with a caller-owned workspace, optional
-//                           forced-token stream, fp32 logits, status block
+//                           forced-token stream, fp32 logits, status block, trace
 //   workspace_bytes()    -> qmk_workspace_bytes
 //   workspace_init(ws)   -> qmk_workspace_init
 //   default_status()     -> qmk_read_default_status (after a synchronize)
 //   num_ctas()           -> qmk_num_ctas(current device)
+//   trace_words()        -> qmk_trace_words
 #include <Python.h>
+
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <cuda_runtime.h>
 #include <torch/all.h>
 #include <torch/library.h>
 
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+
 #include "qwen_megakernel.h"
 
 namespace {
 
-void check_cuda(const torch::Tensor &t, const char *name) {
-  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
-  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+// Error messages are formatted with vsnprintf and handed to TORCH_CHECK as a
+// plain C string.  This library is compiled against GCC 13 headers but runs
+// on the process's newer libstdc++; iostream number formatting instantiated
+// from the older headers crashed inside the newer runtime's facets, so no
+// number is ever streamed through an iostream here.
+[[noreturn]] void fail(const char *fmt, ...) {
+  char buf[640];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  TORCH_CHECK(false, static_cast<const char *>(buf));
+  abort();  // unreachable
 }
 
-void check_bf16(const torch::Tensor &t, const char *name) {
+#define QMK_CHECK(cond, ...)          \
+  do {                                \
+    if (!(cond)) fail(__VA_ARGS__);   \
+  } while (0)
+
+using ll = long long;
+
+void check_cuda(const torch::Tensor &t, const char *name) {
+  QMK_CHECK(t.is_cuda(), "%s must be a CUDA tensor", name);
+  QMK_CHECK(t.is_contiguous(), "%s must be contiguous", name);
+}
+
+void check_dtype(const torch::Tensor &t, c10::ScalarType want, const char *name, const char *want_name) {
   check_cuda(t, name);
-  TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, " must be bfloat16, got ", t.scalar_type());
+  QMK_CHECK(t.scalar_type() == want, "%s must be %s", name, want_name);
 }
 
 void check_same_device(const torch::Tensor &t, const torch::Tensor &ref, const char *name) {
-  TORCH_CHECK(t.device() == ref.device(), name, " is on ", t.device(), " but the weights are on ",
-              ref.device());
+  QMK_CHECK(t.device() == ref.device(), "%s is on cuda:%d but the weights are on cuda:%d", name,
+            (int)t.device().index(), (int)ref.device().index());
 }
 
 // Shared checks of the model tensors of every operator.
@@ -47,54 +75,58 @@ void check_model(const torch::Tensor &embed_weight, const torch::Tensor &layer_w
                  const torch::Tensor &cos_table, const torch::Tensor &sin_table,
                  const torch::Tensor &k_cache, const torch::Tensor &v_cache, int64_t num_layers,
                  int64_t last_position, int64_t max_seq_len) {
-  check_bf16(embed_weight, "embed_weight");
-  TORCH_CHECK(embed_weight.dim() == 2 && embed_weight.size(0) == QMK_VOCAB &&
-                  embed_weight.size(1) == QMK_HIDDEN,
-              "embed_weight must be [", QMK_VOCAB, ", ", QMK_HIDDEN, "], got ", embed_weight.sizes());
-  check_bf16(lm_head_weight, "lm_head_weight");
-  TORCH_CHECK(lm_head_weight.sizes() == embed_weight.sizes(), "lm_head_weight must be [", QMK_VOCAB,
-              ", ", QMK_HIDDEN, "]");
-  check_bf16(final_norm_weight, "final_norm_weight");
-  TORCH_CHECK(final_norm_weight.numel() == QMK_HIDDEN, "final_norm_weight must have ", QMK_HIDDEN,
-              " elements");
+  check_dtype(embed_weight, torch::kBFloat16, "embed_weight", "bfloat16");
+  QMK_CHECK(embed_weight.dim() == 2 && embed_weight.size(0) == QMK_VOCAB && embed_weight.size(1) == QMK_HIDDEN,
+            "embed_weight must be [%d, %d]", QMK_VOCAB, QMK_HIDDEN);
+  check_dtype(lm_head_weight, torch::kBFloat16, "lm_head_weight", "bfloat16");
+  QMK_CHECK(lm_head_weight.sizes() == embed_weight.sizes(), "lm_head_weight must be [%d, %d]", QMK_VOCAB,
+            QMK_HIDDEN);
+  check_dtype(final_norm_weight, torch::kBFloat16, "final_norm_weight", "bfloat16");
+  QMK_CHECK(final_norm_weight.numel() == QMK_HIDDEN, "final_norm_weight must have %d elements", QMK_HIDDEN);
   check_cuda(layer_weights_packed, "layer_weights_packed");
-  TORCH_CHECK(num_layers >= 1 && num_layers <= QMK_MAX_LAYERS, "num_layers must be in [1, ",
-              QMK_MAX_LAYERS, "], got ", num_layers);
-  TORCH_CHECK(layer_weights_packed.nbytes() >= (size_t)num_layers * sizeof(LDGLayerWeights),
-              "layer_weights_packed holds ", layer_weights_packed.nbytes(), " bytes; ", num_layers,
-              " layers need ", (size_t)num_layers * sizeof(LDGLayerWeights));
-  check_bf16(cos_table, "cos_table");
-  check_bf16(sin_table, "sin_table");
-  TORCH_CHECK(cos_table.dim() == 2 && cos_table.size(1) == QMK_HEAD_DIM,
-              "cos_table must be [rows, 128], got ", cos_table.sizes());
-  TORCH_CHECK(sin_table.sizes() == cos_table.sizes(), "sin_table must match cos_table");
-  TORCH_CHECK(cos_table.size(0) > last_position, "cos/sin tables have ", cos_table.size(0),
-              " rows; position ", last_position, " needs ", last_position + 1);
-  check_bf16(k_cache, "k_cache");
-  check_bf16(v_cache, "v_cache");
-  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(0) >= num_layers && k_cache.size(1) == QMK_NUM_KV_HEADS &&
-                  k_cache.size(2) == max_seq_len && k_cache.size(3) == QMK_HEAD_DIM,
-              "k_cache must be [>=num_layers, 8, max_seq_len=", max_seq_len, ", 128], got ",
-              k_cache.sizes());
-  TORCH_CHECK(v_cache.sizes() == k_cache.sizes(), "v_cache must match k_cache");
-  TORCH_CHECK(last_position < max_seq_len, "position ", last_position, " >= max_seq_len ", max_seq_len);
-  for (const torch::Tensor *t : {&layer_weights_packed, &final_norm_weight, &lm_head_weight, &cos_table,
-                                 &sin_table, &k_cache, &v_cache})
-    check_same_device(*t, embed_weight, "tensor");
+  QMK_CHECK(num_layers >= 1 && num_layers <= QMK_MAX_LAYERS, "num_layers must be in [1, %d], got %lld",
+            QMK_MAX_LAYERS, (ll)num_layers);
+  QMK_CHECK(layer_weights_packed.nbytes() >= (size_t)num_layers * sizeof(LDGLayerWeights),
+            "layer_weights_packed holds %lld bytes; %lld layers need %lld", (ll)layer_weights_packed.nbytes(),
+            (ll)num_layers, (ll)(num_layers * (int64_t)sizeof(LDGLayerWeights)));
+  check_dtype(cos_table, torch::kBFloat16, "cos_table", "bfloat16");
+  check_dtype(sin_table, torch::kBFloat16, "sin_table", "bfloat16");
+  QMK_CHECK(cos_table.dim() == 2 && cos_table.size(1) == QMK_HEAD_DIM, "cos_table must be [rows, %d]",
+            QMK_HEAD_DIM);
+  QMK_CHECK(sin_table.sizes() == cos_table.sizes(), "sin_table must match cos_table");
+  QMK_CHECK(cos_table.size(0) > last_position, "cos/sin tables have %lld rows; position %lld needs %lld",
+            (ll)cos_table.size(0), (ll)last_position, (ll)(last_position + 1));
+  check_dtype(k_cache, torch::kBFloat16, "k_cache", "bfloat16");
+  check_dtype(v_cache, torch::kBFloat16, "v_cache", "bfloat16");
+  QMK_CHECK(k_cache.dim() == 4 && k_cache.size(0) >= num_layers && k_cache.size(1) == QMK_NUM_KV_HEADS &&
+                k_cache.size(2) == max_seq_len && k_cache.size(3) == QMK_HEAD_DIM,
+            "k_cache must be [>=num_layers, %d, max_seq_len=%lld, %d]", QMK_NUM_KV_HEADS, (ll)max_seq_len,
+            QMK_HEAD_DIM);
+  QMK_CHECK(v_cache.sizes() == k_cache.sizes(), "v_cache must match k_cache");
+  QMK_CHECK(last_position < max_seq_len, "position %lld >= max_seq_len %lld", (ll)last_position,
+            (ll)max_seq_len);
+  const torch::Tensor *others[] = {&layer_weights_packed, &final_norm_weight, &lm_head_weight, &cos_table,
+                                   &sin_table,            &k_cache,           &v_cache};
+  for (const torch::Tensor *t : others) check_same_device(*t, embed_weight, "model tensor");
+}
+
+void check_token(int64_t tok, const char *name) {
+  QMK_CHECK(tok >= 0 && tok < QMK_VOCAB, "%s %lld outside [0, %d)", name, (ll)tok, QMK_VOCAB);
+}
+
+void check_normalized(const torch::Tensor &normalized) {
+  check_dtype(normalized, torch::kFloat32, "normalized", "float32");
+  QMK_CHECK(normalized.numel() >= QMK_HIDDEN, "normalized must have >= %d elements", QMK_HIDDEN);
 }
 
 void raise_if_error(int rc) {
-  if (rc != QMK_OK) {
-    TORCH_CHECK(false, "qwen_megakernel: ", qmk_error_string(rc), ": ", qmk_get_last_error_message());
-  }
+  if (rc != QMK_OK) fail("qwen_megakernel: %s: %s", qmk_error_string(rc), qmk_get_last_error_message());
 }
 
 void raise_if_status(const QmkStatus &st) {
-  if (st.error_code != QMK_OK) {
-    TORCH_CHECK(false, "qwen_megakernel: device error: ", qmk_error_string((int)st.error_code),
-                " (cta ", (st.error_info >> 16), ", site ", ((st.error_info >> 8) & 0xff), ", layer ",
-                (st.error_info & 0xff), ")");
-  }
+  if (st.error_code != QMK_OK)
+    fail("qwen_megakernel: device error: %s (cta %u, site %u, layer %u)", qmk_error_string((int)st.error_code),
+         st.error_info >> 16, (st.error_info >> 8) & 0xffu, st.error_info & 0xffu);
 }
 
 }  // namespace
@@ -108,17 +140,13 @@ void decode(torch::Tensor output_token, int64_t input_token_id, torch::Tensor em
             torch::Tensor v, torch::Tensor attn_out, torch::Tensor mlp_intermediate,
             torch::Tensor normalized, torch::Tensor block_max_vals, torch::Tensor block_max_idxs,
             int64_t num_layers, int64_t position, int64_t max_seq_len, double attn_scale) {
+  QMK_CHECK(position >= 0, "position must be >= 0");
   check_model(embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight, cos_table,
               sin_table, k_cache, v_cache, num_layers, position, max_seq_len);
-  TORCH_CHECK(position >= 0, "position must be >= 0");
-  TORCH_CHECK(input_token_id >= 0 && input_token_id < QMK_VOCAB, "input_token_id ", input_token_id,
-              " outside [0, ", QMK_VOCAB, ")");
-  check_cuda(output_token, "output_token");
-  TORCH_CHECK(output_token.scalar_type() == torch::kInt32 && output_token.numel() >= 1,
-              "output_token must be int32 with >= 1 element");
-  check_cuda(normalized, "normalized");
-  TORCH_CHECK(normalized.scalar_type() == torch::kFloat32 && normalized.numel() >= QMK_HIDDEN,
-              "normalized must be float32 with >= ", QMK_HIDDEN, " elements");
+  check_token(input_token_id, "input_token_id");
+  check_dtype(output_token, torch::kInt32, "output_token", "int32");
+  QMK_CHECK(output_token.numel() >= 1, "output_token must have >= 1 element");
+  check_normalized(normalized);
   c10::cuda::CUDAGuard guard(embed_weight.device());
   launch_ldg_decode_direct(
       (int)input_token_id, static_cast<int *>(output_token.data_ptr()), embed_weight.data_ptr(),
@@ -144,19 +172,15 @@ torch::Tensor generate_nosync(int64_t first_token_id, int64_t num_steps, torch::
                               torch::Tensor normalized, torch::Tensor block_max_vals,
                               torch::Tensor block_max_idxs, int64_t num_layers,
                               int64_t start_position, int64_t max_seq_len, double attn_scale) {
-  TORCH_CHECK(num_steps >= 1, "num_steps must be >= 1");
-  TORCH_CHECK(start_position >= 0, "start_position must be >= 0");
+  QMK_CHECK(num_steps >= 1, "num_steps must be >= 1");
+  QMK_CHECK(start_position >= 0, "start_position must be >= 0");
   check_model(embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight, cos_table,
               sin_table, k_cache, v_cache, num_layers, start_position + num_steps - 1, max_seq_len);
-  TORCH_CHECK(first_token_id >= 0 && first_token_id < QMK_VOCAB, "first_token_id ", first_token_id,
-              " outside [0, ", QMK_VOCAB, ")");
-  check_cuda(normalized, "normalized");
-  TORCH_CHECK(normalized.scalar_type() == torch::kFloat32 && normalized.numel() >= QMK_HIDDEN,
-              "normalized must be float32 with >= ", QMK_HIDDEN, " elements");
+  check_token(first_token_id, "first_token_id");
+  check_normalized(normalized);
   c10::cuda::CUDAGuard guard(embed_weight.device());
   auto stream = c10::cuda::getCurrentCUDAStream().stream();
-  auto output_log =
-      torch::empty({num_steps}, torch::dtype(torch::kInt32).device(embed_weight.device()));
+  auto output_log = torch::empty({num_steps}, torch::dtype(torch::kInt32).device(embed_weight.device()));
   launch_ldg_generate_nosync(
       (int)first_token_id, (int)num_steps, embed_weight.data_ptr(),
       reinterpret_cast<const LDGLayerWeights *>(layer_weights_packed.data_ptr()),
@@ -168,14 +192,14 @@ torch::Tensor generate_nosync(int64_t first_token_id, int64_t num_steps, torch::
       (int)num_layers, (int)start_position, (int)max_seq_len, (float)attn_scale, stream);
   raise_if_error(qmk_get_last_error());
   cudaError_t e = cudaStreamSynchronize(stream);
-  TORCH_CHECK(e == cudaSuccess, "qwen_megakernel: cudaStreamSynchronize: ", cudaGetErrorString(e));
+  QMK_CHECK(e == cudaSuccess, "qwen_megakernel: cudaStreamSynchronize: %s", cudaGetErrorString(e));
   QmkStatus st;
   raise_if_error(qmk_read_default_status(&st));
   raise_if_status(st);
   return output_log;
 }
 
-// Extended operator: explicit workspace, forced tokens, logits, status.
+// Extended operator: explicit workspace, forced tokens, logits, status, trace.
 void run(torch::Tensor workspace, torch::Tensor embed_weight, torch::Tensor layer_weights_packed,
          torch::Tensor final_norm_weight, torch::Tensor lm_head_weight, torch::Tensor cos_table,
          torch::Tensor sin_table, torch::Tensor k_cache, torch::Tensor v_cache,
@@ -183,65 +207,72 @@ void run(torch::Tensor workspace, torch::Tensor embed_weight, torch::Tensor laye
          int64_t num_steps, int64_t num_layers, int64_t max_seq_len, double attn_scale,
          std::optional<torch::Tensor> output_log, std::optional<torch::Tensor> output_token,
          std::optional<torch::Tensor> logits, std::optional<torch::Tensor> final_hidden,
-         std::optional<torch::Tensor> status, int64_t timeout_ns, int64_t debug_stall) {
-  TORCH_CHECK(num_steps >= 1, "num_steps must be >= 1");
-  TORCH_CHECK(start_position >= 0, "start_position must be >= 0");
+         std::optional<torch::Tensor> status, int64_t timeout_ns, int64_t debug_stall,
+         std::optional<torch::Tensor> trace, int64_t trace_step, int64_t poll_backoff_ns,
+         int64_t tuning) {
+  QMK_CHECK(num_steps >= 1, "num_steps must be >= 1");
+  QMK_CHECK(start_position >= 0, "start_position must be >= 0");
   check_model(embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight, cos_table,
               sin_table, k_cache, v_cache, num_layers, start_position + num_steps - 1, max_seq_len);
   check_cuda(workspace, "workspace");
   check_same_device(workspace, embed_weight, "workspace");
-  TORCH_CHECK(workspace.nbytes() >= qmk_workspace_bytes(), "workspace holds ", workspace.nbytes(),
-              " bytes; needs ", qmk_workspace_bytes());
+  QMK_CHECK(workspace.nbytes() >= qmk_workspace_bytes(), "workspace holds %lld bytes; needs %lld",
+            (ll)workspace.nbytes(), (ll)qmk_workspace_bytes());
   QmkRunArgs a;
   memset(&a, 0, sizeof(a));
   int n_forced = 0;
   if (forced_tokens.has_value()) {
     const auto &f = *forced_tokens;
-    check_cuda(f, "forced_tokens");
+    check_dtype(f, torch::kInt32, "forced_tokens", "int32");
     check_same_device(f, embed_weight, "forced_tokens");
-    TORCH_CHECK(f.scalar_type() == torch::kInt32, "forced_tokens must be int32");
     n_forced = (int)std::min<int64_t>(f.numel(), num_steps);
     a.forced_tokens = static_cast<const int *>(f.data_ptr());
   } else {
-    TORCH_CHECK(first_token >= 0 && first_token < QMK_VOCAB, "first_token ", first_token,
-                " outside [0, ", QMK_VOCAB, ")");
+    check_token(first_token, "first_token");
   }
   if (output_log.has_value()) {
-    check_cuda(*output_log, "output_log");
+    check_dtype(*output_log, torch::kInt32, "output_log", "int32");
     check_same_device(*output_log, embed_weight, "output_log");
-    TORCH_CHECK(output_log->scalar_type() == torch::kInt32 && output_log->numel() >= num_steps,
-                "output_log must be int32 with >= num_steps elements");
+    QMK_CHECK(output_log->numel() >= num_steps, "output_log must have >= num_steps elements");
     a.output_log = static_cast<int *>(output_log->data_ptr());
   }
   if (output_token.has_value()) {
-    check_cuda(*output_token, "output_token");
+    check_dtype(*output_token, torch::kInt32, "output_token", "int32");
     check_same_device(*output_token, embed_weight, "output_token");
-    TORCH_CHECK(output_token->scalar_type() == torch::kInt32 && output_token->numel() >= 1,
-                "output_token must be int32 with >= 1 element");
+    QMK_CHECK(output_token->numel() >= 1, "output_token must have >= 1 element");
     a.output_token = static_cast<int *>(output_token->data_ptr());
   }
   if (logits.has_value()) {
-    check_cuda(*logits, "logits");
+    check_dtype(*logits, torch::kFloat32, "logits", "float32");
     check_same_device(*logits, embed_weight, "logits");
-    TORCH_CHECK(logits->scalar_type() == torch::kFloat32 && logits->numel() >= num_steps * QMK_VOCAB,
-                "logits must be float32 with >= num_steps * ", QMK_VOCAB, " elements");
+    QMK_CHECK(logits->numel() >= num_steps * QMK_VOCAB, "logits must have >= num_steps * %d elements",
+              QMK_VOCAB);
     a.logits = static_cast<float *>(logits->data_ptr());
   }
   if (final_hidden.has_value()) {
-    check_cuda(*final_hidden, "final_hidden");
+    check_dtype(*final_hidden, torch::kFloat32, "final_hidden", "float32");
     check_same_device(*final_hidden, embed_weight, "final_hidden");
-    TORCH_CHECK(final_hidden->scalar_type() == torch::kFloat32 && final_hidden->numel() >= QMK_HIDDEN,
-                "final_hidden must be float32 with >= ", QMK_HIDDEN, " elements");
+    QMK_CHECK(final_hidden->numel() >= QMK_HIDDEN, "final_hidden must have >= %d elements", QMK_HIDDEN);
     a.final_hidden = static_cast<float *>(final_hidden->data_ptr());
   }
   if (status.has_value()) {
     const auto &s = *status;
-    TORCH_CHECK(!s.is_cuda() && s.is_pinned(), "status must be a pinned CPU tensor");
-    TORCH_CHECK(s.nbytes() >= sizeof(QmkStatus), "status must hold >= ", sizeof(QmkStatus), " bytes");
+    QMK_CHECK(!s.is_cuda() && s.is_pinned(), "status must be a pinned CPU tensor");
+    QMK_CHECK(s.nbytes() >= sizeof(QmkStatus), "status must hold >= %d bytes", (int)sizeof(QmkStatus));
     void *dev = nullptr;
     cudaError_t e = cudaHostGetDevicePointer(&dev, s.data_ptr(), 0);
-    TORCH_CHECK(e == cudaSuccess, "status: cudaHostGetDevicePointer: ", cudaGetErrorString(e));
+    QMK_CHECK(e == cudaSuccess, "status: cudaHostGetDevicePointer: %s", cudaGetErrorString(e));
     a.status = static_cast<QmkStatus *>(dev);
+  }
+  if (trace.has_value()) {
+    check_dtype(*trace, torch::kInt64, "trace", "int64");
+    check_same_device(*trace, embed_weight, "trace");
+    const int n = qmk_num_ctas((int)embed_weight.device().index());
+    QMK_CHECK(n > 0 && trace->numel() >= (int64_t)n * qmk_trace_words(),
+              "trace must have >= num_ctas * qmk_trace_words() = %lld elements",
+              (ll)n * (ll)qmk_trace_words());
+    a.trace = reinterpret_cast<unsigned long long *>(trace->data_ptr());
+    a.trace_step = (int)trace_step;
   }
   a.embed_weight = embed_weight.data_ptr();
   a.layer_weights = reinterpret_cast<const LDGLayerWeights *>(layer_weights_packed.data_ptr());
@@ -262,6 +293,8 @@ void run(torch::Tensor workspace, torch::Tensor embed_weight, torch::Tensor laye
   a.attn_scale = (float)attn_scale;
   a.timeout_ns = (unsigned long long)std::max<int64_t>(timeout_ns, 0);
   a.debug_stall = (int)debug_stall;
+  a.poll_backoff_ns = (unsigned)std::min<int64_t>(std::max<int64_t>(poll_backoff_ns, 0), 4096);
+  a.tuning = (unsigned)tuning;
   c10::cuda::CUDAGuard guard(embed_weight.device());
   raise_if_error(qmk_run(&a, c10::cuda::getCurrentCUDAStream().stream()));
 }
@@ -284,11 +317,13 @@ std::vector<int64_t> default_status() {
 int64_t num_ctas() {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  TORCH_CHECK(e == cudaSuccess, "cudaGetDevice: ", cudaGetErrorString(e));
+  QMK_CHECK(e == cudaSuccess, "cudaGetDevice: %s", cudaGetErrorString(e));
   const int n = qmk_num_ctas(dev);
-  raise_if_error(n < 0 ? qmk_get_last_error() : QMK_OK);
+  if (n < 0) raise_if_error(qmk_get_last_error());
   return n;
 }
+
+int64_t trace_words() { return qmk_trace_words(); }
 
 TORCH_LIBRARY(qwen_megakernel_C, ops) {
   ops.def(
@@ -325,7 +360,8 @@ TORCH_LIBRARY(qwen_megakernel_C, ops) {
       "Tensor k_cache, Tensor v_cache, Tensor? forced_tokens, int first_token, "
       "int start_position, int num_steps, int num_layers, int max_seq_len, float attn_scale, "
       "Tensor? output_log, Tensor? output_token, Tensor? logits, Tensor? final_hidden, "
-      "Tensor? status, int timeout_ns=0, int debug_stall=0) -> ()");
+      "Tensor? status, int timeout_ns=0, int debug_stall=0, Tensor? trace=None, "
+      "int trace_step=0, int poll_backoff_ns=0, int tuning=0) -> ()");
   ops.impl("run", torch::kCUDA, &run);
 
   ops.def("workspace_bytes() -> int", &workspace_bytes);
@@ -333,6 +369,7 @@ TORCH_LIBRARY(qwen_megakernel_C, ops) {
   ops.impl("workspace_init", torch::kCUDA, &workspace_init);
   ops.def("default_status() -> int[]", &default_status);
   ops.def("num_ctas() -> int", &num_ctas);
+  ops.def("trace_words() -> int", &trace_words);
 }
 
 // Importable as a Python module too (mirrors the reference's REGISTER_EXTENSION,

@@ -128,6 +128,8 @@ class Decoder:
             )
         self._attn_scale = 1.0 / math.sqrt(HEAD_DIM)
         self._timeout_ns = int(timeout_ns)
+        self.poll_backoff_ns = 0  # tuning knob of the dataflow polls (ns, 0 = spin)
+        self.tuning = 0  # QmkRunArgs.tuning flags
 
         kv_shape = (self.num_layers, NUM_KV_HEADS, self.max_seq_len, HEAD_DIM)
         self._k_cache = torch.zeros(kv_shape, dtype=torch.bfloat16, device=self.device)
@@ -182,6 +184,10 @@ class Decoder:
         logits: torch.Tensor | None = None,
         final_hidden: torch.Tensor | None = None,
         debug_stall: int = 0,
+        trace: torch.Tensor | None = None,
+        trace_step: int = 0,
+        poll_backoff_ns: int | None = None,
+        tuning: int | None = None,
     ) -> None:
         """Queue one launch of ``num_steps`` decode steps (no host sync).
 
@@ -218,6 +224,10 @@ class Decoder:
             self._status,
             self._timeout_ns,
             int(debug_stall),
+            trace,
+            int(trace_step),
+            int(self.poll_backoff_ns if poll_backoff_ns is None else poll_backoff_ns),
+            int(self.tuning if tuning is None else tuning),
         )
 
     # ------------------------------------------------------- reference API

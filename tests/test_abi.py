@@ -125,6 +125,10 @@ class QmkRunArgs(ctypes.Structure):
         ("status", ctypes.c_void_p),
         ("timeout_ns", ctypes.c_ulonglong),
         ("debug_stall", ctypes.c_int),
+        ("trace", ctypes.c_void_p),
+        ("trace_step", ctypes.c_int),
+        ("poll_backoff_ns", ctypes.c_uint),
+        ("tuning", ctypes.c_uint),
     ]
 
 

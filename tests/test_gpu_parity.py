@@ -72,23 +72,40 @@ def test_single_steps_match_prefill():
     assert torch.equal(a.k_cache, b.k_cache) and torch.equal(a.v_cache, b.v_cache)
 
 
+def _bf16_ulp(x: torch.Tensor) -> torch.Tensor:
+    e = torch.floor(torch.log2(x.abs().clamp_min(1e-30)))
+    return torch.exp2(e - 7)
+
+
 def test_kv_cache_layout_matches_oracle():
+    """The cache holds bf16 K (after QK-norm and RoPE) and V at
+    [layer, kv_head, position, dim]; every element is the oracle's value
+    rounded to bf16, up to one bf16 ulp where the fp32 results of the two
+    summation orders straddle a rounding boundary (plus a 1e-5 absolute floor
+    for values that RoPE brings near zero by cancellation, where fp32
+    rounding differences exceed a bf16 ulp)."""
     from oracle.qwen3_mirror import MirrorDecoder
     from qwen_megakernel_b200 import Decoder
 
     w = small_model(2)
     toks = list(range(500, 530))
+    n = len(toks)
     dec = Decoder(w, max_seq_len=64)
     dec.prefill(toks)
     m = MirrorDecoder(w, 64, device="cuda")
     m.prefill(toks, 0)
     for kc, mk in ((dec.k_cache, m.k_cache), (dec.v_cache, m.v_cache)):
-        a = kc[:, :, : len(toks)].float()
-        b = mk[:, :, : len(toks)].float()
-        # bf16 rounding may flip on the last bit where fp32 sums differ in order
-        assert (a - b).abs().max().item() <= 1e-2 * max(1.0, b.abs().max().item())
-        assert (a != b).float().mean().item() < 1e-3
-        assert kc[:, :, len(toks) :].abs().max().item() == 0.0
+        a = kc[:, :, :n].float()
+        b = mk[:, :, :n].float()
+        # layer 0 sees identical inputs: at most one bf16 ulp apart
+        d0 = (a[0] - b[0]).abs() - (_bf16_ulp(b[0]) * 1.001 + 1e-5)
+        assert d0.max().item() <= 0, f"layer 0 cache entry off by more than 1 bf16 ulp ({d0.max().item()})"
+        # later layers inherit the tiny input differences: still close everywhere,
+        # while a wrong [layer, head, position, dim] layout would be off by O(1)
+        far = (a - b).abs() > 4 * _bf16_ulp(b) + 1e-4
+        assert far.float().mean().item() < 0.01
+        assert (a - b).abs().max().item() < 0.05 * b.abs().max().item()
+        assert kc[:, :, n:].abs().max().item() == 0.0
 
 
 @pytest.fixture(scope="module")
@@ -153,7 +170,7 @@ def test_config1_greedy_generation(decoder28, golden1):
     assert len(out) == len(g["tokens"])
     low = np.nonzero(g["gap"] <= TOL_MAX_ABS)[0]
     t0 = int(low[0]) if len(low) else len(out)
-    assert out[: t0 + 1][:t0] == g["tokens"][:t0].tolist(), f"diverged before step {t0}"
+    assert out[:t0] == g["tokens"][:t0].tolist(), f"diverged before step {t0}"
 
 
 def _reference_scratch():
