@@ -118,6 +118,7 @@ void launch_ldg_generate_nosync(
 #define QMK_ERR_TIMEOUT 4       /* a bounded device-side wait expired        */
 #define QMK_ERR_TOKEN 5         /* token id outside [0, vocab) on device     */
 #define QMK_ERR_WORKSPACE 6     /* workspace too small / misaligned          */
+#define QMK_ERR_SMEM 7          /* shared memory not 1 KB aligned on device  */
 
 /* Host-visible status written by the kernel when it finishes (last CTA).
  * Lives in pinned, device-mapped host memory supplied by the caller. */

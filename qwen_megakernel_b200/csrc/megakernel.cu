@@ -61,6 +61,7 @@ enum Site : unsigned {
   kSiteArg = 9,
   kSiteKVReady = 10,
   kSiteToken = 11,
+  kSiteMma = 12,
 };
 
 struct Params {
@@ -102,7 +103,16 @@ constexpr int kSmA = kSmX + 4 * kHidden;       // post-attention residual, fp32 
 constexpr int kSmAtt = kSmA + 4 * kHidden;     // attention output, fp32 [2048]
 constexpr int kSmU = kSmAtt + 4 * kQSize;      // MLP intermediate / attention scratch, fp32 [3072]
 constexpr int kSmMisc = kSmU + 4 * kInter;
-constexpr int kSmBytes = kSmMisc + 256;
+// misc: full/empty mbarriers (96 B), per-warp argmax (64 B), reductions (128 B),
+// tensor-core completion mbarrier (8 B), TMEM base address (4 B)
+constexpr int kMiscRed = 160;
+constexpr int kMiscMmaBar = 288;   // [kTmemBufs] tensor-core completion (count 1)
+constexpr int kMiscTmemFree = 352; // [kTmemBufs] accumulator read by warps 0-3 (count 4)
+constexpr int kMiscTmem = 416;
+constexpr int kTmemBufs = 8;       // GEMV units (M blocks) in flight
+constexpr int kTmemBufCols = 64;   // D of one unit: 128 lanes x N (<= 48) fp32 columns
+constexpr int kTmemCols = kTmemBufs * kTmemBufCols;
+constexpr int kSmBytes = kSmMisc + 512;
 static_assert(kSmBytes <= 232448, "shared memory plan exceeds the sm_100 per-block limit");
 
 // Attention scratch inside the U region (floats).
@@ -123,11 +133,18 @@ static_assert(kMaxSplits * kMergeWordsPerSplit <= kInter, "merge scratch too lar
 // and after the last layer (slot base num_layers*16): 0 LM input ready,
 // 1 LM done, 3 producer LM first tile, 4 producer LM last tile, 5 step start.
 // Then, per ring tile k of the step (k < kTraceTiles): [kTraceTileBase + 2k]
-// consumer warp 0 starts waiting for it, [+2k+1] it has landed, and
-// [kTraceTileBase + 2*kTraceTiles + k] the producer issued its copy.
+// consumer warp 0 starts waiting for it, [+2k+1] it has landed,
+// [kTraceTileBase + 2*kTraceTiles + k] the producer issued its copy and
+// [kTraceTileBase + 3*kTraceTiles + k] consumer warp 0 released it; for
+// tensor-core tiles [+4*kTraceTiles + k] thread 0 read its accumulator,
+// [+5*kTraceTiles + k] finished its rows, and in SM clock cycles (clock64)
+// [+6*kTraceTiles + k] the issuer of M block 0 started its MMAs,
+// [+7*kTraceTiles + k] it committed them, [+8*kTraceTiles + k] thread 0
+// saw them complete; [+9k] the issuer entered the phase, [+10k] it had
+// passed the TMEM-buffer wait, [+11k] thread 0 entered the phase.
 constexpr int kTraceTiles = 512;
 constexpr int kTraceTileBase = (kMaxLayers + 1) * 16;
-constexpr int kTraceStride = kTraceTileBase + 3 * kTraceTiles;
+constexpr int kTraceStride = kTraceTileBase + 12 * kTraceTiles;
 
 struct Ctx {
   uint8_t *ring;
@@ -147,6 +164,9 @@ struct Ctx {
   uint32_t trace_tile0;       // ring tile index at the start of the traced step
   unsigned poll_backoff_ns;   // sleep between failed dataflow polls (0: spin)
   unsigned tuning;            // QmkRunArgs.tuning
+  uint64_t *mma_bar;          // [kTmemBufs] tensor-core completion (tcgen05.commit)
+  uint64_t *tmem_free;        // [kTmemBufs] accumulator buffer read out
+  uint32_t tmem;              // TMEM base address of the GEMV accumulators
 };
 
 __device__ __forceinline__ unsigned epoch_of(const Ctx &c, int step, int layer, int num_layers) {
@@ -247,19 +267,111 @@ __device__ __forceinline__ bool wait_full(Ctx &c, uint32_t tile) {
 }
 
 __device__ __forceinline__ void release_tile(Ctx &c, uint32_t tile, bool ok) {
+  const uint32_t k = tile - c.trace_tile0;
+  if (c.trace && threadIdx.x == 0 && k < (uint32_t)kTraceTiles)
+    c.trace[kTraceTileBase + 3 * kTraceTiles + k] = global_timer_ns();
   __syncwarp();
   if (ok && (threadIdx.x & 31) == 0) mbar_arrive(&c.empty[tile % kNumSlots]);
+}
+
+// wait_full for one thread (the tensor-core issuer).
+__device__ __forceinline__ bool wait_full_one(Ctx &c, uint32_t tile) {
+  if (*c.abort_flag) return false;
+  const uint32_t k = tile - c.trace_tile0;
+  const bool stamp = c.trace && k < (uint32_t)kTraceTiles;
+  if (stamp) c.trace[kTraceTileBase + 2 * k] = global_timer_ns();
+  const int slot = tile % kNumSlots;
+  const unsigned par = (tile / kNumSlots) & 1u;
+  Waiter w;
+  while (!mbar_try_wait(&c.full[slot], par)) {
+    if (!w.keep_going(c, kSiteFull)) return false;
+  }
+  if (stamp) c.trace[kTraceTileBase + 2 * k + 1] = global_timer_ns();
+  return true;
 }
 
 __device__ __forceinline__ const uint8_t *slot_ptr(const Ctx &c, uint32_t tile) {
   return c.ring + (tile % kNumSlots) * kSlotBytes;
 }
 
+// ------------------------------------------------------------- GEMV (tcgen05)
+// y = W x for the rows of one 32 KB ring tile runs on the 5th-generation
+// tensor cores: tcgen05.mma (M = 128, N = 16S, K = 16, bf16 in, fp32
+// accumulate in TMEM) with the tile's weights as the A operand exactly as
+// the 1-D bulk copies deliver them and the activation vector as the B
+// operand, both read through the 128-byte-swizzle descriptor:
+//
+//  * the tile is 16 "segments" of 2 KB (1024 weights): a row for K = 1024,
+//    half a row for K = 2048, and for K = 3072 (rows at an 8 KB pitch) a
+//    third of a row or an unused quarter.  Segment j, half h' (0/1) is the
+//    1 KB swizzle atom at byte 2048j + 1024h': 8 lines of 128 bytes, line q
+//    holding weights 512h' + 64q + (0..63) of the segment;
+//  * M block h' of the tile = atoms (j, h') for j = 0..15 (SBO 2048 bytes):
+//    MMA row 8j + q is line q of segment j, and 4 instructions walk K = 64;
+//  * the descriptor's swizzle reads logical 16-byte chunk c of line q from
+//    chunk c ^ q.  B line (s, g, q) holds part g (0 = hi, 1 = lo) of the 64
+//    activations that line q of a segment in slot s multiplies, in plain
+//    order, so its chunks are permuted the same way and
+//    D[8j + q][16s + 8g + q] (s = slot of segment j) is the line's partial
+//    dot product (the "diagonal" entries; the others are unused).  Slots:
+//    one for K = 1024, the half for K = 2048, the third for K = 3072, so
+//    N = 16, 32, 48;
+//  * the fp32 activation x is split as x = hi + lo (two bf16 parts, the
+//    second holding the rounding remainder of the first): products are exact
+//    and the representation error of x is ~2^-17 relative.
+// Both M blocks map TMEM lane 8j + q to segment j, so a row's dot product is
+// the sum of the two blocks' diagonal entries over 8 lanes (one segment),
+// 16 lanes (K = 2048) or a whole warp (K = 3072), added with shuffles.
+//
+// B operand ("bop") for K = 1024S: the lines of block h' are contiguous
+// (1 KB groups of 8 lines, group 2S*h' + 2s + g), so element e (slice
+// h = e >> 9 = 2s + h', line q = (e >> 6) & 7) has its hi part at
+// bop_offset<S>(e) and its lo part 1024 bytes further; 4S KB in all.
+enum TcKind : int { kTcRow = 0, kTcGU = 1, kTcHalf = 2, kTcQuarter = 3 };
+
+template <int S>
+__device__ __forceinline__ int bop_offset(int e) {
+  const int h = e >> 9;
+  return 1024 * (2 * S * (h & 1) + 2 * (h >> 1)) + 128 * ((e >> 6) & 7) + 2 * (e & 63);
+}
+
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
+
+// Split (v0, v1) into bf16 pairs hi and lo with v ~= hi + lo.
+__device__ __forceinline__ void split_pair(float v0, float v1, uint32_t &hi, uint32_t &lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+  const float2 hf = __bfloat1622float2(h);
+  hi = bf2_bits(h);
+  lo = bf2_bits(__floats2bfloat162_rn(v0 - hf.x, v1 - hf.y));
+}
+
+// Elements e, e+1 (e even) of the activation vector (K = 1024S) into the B
+// operand.
+template <int S>
+__device__ __forceinline__ void store_bop_pair(uint8_t *bop, int e, float v0, float v1) {
+  uint32_t hi, lo;
+  split_pair(v0, v1, hi, lo);
+  uint8_t *q = bop + bop_offset<S>(e);
+  *reinterpret_cast<uint32_t *>(q) = hi;
+  *reinterpret_cast<uint32_t *>(q + 1024) = lo;
+}
+
 // ------------------------------------------------------------- LL staging
-// All consumer threads: poll the N words of `src` (flag == expected) into
-// fp32 `dst`, two words per 16-byte load, then consumer_sync().
-template <int N>
-__device__ void stage_vec(Ctx &c, float *dst, const uint64_t *src, unsigned flag, unsigned site) {
+enum StageMode : int {
+  kStageF32 = 0,    // fp32 copy into dst
+  kStageSumSq = 1,  // fp32 copy into dst, returns sum of squares of the vector
+  kStageFrag = 2,   // B fragments (tensor-core GEMV operand) into frag
+};
+
+// All consumer threads: poll the N words of `src` until their flag equals
+// `flag` (two words per 16-byte load) and store them per MODE, then
+// consumer_sync().  kStageSumSq folds a block reduction into that barrier,
+// using red[kConsumerWarps] (one array per call site); the sum is taken in a
+// fixed order whatever the order in which the words arrive.  kStageFrag
+// writes the tensor-core B operand (K = N) and fences it for the async proxy.
+template <int N, int MODE>
+__device__ float stage_vec(Ctx &c, float *dst, uint8_t *bop, const uint64_t *src, unsigned flag, unsigned site,
+                           float *red) {
   constexpr int kPairs = N / 2;
   constexpr int P = (kPairs + kConsumerThreads - 1) / kConsumerThreads;
   static_assert(N % 2 == 0 && P <= 32, "stage_vec size");
@@ -269,6 +381,9 @@ __device__ void stage_vec(Ctx &c, float *dst, const uint64_t *src, unsigned flag
   for (int k = 0; k < P; ++k)
     if (k * kConsumerThreads + tid < kPairs) pending |= 1u << k;
   if (*c.abort_flag) pending = 0;
+  float keep[MODE == kStageSumSq ? P : 1][2];
+#pragma unroll
+  for (int k = 0; k < (MODE == kStageSumSq ? P : 1); ++k) keep[k][0] = keep[k][1] = 0.f;
   Waiter w;
   while (pending) {
     uint64_t a[P], b[P];
@@ -281,8 +396,17 @@ __device__ void stage_vec(Ctx &c, float *dst, const uint64_t *src, unsigned flag
 #pragma unroll
     for (int k = 0; k < P; ++k) {
       if ((pending & (1u << k)) && ll_flag(a[k]) == flag && ll_flag(b[k]) == flag) {
-        reinterpret_cast<float2 *>(dst)[k * kConsumerThreads + tid] =
-            make_float2(ll_value(a[k]), ll_value(b[k]));
+        const int q = k * kConsumerThreads + tid;
+        const float v0 = ll_value(a[k]), v1 = ll_value(b[k]);
+        if (MODE == kStageFrag) {
+          store_bop_pair<N / 1024>(bop, 2 * q, v0, v1);
+        } else {
+          reinterpret_cast<float2 *>(dst)[q] = make_float2(v0, v1);
+          if (MODE == kStageSumSq) {
+            keep[MODE == kStageSumSq ? k : 0][0] = v0;
+            keep[MODE == kStageSumSq ? k : 0][1] = v1;
+          }
+        }
         pending &= ~(1u << k);
       }
     }
@@ -291,7 +415,54 @@ __device__ void stage_vec(Ctx &c, float *dst, const uint64_t *src, unsigned flag
       if (c.poll_backoff_ns) __nanosleep(c.poll_backoff_ns);
     }
   }
+  if (MODE == kStageFrag) fence_proxy_async_smem();
+  if (MODE == kStageSumSq) {
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < (MODE == kStageSumSq ? P : 1); ++k)
+      ss = fmaf(keep[k][0], keep[k][0], fmaf(keep[k][1], keep[k][1], ss));
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+  }
   consumer_sync();
+  float total = 0.f;
+  if (MODE == kStageSumSq) {
+#pragma unroll
+    for (int q = 0; q < kConsumerWarps; ++q) total += red[q];
+  }
+  return total;
+}
+
+// Norm weights (bf16 pairs) of the elements thread `tid` writes in
+// build_norm_bop<K>, fetched before the dataflow wait.
+template <int K>
+struct NormPrefetch {
+  static constexpr int kPer = (K / 2 + kConsumerThreads - 1) / kConsumerThreads;
+  uint32_t w[kPer];
+  __device__ __forceinline__ void load(const __nv_bfloat16 *nw, int tid) {
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int q = tid + j * kConsumerThreads;
+      w[j] = (q < K / 2) ? __ldg(reinterpret_cast<const unsigned *>(nw) + q) : 0u;
+    }
+  }
+};
+
+// B operand <- RMSNorm(x) * w, i.e. x * rstd * w (fp32, the order of the
+// reference and of HF's Qwen3RMSNorm), fenced for the tensor cores; the
+// caller's next consumer_sync publishes it.
+template <int K>
+__device__ __forceinline__ void build_norm_bop(uint8_t *bop, const float *x, float rstd, const NormPrefetch<K> &nw,
+                                               int tid) {
+#pragma unroll
+  for (int j = 0; j < NormPrefetch<K>::kPer; ++j) {
+    const int q = tid + j * kConsumerThreads;
+    if (q < K / 2) {
+      const float2 v = reinterpret_cast<const float2 *>(x)[q];
+      store_bop_pair<K / 1024>(bop, 2 * q, (v.x * rstd) * bf_lo(nw.w[j]), (v.y * rstd) * bf_hi(nw.w[j]));
+    }
+  }
+  fence_proxy_async_smem();
 }
 
 // Poll up to K words per thread at arbitrary addresses: word i (i < n) of the
@@ -326,99 +497,6 @@ __device__ void stage_list(Ctx &c, float *dst, int n, AddrFn addr, unsigned flag
     }
   }
   consumer_sync();
-}
-
-// ------------------------------------------------------------- GEMV pieces
-// Lane l owns columns {256*j + 8*l + e : j < J, e < 8} of a K = 256*J vector.
-template <int J>
-__device__ __forceinline__ void load_act(float (&act)[J * 8], const float *s, int lane) {
-#pragma unroll
-  for (int j = 0; j < J; ++j) {
-    const float4 *p = reinterpret_cast<const float4 *>(s + 256 * j + 8 * lane);
-    const float4 x = p[0], y = p[1];
-    act[j * 8 + 0] = x.x;
-    act[j * 8 + 1] = x.y;
-    act[j * 8 + 2] = x.z;
-    act[j * 8 + 3] = x.w;
-    act[j * 8 + 4] = y.x;
-    act[j * 8 + 5] = y.y;
-    act[j * 8 + 6] = y.z;
-    act[j * 8 + 7] = y.w;
-  }
-}
-
-// Norm weights of lane l's columns (see load_act<4>), fetched before the
-// dataflow wait so their L2 latency overlaps it.
-__device__ __forceinline__ void load_norm_w(uint4 (&wv)[4], const __nv_bfloat16 *w, int lane) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) wv[j] = __ldg(reinterpret_cast<const uint4 *>(w + 256 * j + 8 * lane));
-}
-
-// act <- RMSNorm(s) * w (fp32, eps 1e-6), for a 1024-vector.  Each warp holds
-// the whole vector across its lanes, so no cross-warp reduction is needed.
-__device__ __forceinline__ void rmsnorm_act(float (&act)[32], const float *s, const uint4 (&wv)[4],
-                                            int lane) {
-  load_act<4>(act, s, lane);
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) ss = fmaf(act[i], act[i], ss);
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)kHidden + kRmsEps);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const unsigned ww[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      act[j * 8 + 2 * e] = (act[j * 8 + 2 * e] * r) * bf_lo(ww[e]);
-      act[j * 8 + 2 * e + 1] = (act[j * 8 + 2 * e + 1] * r) * bf_hi(ww[e]);
-    }
-  }
-}
-
-// Lane-partial dot product of one bf16 row (K = 256*J, in shared memory).
-template <int J>
-__device__ __forceinline__ float dot_row(const uint8_t *row, const float (&act)[J * 8], int lane) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-  for (int j = 0; j < J; ++j) {
-    const uint4 w = *reinterpret_cast<const uint4 *>(row + 512 * j + 16 * lane);
-    s0 = fmaf(bf_lo(w.x), act[j * 8 + 0], s0);
-    s1 = fmaf(bf_hi(w.x), act[j * 8 + 1], s1);
-    s2 = fmaf(bf_lo(w.y), act[j * 8 + 2], s2);
-    s3 = fmaf(bf_hi(w.y), act[j * 8 + 3], s3);
-    s0 = fmaf(bf_lo(w.z), act[j * 8 + 4], s0);
-    s1 = fmaf(bf_hi(w.z), act[j * 8 + 5], s1);
-    s2 = fmaf(bf_lo(w.w), act[j * 8 + 6], s2);
-    s3 = fmaf(bf_hi(w.w), act[j * 8 + 7], s3);
-  }
-  return (s0 + s1) + (s2 + s3);
-}
-
-// Process rows [0, n) of one ring tile holding rows of K = 256*J; warp w takes
-// rows w, w+W, ... (W consumer warps) and keeps R of them in flight so their
-// load -> FMA -> shuffle-reduction chains overlap.  `emit(local_row, value)`
-// is called by every lane.
-template <int J, int R, typename Emit>
-__device__ __forceinline__ void gemv_tile(const uint8_t *base, int n, const float (&act)[J * 8],
-                                          int warp, int lane, Emit emit) {
-  for (int r0 = warp; r0 < n; r0 += R * kConsumerWarps) {
-    float acc[R];
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-      const int r = r0 + i * kConsumerWarps;
-      acc[i] = (r < n) ? dot_row<J>(base + (size_t)r * (512 * J), act, lane) : 0.f;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-      for (int i = 0; i < R; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
-    }
-#pragma unroll
-    for (int i = 0; i < R; ++i) {
-      const int r = r0 + i * kConsumerWarps;
-      if (r < n) emit(r, acc[i]);
-    }
-  }
 }
 
 // ------------------------------------------------------------- argmax
@@ -512,13 +590,20 @@ struct Producer {
   }
   __device__ __forceinline__ uint64_t *bar() { return &c.full[tile % kNumSlots]; }
 
-  __device__ void rows(const __nv_bfloat16 *mat, int row_bytes, Range r, int tile_rows) {
+  // Rows of `mat` in tiles of tile_rows; row k of a tile lands at
+  // k * dst_pitch (one copy when the rows are contiguous in the tile).
+  __device__ void rows(const __nv_bfloat16 *mat, int row_bytes, Range r, int tile_rows, int dst_pitch) {
     for (int r0 = r.begin; r0 < r.end && alive; r0 += tile_rows) {
       const int n = min(tile_rows, r.end - r0);
       uint8_t *dst = begin((unsigned)(n * row_bytes));
       if (!dst) return;
-      bulk_g2s(dst, reinterpret_cast<const uint8_t *>(mat) + (size_t)r0 * row_bytes,
-               (unsigned)(n * row_bytes), bar(), pol);
+      const uint8_t *src = reinterpret_cast<const uint8_t *>(mat) + (size_t)r0 * row_bytes;
+      if (dst_pitch == row_bytes) {
+        bulk_g2s(dst, src, (unsigned)(n * row_bytes), bar(), pol);
+      } else {
+        for (int k = 0; k < n; ++k)
+          bulk_g2s(dst + (size_t)k * dst_pitch, src + (size_t)k * row_bytes, (unsigned)row_bytes, bar(), pol);
+      }
       ++tile;
     }
   }
@@ -561,11 +646,14 @@ struct Producer {
       const int n = min(kGUTileRows, r.end - r0);
       uint8_t *dst = begin((unsigned)(2 * n * 2048));
       if (!dst) return;
-      bulk_g2s(dst, reinterpret_cast<const uint8_t *>(w.gate_proj_weight) + (size_t)r0 * 2048,
-               (unsigned)(n * 2048), bar(), pol);
-      bulk_g2s(dst + kGUTileRows * 2048,
-               reinterpret_cast<const uint8_t *>(w.up_proj_weight) + (size_t)r0 * 2048,
-               (unsigned)(n * 2048), bar(), pol);
+      // gate row k at 4096k, up row k at 4096k + 2048: one tensor-core
+      // segment pair per output row.
+      const uint8_t *g = reinterpret_cast<const uint8_t *>(w.gate_proj_weight) + (size_t)r0 * 2048;
+      const uint8_t *u = reinterpret_cast<const uint8_t *>(w.up_proj_weight) + (size_t)r0 * 2048;
+      for (int k = 0; k < n; ++k) {
+        bulk_g2s(dst + (size_t)k * 4096, g + (size_t)k * 2048, 2048u, bar(), pol);
+        bulk_g2s(dst + (size_t)k * 4096 + 2048, u + (size_t)k * 2048, 2048u, bar(), pol);
+      }
       ++tile;
     }
   }
@@ -613,13 +701,14 @@ struct Producer {
         trace_stamp(c, true, l * 16 + 12);
         qkv(w, qkv_rows(c.cta, c.ncta));
         if (item >= 0) kv(t, l, item / p.splits, kv_chunk(pos, item % p.splits, p.splits));
-        rows((const __nv_bfloat16 *)w.o_proj_weight, kQSize * 2, o_rows(c.cta, c.ncta), kOTileRows);
+        rows((const __nv_bfloat16 *)w.o_proj_weight, kQSize * 2, o_rows(c.cta, c.ncta), kOTileRows, kQSize * 2);
         gate_up(w, gu_rows(c.cta, c.ncta));
-        rows((const __nv_bfloat16 *)w.down_proj_weight, kInter * 2, d_rows(c.cta, c.ncta), kDTileRows);
+        rows((const __nv_bfloat16 *)w.down_proj_weight, kInter * 2, d_rows(c.cta, c.ncta), kDTileRows,
+             kDRowPitch);
         trace_stamp(c, true, l * 16 + 13);
       }
       trace_stamp(c, true, p.num_layers * 16 + 3);
-      rows(p.lm_head, kHidden * 2, lm_rows(c.cta, c.ncta), kLMTileRows);
+      rows(p.lm_head, kHidden * 2, lm_rows(c.cta, c.ncta), kLMTileRows, kHidden * 2);
       trace_stamp(c, true, p.num_layers * 16 + 4);
     }
     // Drain: the last tile issued into each slot must land before the CTA exits.
@@ -645,20 +734,197 @@ struct Consumer {
   const Params &p;
   uint8_t *smem;
   float *sX, *sA, *sAtt, *sU;
+  float *red_x, *red_a, *red_lm, *red_e;  // block-reduction slots, one per call site
   uint32_t tile = 0;
+  unsigned mma_seq = 0;      // tensor-core units consumed (buffer = seq % kTmemBufs)
+  unsigned mma_issued = 0;   // issuer threads: 1 + the last unit this thread issued
   int warp, lane, tid;
+  uint64_t kv_written = 0;  // layers whose new K/V row this CTA wrote this step
 
   __device__ Consumer(Ctx &c_, const Params &p_, uint8_t *smem_) : c(c_), p(p_), smem(smem_) {
     sX = reinterpret_cast<float *>(smem + kSmX);
     sA = reinterpret_cast<float *>(smem + kSmA);
     sAtt = reinterpret_cast<float *>(smem + kSmAtt);
     sU = reinterpret_cast<float *>(smem + kSmU);
+    float *red = reinterpret_cast<float *>(smem + kSmMisc + kMiscRed);
+    red_x = red;
+    red_a = red + 8;
+    red_lm = red + 16;
+    red_e = red + 24;
     tid = threadIdx.x;
     warp = tid >> 5;
     lane = tid & 31;
   }
 
   __device__ __forceinline__ bool live() const { return *c.abort_flag == 0; }
+
+  // Slots (N / 16) of a GEMV kind.
+  template <int KIND>
+  __host__ __device__ static constexpr int tc_slots() {
+    return (KIND == kTcHalf) ? 2 : (KIND == kTcQuarter) ? 3 : 1;
+  }
+
+  // Issue the 4 MMAs of M block hp of ring tile `tl` (tensor-core unit
+  // number seq) into TMEM buffer seq % kTmemBufs, against the B operand at
+  // bop.  Layout of A, B and D: see the GEMV section above.
+  template <int KIND>
+  __device__ bool tc_issue_unit(uint32_t tl, int hp, unsigned seq, const uint8_t *bop) {
+    constexpr int S = tc_slots<KIND>();
+    constexpr uint32_t kIdesc = mma_idesc_bf16(128, 16 * S);
+    const unsigned b = seq % kTmemBufs;
+    const uint32_t tk0 = tl - c.trace_tile0;
+    if (c.trace && hp == 0 && tk0 < (uint32_t)kTraceTiles) c.trace[kTraceTileBase + 9 * kTraceTiles + tk0] = clock64();
+    if (seq >= (unsigned)kTmemBufs) {
+      // the unit that used this buffer before must have been read out
+      const unsigned par = ((seq / kTmemBufs) - 1u) & 1u;
+      Waiter w;
+      while (!mbar_try_wait(&c.tmem_free[b], par))
+        if (!w.keep_going(c, kSiteMma)) return false;
+    }
+    if (c.trace && hp == 0 && tk0 < (uint32_t)kTraceTiles) c.trace[kTraceTileBase + 10 * kTraceTiles + tk0] = clock64();
+    if (!wait_full_one(c, tl)) return false;
+    tc_fence_after_sync();
+    const uint32_t tk = tl - c.trace_tile0;
+    const bool tstamp = c.trace && hp == 0 && tk < (uint32_t)kTraceTiles;
+    if (tstamp) c.trace[kTraceTileBase + 6 * kTraceTiles + tk] = clock64();
+    const uint32_t a0 = smem_addr(slot_ptr(c, tl)) + 1024u * (uint32_t)hp;
+    const uint32_t b0 = smem_addr(bop) + 2048u * S * (uint32_t)hp;
+    const uint32_t d = c.tmem + (uint32_t)kTmemBufCols * b;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+      tc_mma_bf16(d, smem_desc_sw128(a0 + 32u * kk, 2048u), smem_desc_sw128(b0 + 32u * kk, 1024u), kIdesc, kk > 0);
+    tc_commit(&c.mma_bar[b]);
+    if (tstamp) c.trace[kTraceTileBase + 7 * kTraceTiles + tk] = clock64();
+    mma_issued = seq + 1u;
+    return true;
+  }
+
+  // Reader side: wait (bounded) for tensor-core unit seq.
+  __device__ bool wait_unit(unsigned seq) {
+    const unsigned par = (seq / kTmemBufs) & 1u;
+    Waiter w;
+    while (!mbar_try_wait(&c.mma_bar[seq % kTmemBufs], par))
+      if (!w.keep_going(c, kSiteMma)) return false;
+    return true;
+  }
+
+  // GEMV phase over `ntiles` consecutive ring tiles on the tensor cores.
+  // A unit is one M block (4 MMAs); lane 0 of warps 4-6 issue the units
+  // round-robin (a single issuing thread is limited by the issue latency of
+  // tcgen05.mma), up to kTmemBufs units in flight; warps 0-3 read both units
+  // of a tile (one TMEM lane each), add the diagonal entries of every output
+  // row with warp shuffles and call emit(tile, row, value, value2) from one
+  // lane per row.
+  //   kTcRow     K = 1024, 16 rows
+  //   kTcGU      K = 1024, tile rows 2k (gate) and 2k+1 (up) of output row
+  //              k (8 rows); emit gets (gate, up)
+  //   kTcHalf    K = 2048, 8 rows
+  //   kTcQuarter K = 3072, 4 rows at an 8 KB pitch
+  template <int KIND, typename Emit>
+  __device__ void tc_phase(int ntiles, const uint8_t *bop, Emit emit) {
+    constexpr int S = tc_slots<KIND>();
+    constexpr int kIssuers = kConsumerWarps - 4;
+    const unsigned seq0 = mma_seq;
+    const int nunits = 2 * ntiles;
+    if (tid == 0 && c.trace && tile - c.trace_tile0 < (uint32_t)kTraceTiles)
+      c.trace[kTraceTileBase + 11 * kTraceTiles + (tile - c.trace_tile0)] = clock64();
+    if (warp >= 4 && lane == 0) {
+      bool ok = live();
+      for (int u = warp - 4; u < nunits && ok; u += kIssuers)
+        ok = tc_issue_unit<KIND>(tile + (uint32_t)(u >> 1), u & 1, seq0 + (unsigned)u, bop);
+    }
+    if (warp < 4) {
+      const int q = lane & 7;
+      const int j = (32 * warp + lane) >> 3;  // segment of this lane
+      const int slot = (KIND == kTcHalf) ? (j & 1) : (KIND == kTcQuarter) ? (j & 3) : 0;
+      const bool valid = slot < S;            // K = 3072: quarter 3 of a row is unused
+      for (int t = 0; t < ntiles; ++t) {
+        const unsigned seq = seq0 + 2u * (unsigned)t;
+        bool got = live() && wait_unit(seq) && wait_unit(seq + 1u);
+        got = __all_sync(0xffffffffu, got);
+        const uint32_t tk = tile + (uint32_t)t - c.trace_tile0;
+        const bool tstamp = c.trace && tid == 0 && tk < (uint32_t)kTraceTiles;
+        if (tstamp) c.trace[kTraceTileBase + 8 * kTraceTiles + tk] = clock64();
+        if (got && tid == 0) {
+          // both units' MMAs have read the tile: hand the ring slot back
+          if (tstamp) c.trace[kTraceTileBase + 3 * kTraceTiles + tk] = global_timer_ns();
+          mbar_arrive_cnt(&c.empty[(tile + (uint32_t)t) % kNumSlots], kConsumerWarps);
+        }
+        __syncwarp();
+        float v = 0.f;
+        if (got) {
+          tc_fence_after_sync();
+#pragma unroll
+          for (int hp = 0; hp < 2; ++hp) {
+            const uint32_t taddr =
+                c.tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)kTmemBufCols * ((seq + (unsigned)hp) % kTmemBufs);
+            if (S == 1) {
+              uint32_t r[16];
+              tmem_ld16(taddr, r);
+#pragma unroll
+              for (int col = 0; col < 8; ++col)
+                if (col == q) v += __uint_as_float(r[col]) + __uint_as_float(r[8 + col]);
+            } else {
+              uint32_t r[32];
+              tmem_ld32(taddr, r);
+#pragma unroll
+              for (int ss = 0; ss < 2; ++ss)
+#pragma unroll
+                for (int col = 0; col < 8; ++col)
+                  if (ss == slot && col == q) v += __uint_as_float(r[16 * ss + col]) + __uint_as_float(r[16 * ss + 8 + col]);
+              if (S == 3) {
+                uint32_t r2[16];
+                tmem_ld16(taddr + 32u, r2);
+#pragma unroll
+                for (int col = 0; col < 8; ++col)
+                  if (slot == 2 && col == q) v += __uint_as_float(r2[col]) + __uint_as_float(r2[8 + col]);
+              }
+            }
+          }
+          if (!valid) v = 0.f;
+        }
+        tc_fence_before_sync();
+        if (tstamp) c.trace[kTraceTileBase + 4 * kTraceTiles + tk] = global_timer_ns();
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        if (KIND == kTcRow) {
+          if (got && q == 0) emit(t, j, v, 0.f);
+        } else if (KIND == kTcGU) {
+          const float up = __shfl_down_sync(0xffffffffu, v, 8);
+          if (got && (lane & 15) == 0) emit(t, j >> 1, v, up);
+        } else if (KIND == kTcHalf) {
+          v += __shfl_xor_sync(0xffffffffu, v, 8);
+          if (got && (lane & 15) == 0) emit(t, j >> 1, v, 0.f);
+        } else {
+          v += __shfl_xor_sync(0xffffffffu, v, 8);
+          v += __shfl_xor_sync(0xffffffffu, v, 16);
+          if (got && lane == 0) emit(t, warp, v, 0.f);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&c.tmem_free[seq % kTmemBufs]);
+          mbar_arrive(&c.tmem_free[(seq + 1u) % kTmemBufs]);
+        }
+        if (tstamp) c.trace[kTraceTileBase + 5 * kTraceTiles + tk] = global_timer_ns();
+      }
+    }
+    tile += (uint32_t)ntiles;
+    mma_seq += (unsigned)nunits;
+  }
+
+  // Issuer threads: wait (bounded) for the last MMAs they issued, so that
+  // TMEM can be freed (normally they were consumed already).
+  __device__ void drain_mma() {
+    if (mma_issued > 0u) {
+      const unsigned seq = mma_issued - 1u;
+      const unsigned par = (seq / kTmemBufs) & 1u;
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(&c.mma_bar[seq % kTmemBufs], par)) {
+        if (global_timer_ns() - t0 > c.timeout_ns) break;
+      }
+    }
+  }
 
   // Store of one dataflow word.  Default: an L2 atomic max (red.max.u64) --
   // plain stores could sit in the SM's write path for microseconds before
@@ -679,28 +945,22 @@ struct Consumer {
 
   // P1: RMSNorm(x) then q|k|v rows of this CTA.
   // x_flag: epoch of the X words to stage, or 0 when sX already holds the
-  // layer input (the embedding row of layer 0).
-  __device__ void phase_qkv(const LDGLayerWeights &w, unsigned E, int l, unsigned x_flag) {
-    uint4 wn[4];
-    load_norm_w(wn, (const __nv_bfloat16 *)w.input_layernorm_weight, lane);
-    if (x_flag) stage_vec<kHidden>(c, sX, c.wX, x_flag, kSiteX);
+  // layer input (the embedding row of layer 0) and x_ss its sum of squares.
+  __device__ void phase_qkv(const LDGLayerWeights &w, unsigned E, int l, unsigned x_flag, float x_ss) {
+    NormPrefetch<kHidden> nw;
+    nw.load((const __nv_bfloat16 *)w.input_layernorm_weight, tid);
+    if (x_flag) x_ss = stage_vec<kHidden, kStageSumSq>(c, sX, nullptr, c.wX, x_flag, kSiteX, red_x);
     trace_stamp(c, tid == 0, l * 16 + 0);
-    float act[32];
-    rmsnorm_act(act, sX, wn, lane);
+    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
+    build_norm_bop<kHidden>(bop, sX, rsqrtf(x_ss / (float)kHidden + kRmsEps), nw, tid);
+    consumer_sync();
     const Range R = qkv_rows(c.cta, c.ncta);
-    for (int r0 = R.begin; r0 < R.end; r0 += kQKVTileRows) {
-      const int n = min(kQKVTileRows, R.end - r0);
-      const bool ok = wait_full(c, tile);
-      if (ok) {
-        uint64_t *out = c.wQKV + r0;
-        gemv_tile<4, 4>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
-          if (lane == 0) put(out + r, ll_pack(v, E));
-        });
-      }
-      release_tile(c, tile, ok);
-      ++tile;
-    }
+    tc_phase<kTcRow>((R.end - R.begin + kQKVTileRows - 1) / kQKVTileRows, bop, [&](int t, int r, float v, float) {
+      const int row = R.begin + t * kQKVTileRows + r;
+      if (row < R.end) put(c.wQKV + row, ll_pack(v, E));
+    });
     flush();
+    consumer_sync();  // the fragments in sU are overwritten by the next phase
     trace_stamp(c, tid == 0, l * 16 + 1);
   }
 
@@ -787,10 +1047,9 @@ struct Consumer {
       }
     }
     consumer_sync();
-    if (last && tid == 0 && live()) {
-      __threadfence();
-      st_release_u32(&c.ctrl->kv_ready[layer * kNumKVHeads + g], E);
-    }
+    // The new K/V row is published (kv_ready) at the start of the LM-head
+    // phase, off the critical path: only the next step's producers read it.
+    if (last) kv_written |= 1ull << layer;
 
     float q0[4], q1[4];
 #pragma unroll
@@ -949,130 +1208,104 @@ struct Consumer {
 
   // P3: O-projection rows + residual -> A words.
   __device__ void phase_o(const LDGLayerWeights &w, unsigned E, bool stall, int l) {
+    uint8_t *bop = reinterpret_cast<uint8_t *>(sAtt);
     // Test hook: 0xFFFFFFFF is never an epoch, so this wait can only expire.
-    stage_vec<kQSize>(c, sAtt, c.wAtt, stall ? 0xFFFFFFFFu : E, kSiteAtt);
+    stage_vec<kQSize, kStageFrag>(c, nullptr, bop, c.wAtt, stall ? 0xFFFFFFFFu : E, kSiteAtt, nullptr);
     trace_stamp(c, tid == 0, l * 16 + 6);
-    float act[64];
-    load_act<8>(act, sAtt, lane);
     const Range R = o_rows(c.cta, c.ncta);
-    for (int r0 = R.begin; r0 < R.end; r0 += kOTileRows) {
-      const int n = min(kOTileRows, R.end - r0);
-      const bool ok = wait_full(c, tile);
-      if (ok) {
-        gemv_tile<8, 2>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
-          if (lane == 0) put(c.wA + r0 + r, ll_pack(v + sX[r0 + r], E));
-        });
-      }
-      release_tile(c, tile, ok);
-      ++tile;
-    }
+    tc_phase<kTcHalf>((R.end - R.begin + kOTileRows - 1) / kOTileRows, bop, [&](int t, int r, float v, float) {
+      const int row = R.begin + t * kOTileRows + r;
+      if (row < R.end) put(c.wA + row, ll_pack(v + sX[row], E));
+    });
     flush();
     trace_stamp(c, tid == 0, l * 16 + 7);
   }
 
   // P4: RMSNorm(a) then gate/up rows, SiLU(gate) * up -> M words.
   __device__ void phase_gate_up(const LDGLayerWeights &w, unsigned E, int l) {
-    uint4 wn[4];
-    load_norm_w(wn, (const __nv_bfloat16 *)w.post_attn_layernorm_weight, lane);
-    stage_vec<kHidden>(c, sA, c.wA, E, kSiteA);
+    NormPrefetch<kHidden> nw;
+    nw.load((const __nv_bfloat16 *)w.post_attn_layernorm_weight, tid);
+    const float ss = stage_vec<kHidden, kStageSumSq>(c, sA, nullptr, c.wA, E, kSiteA, red_a);
     trace_stamp(c, tid == 0, l * 16 + 8);
-    float act[32];
-    rmsnorm_act(act, sA, wn, lane);
+    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
+    build_norm_bop<kHidden>(bop, sA, rsqrtf(ss / (float)kHidden + kRmsEps), nw, tid);
+    consumer_sync();
     const Range R = gu_rows(c.cta, c.ncta);
-    for (int r0 = R.begin; r0 < R.end; r0 += kGUTileRows) {
-      const int n = min(kGUTileRows, R.end - r0);
-      const bool ok = wait_full(c, tile);
-      if (ok) {
-        const uint8_t *gt = slot_ptr(c, tile);
-        const uint8_t *ut = gt + kGUTileRows * 2048;
-        // Two (gate, up) row pairs in flight per warp.
-        for (int ra = warp; ra < n; ra += 2 * kConsumerWarps) {
-          const int rb = ra + kConsumerWarps;
-          const bool has_b = rb < n;
-          float gs0 = dot_row<4>(gt + (size_t)ra * 2048, act, lane);
-          float us0 = dot_row<4>(ut + (size_t)ra * 2048, act, lane);
-          float gs1 = has_b ? dot_row<4>(gt + (size_t)rb * 2048, act, lane) : 0.f;
-          float us1 = has_b ? dot_row<4>(ut + (size_t)rb * 2048, act, lane) : 0.f;
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            gs0 += __shfl_xor_sync(0xffffffffu, gs0, o);
-            us0 += __shfl_xor_sync(0xffffffffu, us0, o);
-            gs1 += __shfl_xor_sync(0xffffffffu, gs1, o);
-            us1 += __shfl_xor_sync(0xffffffffu, us1, o);
-          }
-          if (lane == 0) {
-            const float silu0 = gs0 * fast_rcp(1.0f + fast_exp2(-gs0 * kLog2e));
-            put(c.wM + r0 + ra, ll_pack(silu0 * us0, E));
-            if (has_b) {
-              const float silu1 = gs1 * fast_rcp(1.0f + fast_exp2(-gs1 * kLog2e));
-              put(c.wM + r0 + rb, ll_pack(silu1 * us1, E));
-            }
-          }
-        }
+    tc_phase<kTcGU>((R.end - R.begin + kGUTileRows - 1) / kGUTileRows, bop, [&](int t, int r, float gs, float us) {
+      const int row = R.begin + t * kGUTileRows + r;
+      if (row < R.end) {
+        const float silu = gs * fast_rcp(1.0f + fast_exp2(-gs * kLog2e));
+        put(c.wM + row, ll_pack(silu * us, E));
       }
-      release_tile(c, tile, ok);
-      ++tile;
-    }
+    });
     flush();
+    consumer_sync();  // the fragments in sU are overwritten by the next phase
     trace_stamp(c, tid == 0, l * 16 + 9);
   }
 
   // P5: down rows + residual -> X words (next layer's input).
   __device__ void phase_down(const LDGLayerWeights &w, unsigned E, int l) {
-    stage_vec<kInter>(c, sU, c.wM, E, kSiteM);
+    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
+    stage_vec<kInter, kStageFrag>(c, nullptr, bop, c.wM, E, kSiteM, nullptr);
     trace_stamp(c, tid == 0, l * 16 + 10);
-    float act[96];
-    load_act<12>(act, sU, lane);
     const Range R = d_rows(c.cta, c.ncta);
-    for (int r0 = R.begin; r0 < R.end; r0 += kDTileRows) {
-      const int n = min(kDTileRows, R.end - r0);
-      const bool ok = wait_full(c, tile);
-      if (ok) {
-        gemv_tile<12, 1>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
-          if (lane == 0) put(c.wX + r0 + r, ll_pack(v + sA[r0 + r], E));
-        });
-      }
-      release_tile(c, tile, ok);
-      ++tile;
-    }
-    consumer_sync();  // sU (MLP intermediate) is reused by the next phase
+    tc_phase<kTcQuarter>((R.end - R.begin + kDTileRows - 1) / kDTileRows, bop, [&](int t, int r, float v, float) {
+      const int row = R.begin + t * kDTileRows + r;
+      if (row < R.end) put(c.wX + row, ll_pack(v + sA[row], E));
+    });
     flush();
+    consumer_sync();  // sU (fragments) is reused by the next phase
     trace_stamp(c, tid == 0, l * 16 + 11);
   }
 
   // Final RMSNorm + LM head rows + CTA argmax -> ARG words.
   __device__ void phase_lm_head(int step, unsigned E_x, unsigned E) {
-    uint4 wn[4];
-    load_norm_w(wn, p.final_norm, lane);
-    stage_vec<kHidden>(c, sX, c.wX, E_x, kSiteX);
-    trace_stamp(c, tid == 0, p.num_layers * 16 + 0);
-    float act[32];
-    rmsnorm_act(act, sX, wn, lane);
-    if (p.final_hidden && c.cta == 0 && warp == 0 && step == p.num_steps - 1 && live()) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) p.final_hidden[256 * j + 8 * lane + e] = act[j * 8 + e];
+    // Publish this step's K/V rows for the next step's TMA reads: one
+    // gpu-scope fence orders every row written since (the CTA synchronized
+    // with their writers at the named barriers in between), then the flags.
+    if (kv_written && tid == 0 && live()) {
+      __threadfence();
+      const int g = item_of_cta(c.cta, p.splits) / p.splits;
+      for (int l = 0; l < p.num_layers; ++l)
+        if (kv_written & (1ull << l))
+          st_release_u32(&c.ctrl->kv_ready[l * kNumKVHeads + g], epoch_of(c, step, l, p.num_layers));
     }
+    kv_written = 0;
+    NormPrefetch<kHidden> nw;
+    nw.load(p.final_norm, tid);
+    const float ss = stage_vec<kHidden, kStageSumSq>(c, sX, nullptr, c.wX, E_x, kSiteX, red_lm);
+    trace_stamp(c, tid == 0, p.num_layers * 16 + 0);
+    const float rstd = rsqrtf(ss / (float)kHidden + kRmsEps);
+    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
+    build_norm_bop<kHidden>(bop, sX, rstd, nw, tid);
+    if (p.final_hidden && c.cta == 0 && step == p.num_steps - 1 && live()) {
+      for (int i = tid; i < kHidden; i += kConsumerThreads)
+        p.final_hidden[i] = (sX[i] * rstd) * __bfloat162float(p.final_norm[i]);
+    }
+    consumer_sync();
     float best = -INFINITY;
     int best_i = 0x7fffffff;
     float *logits = p.logits ? (p.logits + (size_t)step * kVocab) : nullptr;
     const Range R = lm_rows(c.cta, c.ncta);
-    for (int r0 = R.begin; r0 < R.end; r0 += kLMTileRows) {
-      const int n = min(kLMTileRows, R.end - r0);
-      const bool ok = wait_full(c, tile);
-      if (ok) {
-        gemv_tile<4, 4>(slot_ptr(c, tile), n, act, warp, lane, [&](int r, float v) {
-          const int row = r0 + r;
-          if (v > best || (v == best && row < best_i)) {
-            best = v;
-            best_i = row;
-          }
-          if (logits && lane == 0) logits[row] = v;
-        });
+    tc_phase<kTcRow>((R.end - R.begin + kLMTileRows - 1) / kLMTileRows, bop, [&](int t, int r, float v, float) {
+      const int row = R.begin + t * kLMTileRows + r;
+      if (row < R.end) {
+        if (v > best || (v == best && row < best_i)) {
+          best = v;
+          best_i = row;
+        }
+        if (logits) logits[row] = v;
       }
-      release_tile(c, tile, ok);
-      ++tile;
+    });
+    // warp argmax (largest value, lowest row on ties)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+      if (ov > best || (ov == best && oi < best_i)) {
+        best = ov;
+        best_i = oi;
+      }
     }
     if (lane == 0) {
       c.warp_best_v[warp] = best;
@@ -1098,8 +1331,8 @@ struct Consumer {
         put(c.wArg + 2 * c.cta + 1, ll_pack_u((unsigned)bi, E));
       }
     }
-    consumer_sync();
     flush();
+    consumer_sync();
     trace_stamp(c, tid == 0, p.num_layers * 16 + 1);
   }
 
@@ -1132,23 +1365,32 @@ struct Consumer {
         if (tid == 0 && live() && p.out_log) p.out_log[t - 1] = prev;
       }
       const int tok = step_token(t);
-      // Layer-0 input: the embedding row (bf16 -> fp32).
+      // Layer-0 input: the embedding row (bf16 -> fp32) and its sum of squares.
+      float x_ss;
       {
         const __nv_bfloat16 *erow = p.embed + (size_t)tok * kHidden;
+        float ss = 0.f;
         for (int i = tid; i < kHidden / 4; i += kConsumerThreads) {
           const uint2 v = __ldg(reinterpret_cast<const uint2 *>(erow) + i);
-          sX[4 * i + 0] = bf_lo(v.x);
-          sX[4 * i + 1] = bf_hi(v.x);
-          sX[4 * i + 2] = bf_lo(v.y);
-          sX[4 * i + 3] = bf_hi(v.y);
+          const float e0 = bf_lo(v.x), e1 = bf_hi(v.x), e2 = bf_lo(v.y), e3 = bf_hi(v.y);
+          sX[4 * i + 0] = e0;
+          sX[4 * i + 1] = e1;
+          sX[4 * i + 2] = e2;
+          sX[4 * i + 3] = e3;
+          ss += e0 * e0 + e1 * e1 + e2 * e2 + e3 * e3;
         }
+        ss = warp_sum(ss);
+        if (lane == 0) red_e[warp] = ss;
         consumer_sync();
+        x_ss = 0.f;
+#pragma unroll
+        for (int q = 0; q < kConsumerWarps; ++q) x_ss += red_e[q];
       }
       for (int l = 0; l < L; ++l) {
         c.cur_layer = l;
         const LDGLayerWeights w = p.layers[l];
         const unsigned E = epoch_of(c, t, l, L);
-        phase_qkv(w, E, l, l > 0 ? epoch_of(c, t, l - 1, L) : 0u);
+        phase_qkv(w, E, l, l > 0 ? epoch_of(c, t, l - 1, L) : 0u, x_ss);
         phase_attention(w, l, t, E);
         phase_merge(E, l);
         phase_o(w, E, p.debug_stall == c.cta + 1 && t == 0 && l == 0, l);
@@ -1195,18 +1437,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   c.trace_tile0 = 0;
   c.poll_backoff_ns = p.poll_backoff_ns;
   c.tuning = p.tuning;
+  c.mma_bar = reinterpret_cast<uint64_t *>(smem + kSmMisc + kMiscMmaBar);
+  c.tmem_free = reinterpret_cast<uint64_t *>(smem + kSmMisc + kMiscTmemFree);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kSmMisc + kMiscTmem);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kNumSlots; ++s) {
       mbar_init(&c.full[s], 1);
       mbar_init(&c.empty[s], kConsumerWarps);
     }
+    for (int b = 0; b < kTmemBufs; ++b) {
+      mbar_init(&c.mma_bar[b], 1);
+      mbar_init(&c.tmem_free[b], 4);
+    }
     fence_mbar_init();
     s_abort = 0;
     s_epoch = ld_relaxed_u32(&c.ctrl->epoch);
+    // The tensor-core operands use 1 KB swizzle atoms: refuse to run on a
+    // misaligned dynamic shared memory window instead of computing garbage.
+    if (smem_addr(smem) & 1023u) raise_error_at(&s_abort, c.ctrl, QMK_ERR_SMEM, 0u, c.cta, 0);
   }
+  // One CTA per SM: the TMEM allocation (warp 0) never has to wait.
+  if (threadIdx.x < 32) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before_sync();
   __syncthreads();
+  tc_fence_after_sync();
   c.E0 = s_epoch;
+  c.tmem = *tmem_slot;
 
   if (threadIdx.x >= kConsumerThreads) {
     if ((threadIdx.x & 31) == 0) {
@@ -1216,8 +1473,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   } else {
     Consumer cons(c, p, smem);
     cons.run();
+    cons.drain_mma();
   }
+  tc_fence_before_sync();
   __syncthreads();
+  if (threadIdx.x < 32) {
+    tc_fence_after_sync();
+    tmem_dealloc(c.tmem, kTmemCols);
+  }
 
   if (threadIdx.x == 0) {
     __threadfence();

@@ -39,8 +39,9 @@ constexpr int kSlotBytes = 32768;
 constexpr int kNumSlots = 6;
 constexpr int kQKVTileRows = 16;   // 16 x 2 KB
 constexpr int kOTileRows = 8;      //  8 x 4 KB
-constexpr int kGUTileRows = 8;     //  8 x 2 KB gate + 8 x 2 KB up
-constexpr int kDTileRows = 5;      //  5 x 6 KB
+constexpr int kGUTileRows = 8;     //  8 x (2 KB gate + 2 KB up), interleaved
+constexpr int kDTileRows = 4;      //  4 x 6 KB at an 8 KB pitch
+constexpr int kDRowPitch = 8192;   // down rows in a tile: 3 segments of 2 KB + 2 KB unused
 constexpr int kLMTileRows = 16;    // 16 x 2 KB
 constexpr int kKVTilePos = 64;     // 64 x 256 B K + 64 x 256 B V
 constexpr int kKVTileVOffset = kKVTilePos * kHeadDim * 2;  // 16 KB

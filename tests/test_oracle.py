@@ -65,7 +65,14 @@ def test_mirror_prefill_equals_stepwise(small_weights):
     b = MirrorDecoder(small_weights, 64)
     lb = torch.stack([b.step(t, i) for i, t in enumerate(toks)])
     assert (la - lb).abs().max().item() < 1e-4
-    assert torch.equal(a.k_cache, b.k_cache)
+    # Batched and one-row fp32 matmuls sum in different orders, so an element
+    # close to a bf16 rounding boundary may land one ulp apart (RoPE can
+    # cancel an element to ~1e-5, hence the small absolute term).
+    for ca, cb in ((a.k_cache, b.k_cache), (a.v_cache, b.v_cache)):
+        diff = (ca.float() - cb.float()).abs()
+        ulp = cb.float().abs() * 2.0 ** -7 + 1e-5
+        assert bool((diff <= ulp).all())
+        assert (diff > 0).float().mean().item() < 1e-2
 
 
 def test_rope_tables_match_hf_rotary_embedding():
