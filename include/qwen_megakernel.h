@@ -209,6 +209,45 @@ int qmk_describe_partition(int num_ctas, int splits, int cta, int *out, int out_
  * window), then the LM-head slots. */
 int qmk_trace_words(void);
 
+/* ---- allocation-free variant (no counterpart in the reference) ----------
+ * qmk_generate_static runs the same decode as launch_ldg_generate_nosync
+ * (csrc/torch_bindings.cpp:83-91 of the reference) but allocates nothing:
+ * no cudaMalloc / cudaFree / cudaHostAlloc, no allocator of any library.
+ * Its scratch -- the kernel workspace, the token log and a status block --
+ * is one file-scope __device__ array of QMK_STATIC_SCRATCH_BYTES per device
+ * in this library's static device memory.  It is meant for callers that
+ * must not allocate on this path: a host framework that owns all device
+ * memory through its own pool (a cudaMalloc behind its back can fail or
+ * fragment it), and latency-critical loops where the implicit device-wide
+ * synchronization of cudaMalloc / cudaFree is not acceptable.
+ *
+ *  - Limit: num_steps <= QMK_STATIC_MAX_STEPS (the token log's capacity);
+ *    larger requests return QMK_ERR_ARGS without launching.
+ *  - The first call on a device does one-time setup (cudaGetSymbolAddress
+ *    of the scratch array, kernel attributes); make that first call before
+ *    any stream capture.
+ *  - The workspace part must start zeroed: static device memory is zero
+ *    when the module loads and every launch leaves it valid for the next.
+ *  - All calls on a device share the one scratch array: calls that overlap
+ *    in time (different streams without ordering, or different host
+ *    threads) race on it.  Serialize them, e.g. on one stream.
+ *  - Results: qmk_static_scratch_ptrs gives the device addresses of the
+ *    token log (int32 [QMK_STATIC_MAX_STEPS], entry t = token of step t of
+ *    the last call) and of the QmkStatus block (device memory: copy it to
+ *    the host after the stream completes). */
+#define QMK_STATIC_MAX_STEPS 4096
+#define QMK_STATIC_SCRATCH_BYTES (448 * 1024)
+
+int qmk_generate_static(int first_token_id, int num_steps, const void *embed_weight,
+                        const LDGLayerWeights *layer_weights, const void *final_norm_weight,
+                        const void *lm_head_weight, const void *cos_table, const void *sin_table,
+                        void *k_cache, void *v_cache, int num_layers, int start_position,
+                        int max_seq_len, float attn_scale, cudaStream_t stream);
+
+/* Device addresses (current device) of the static token log and status
+ * block used by qmk_generate_static; either pointer may be NULL. */
+int qmk_static_scratch_ptrs(int **output_log, QmkStatus **status);
+
 /* Library version string. */
 const char *qmk_version(void);
 

@@ -1859,4 +1859,83 @@ void launch_ldg_generate_nosync(int first_token_id, int num_steps, const void *e
                    nullptr, num_layers, start_position, max_seq_len, attn_scale, stream);
 }
 
+// ---- allocation-free variant: file-scope static scratch ----
+
+}  // extern "C"
+
+namespace {
+
+// Scratch of qmk_generate_static: [workspace | token log | status].
+constexpr size_t kStaticLogOff = (size_t)qmk::kWorkspaceBytes;
+constexpr size_t kStaticStatusOff = kStaticLogOff + 4 * (size_t)QMK_STATIC_MAX_STEPS;
+static_assert(kStaticStatusOff + 256 <= (size_t)QMK_STATIC_SCRATCH_BYTES, "static scratch too small");
+static_assert(kStaticLogOff % 256 == 0, "token log alignment");
+
+__device__ __align__(256) unsigned char g_static_scratch[QMK_STATIC_SCRATCH_BYTES];
+
+uint8_t *g_static_ptr[kMaxDevices] = {};
+
+// Device address of g_static_scratch on the current device (looked up once).
+int static_scratch(uint8_t **out) {
+  int dev = 0;
+  if (current_device(&dev) != QMK_OK) return g_last_error;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!g_static_ptr[dev]) {
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (e != cudaSuccess || !ptr)
+      return set_error(QMK_ERR_CUDA, "cudaGetSymbolAddress(static scratch) on device %d: %s", dev,
+                       cudaGetErrorString(e));
+    g_static_ptr[dev] = static_cast<uint8_t *>(ptr);
+  }
+  *out = g_static_ptr[dev];
+  return QMK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qmk_generate_static(int first_token_id, int num_steps, const void *embed_weight,
+                        const LDGLayerWeights *layer_weights, const void *final_norm_weight,
+                        const void *lm_head_weight, const void *cos_table, const void *sin_table,
+                        void *k_cache, void *v_cache, int num_layers, int start_position,
+                        int max_seq_len, float attn_scale, cudaStream_t stream) {
+  if (num_steps < 1 || num_steps > QMK_STATIC_MAX_STEPS)
+    return set_error(QMK_ERR_ARGS,
+                     "qmk_generate_static: num_steps=%d outside [1, %d] (capacity of the static token log)",
+                     num_steps, QMK_STATIC_MAX_STEPS);
+  uint8_t *base = nullptr;
+  if (static_scratch(&base) != QMK_OK) return g_last_error;
+  QmkRunArgs a;
+  memset(&a, 0, sizeof(a));
+  a.embed_weight = embed_weight;
+  a.layer_weights = layer_weights;
+  a.final_norm_weight = final_norm_weight;
+  a.lm_head_weight = lm_head_weight;
+  a.cos_table = cos_table;
+  a.sin_table = sin_table;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.workspace = base;
+  a.workspace_bytes = (size_t)qmk::kWorkspaceBytes;
+  a.first_token = first_token_id;
+  a.start_position = start_position;
+  a.num_steps = num_steps;
+  a.num_layers = num_layers;
+  a.max_seq_len = max_seq_len;
+  a.attn_scale = attn_scale;
+  a.output_log = reinterpret_cast<int *>(base + kStaticLogOff);
+  a.status = reinterpret_cast<QmkStatus *>(base + kStaticStatusOff);
+  return qmk_run(&a, stream);
+}
+
+int qmk_static_scratch_ptrs(int **output_log, QmkStatus **status) {
+  uint8_t *base = nullptr;
+  if (static_scratch(&base) != QMK_OK) return g_last_error;
+  if (output_log) *output_log = reinterpret_cast<int *>(base + kStaticLogOff);
+  if (status) *status = reinterpret_cast<QmkStatus *>(base + kStaticStatusOff);
+  return clear_error();
+}
+
 }  // extern "C"
