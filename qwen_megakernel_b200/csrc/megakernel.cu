@@ -136,15 +136,11 @@ static_assert(kMaxSplits * kMergeWordsPerSplit <= kInter, "merge scratch too lar
 // consumer warp 0 starts waiting for it, [+2k+1] it has landed,
 // [kTraceTileBase + 2*kTraceTiles + k] the producer issued its copy and
 // [kTraceTileBase + 3*kTraceTiles + k] consumer warp 0 released it; for
-// tensor-core tiles [+4*kTraceTiles + k] thread 0 read its accumulator,
-// [+5*kTraceTiles + k] finished its rows, and in SM clock cycles (clock64)
-// [+6*kTraceTiles + k] the issuer of M block 0 started its MMAs,
-// [+7*kTraceTiles + k] it committed them, [+8*kTraceTiles + k] thread 0
-// saw them complete; [+9k] the issuer entered the phase, [+10k] it had
-// passed the TMEM-buffer wait, [+11k] thread 0 entered the phase.
+// tensor-core tiles [+4*kTraceTiles + k] thread 0 read its accumulator and
+// [+5*kTraceTiles + k] finished its rows.
 constexpr int kTraceTiles = 512;
 constexpr int kTraceTileBase = (kMaxLayers + 1) * 16;
-constexpr int kTraceStride = kTraceTileBase + 12 * kTraceTiles;
+constexpr int kTraceStride = kTraceTileBase + 6 * kTraceTiles;
 
 struct Ctx {
   uint8_t *ring;
@@ -328,6 +324,7 @@ __device__ __forceinline__ const uint8_t *slot_ptr(const Ctx &c, uint32_t tile) 
 // h = e >> 9 = 2s + h', line q = (e >> 6) & 7) has its hi part at
 // bop_offset<S>(e) and its lo part 1024 bytes further; 4S KB in all.
 enum TcKind : int { kTcRow = 0, kTcGU = 1, kTcHalf = 2, kTcQuarter = 3 };
+enum TcOut : int { kOutQKV = 0, kOutO = 1, kOutGU = 2, kOutDown = 3, kOutLM = 4 };
 
 template <int S>
 __device__ __forceinline__ int bop_offset(int e) {
@@ -358,108 +355,117 @@ __device__ __forceinline__ void store_bop_pair(uint8_t *bop, int e, float v0, fl
 
 // ------------------------------------------------------------- LL staging
 enum StageMode : int {
-  kStageF32 = 0,    // fp32 copy into dst
-  kStageSumSq = 1,  // fp32 copy into dst, returns sum of squares of the vector
-  kStageFrag = 2,   // B fragments (tensor-core GEMV operand) into frag
+  kStageSumSq = 1,     // fp32 copy into dst, returns sum of squares of the vector
+  kStageFrag = 2,      // tensor-core B operand of the vector into bop
+  kStageNormFrag = 3,  // fp32 copy into dst, B operand of x * w (norm weights
+                       // prefetched in nw), returns sum of squares
 };
 
 // All consumer threads: poll the N words of `src` until their flag equals
 // `flag` (two words per 16-byte load) and store them per MODE, then
-// consumer_sync().  kStageSumSq folds a block reduction into that barrier,
-// using red[kConsumerWarps] (one array per call site); the sum is taken in a
-// fixed order whatever the order in which the words arrive.  kStageFrag
-// writes the tensor-core B operand (K = N) and fences it for the async proxy.
+// consumer_sync().  The sum of squares is folded into that barrier (block
+// reduction through red[kConsumerWarps], one array per call site) and taken
+// in a fixed order whatever the order in which the words arrive.  B operand
+// writes (K = N) are fenced for the async proxy before the barrier.
+// Thread tid handles word pairs q = tid + k * kConsumerThreads.
+// Norm-weight pairs of the words a thread stages (kStageNormFrag), by value.
+struct NormPairs {
+  uint32_t w[4];
+};
+
 template <int N, int MODE>
-__device__ float stage_vec(Ctx &c, float *dst, uint8_t *bop, const uint64_t *src, unsigned flag, unsigned site,
-                           float *red) {
+__device__ __forceinline__ float stage_vec(Ctx &c, float *dst, uint8_t *bop, const uint64_t *src, unsigned flag,
+                                        unsigned site, float *red, NormPairs nw) {
   constexpr int kPairs = N / 2;
   constexpr int P = (kPairs + kConsumerThreads - 1) / kConsumerThreads;
+  constexpr bool kSum = (MODE == kStageSumSq || MODE == kStageNormFrag);
   static_assert(N % 2 == 0 && P <= 32, "stage_vec size");
+  static_assert(MODE != kStageNormFrag || P <= 4, "norm-weight pairs per thread");
   const int tid = threadIdx.x;
   unsigned pending = 0;
 #pragma unroll
   for (int k = 0; k < P; ++k)
     if (k * kConsumerThreads + tid < kPairs) pending |= 1u << k;
   if (*c.abort_flag) pending = 0;
-  float keep[MODE == kStageSumSq ? P : 1][2];
+  float keep[kSum ? P : 1][2];
 #pragma unroll
-  for (int k = 0; k < (MODE == kStageSumSq ? P : 1); ++k) keep[k][0] = keep[k][1] = 0.f;
-  Waiter w;
-  while (pending) {
-    uint64_t a[P], b[P];
+  for (int k = 0; k < (kSum ? P : 1); ++k) keep[k][0] = keep[k][1] = 0.f;
+  uint64_t a0[P], b0[P];
+  auto issue = [&](uint64_t (&a)[P], uint64_t (&b)[P]) {
 #pragma unroll
     for (int k = 0; k < P; ++k) {
       a[k] = 0;
       b[k] = 0;
       if (pending & (1u << k)) ll_load2(src + 2 * (k * kConsumerThreads + tid), a[k], b[k]);
     }
+  };
+  auto check = [&](const uint64_t (&a)[P], const uint64_t (&b)[P]) {
 #pragma unroll
     for (int k = 0; k < P; ++k) {
       if ((pending & (1u << k)) && ll_flag(a[k]) == flag && ll_flag(b[k]) == flag) {
         const int q = k * kConsumerThreads + tid;
         const float v0 = ll_value(a[k]), v1 = ll_value(b[k]);
-        if (MODE == kStageFrag) {
-          store_bop_pair<N / 1024>(bop, 2 * q, v0, v1);
-        } else {
-          reinterpret_cast<float2 *>(dst)[q] = make_float2(v0, v1);
-          if (MODE == kStageSumSq) {
-            keep[MODE == kStageSumSq ? k : 0][0] = v0;
-            keep[MODE == kStageSumSq ? k : 0][1] = v1;
-          }
+        if (MODE != kStageFrag) reinterpret_cast<float2 *>(dst)[q] = make_float2(v0, v1);
+        if (MODE == kStageFrag) store_bop_pair<N / 1024>(bop, 2 * q, v0, v1);
+        if (MODE == kStageNormFrag) {
+          const uint32_t wk = nw.w[k < 4 ? k : 3];
+          store_bop_pair<N / 1024>(bop, 2 * q, v0 * bf_lo(wk), v1 * bf_hi(wk));
+        }
+        if (kSum) {
+          keep[kSum ? k : 0][0] = v0;
+          keep[kSum ? k : 0][1] = v1;
         }
         pending &= ~(1u << k);
       }
     }
-    if (pending) {
-      if (!w.keep_going(c, site)) break;
-      if (c.poll_backoff_ns) __nanosleep(c.poll_backoff_ns);
-    }
+  };
+  Waiter w;
+  while (pending) {
+    issue(a0, b0);
+    check(a0, b0);
+    if (!pending) break;
+    if (!w.keep_going(c, site)) break;
+    if (c.poll_backoff_ns) __nanosleep(c.poll_backoff_ns);
   }
-  if (MODE == kStageFrag) fence_proxy_async_smem();
-  if (MODE == kStageSumSq) {
+  if (MODE == kStageFrag || MODE == kStageNormFrag) fence_proxy_async_smem();
+  if (kSum) {
     float ss = 0.f;
 #pragma unroll
-    for (int k = 0; k < (MODE == kStageSumSq ? P : 1); ++k)
-      ss = fmaf(keep[k][0], keep[k][0], fmaf(keep[k][1], keep[k][1], ss));
+    for (int k = 0; k < (kSum ? P : 1); ++k) ss = fmaf(keep[k][0], keep[k][0], fmaf(keep[k][1], keep[k][1], ss));
     ss = warp_sum(ss);
     if ((tid & 31) == 0) red[tid >> 5] = ss;
   }
   consumer_sync();
   float total = 0.f;
-  if (MODE == kStageSumSq) {
+  if (kSum) {
 #pragma unroll
     for (int q = 0; q < kConsumerWarps; ++q) total += red[q];
   }
   return total;
 }
 
-// Norm weights (bf16 pairs) of the elements thread `tid` writes in
-// build_norm_bop<K>, fetched before the dataflow wait.
-template <int K>
-struct NormPrefetch {
-  static constexpr int kPer = (K / 2 + kConsumerThreads - 1) / kConsumerThreads;
-  uint32_t w[kPer];
-  __device__ __forceinline__ void load(const __nv_bfloat16 *nw, int tid) {
+// Norm weights (bf16 pairs) of the word pairs thread `tid` stages
+// (q = tid + j * kConsumerThreads), fetched before the dataflow wait.
+__device__ __forceinline__ NormPairs load_norm_pairs(const __nv_bfloat16 *nw, int tid) {
+  NormPairs r;
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int q = tid + j * kConsumerThreads;
-      w[j] = (q < K / 2) ? __ldg(reinterpret_cast<const unsigned *>(nw) + q) : 0u;
-    }
-  }
-};
-
-// B operand <- RMSNorm(x) * w, i.e. x * rstd * w (fp32, the order of the
-// reference and of HF's Qwen3RMSNorm), fenced for the tensor cores; the
-// caller's next consumer_sync publishes it.
-template <int K>
-__device__ __forceinline__ void build_norm_bop(uint8_t *bop, const float *x, float rstd, const NormPrefetch<K> &nw,
-                                               int tid) {
-#pragma unroll
-  for (int j = 0; j < NormPrefetch<K>::kPer; ++j) {
+  for (int j = 0; j < 4; ++j) {
     const int q = tid + j * kConsumerThreads;
-    if (q < K / 2) {
+    r.w[j] = (q < kHidden / 2) ? __ldg(reinterpret_cast<const unsigned *>(nw) + q) : 0u;
+  }
+  return r;
+}
+
+// B operand <- x * w (the RMSNorm weight; 1/rms is applied to the GEMV
+// results), fenced for the tensor cores; the caller's next consumer_sync
+// publishes it.  K = 1024.
+__device__ __forceinline__ void build_norm_bop(uint8_t *bop, const float *x, const NormPairs &nw, int tid) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int q = tid + j * kConsumerThreads;
+    if (q < kHidden / 2) {
       const float2 v = reinterpret_cast<const float2 *>(x)[q];
-      store_bop_pair<K / 1024>(bop, 2 * q, (v.x * rstd) * bf_lo(nw.w[j]), (v.y * rstd) * bf_hi(nw.w[j]));
+      store_bop_pair<1>(bop, 2 * q, v.x * bf_lo(nw.w[j]), v.y * bf_hi(nw.w[j]));
     }
   }
   fence_proxy_async_smem();
@@ -476,14 +482,15 @@ __device__ void stage_list(Ctx &c, float *dst, int n, AddrFn addr, unsigned flag
   for (int k = 0; k < K; ++k)
     if (k * kConsumerThreads + tid < n) pending |= 1u << k;
   if (*c.abort_flag) pending = 0;
-  Waiter w;
-  while (pending) {
-    uint64_t v[K];
+  uint64_t v0[K];
+  auto issue = [&](uint64_t (&v)[K]) {
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       v[k] = 0;
       if (pending & (1u << k)) v[k] = ll_load(addr(k * kConsumerThreads + tid));
     }
+  };
+  auto check = [&](const uint64_t (&v)[K]) {
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       if ((pending & (1u << k)) && ll_flag(v[k]) == flag) {
@@ -491,10 +498,14 @@ __device__ void stage_list(Ctx &c, float *dst, int n, AddrFn addr, unsigned flag
         pending &= ~(1u << k);
       }
     }
-    if (pending) {
-      if (!w.keep_going(c, site)) break;
-      if (c.poll_backoff_ns) __nanosleep(c.poll_backoff_ns);
-    }
+  };
+  Waiter w;
+  while (pending) {
+    issue(v0);
+    check(v0);
+    if (!pending) break;
+    if (!w.keep_going(c, site)) break;
+    if (c.poll_backoff_ns) __nanosleep(c.poll_backoff_ns);
   }
   consumer_sync();
 }
@@ -737,7 +748,11 @@ struct Consumer {
   float *red_x, *red_a, *red_lm, *red_e;  // block-reduction slots, one per call site
   uint32_t tile = 0;
   unsigned mma_seq = 0;      // tensor-core units consumed (buffer = seq % kTmemBufs)
+  float lm_best = -INFINITY;  // LM head: this thread's best logit and row
+  int lm_best_i = 0x7fffffff;
+  float *lm_logits = nullptr;
   unsigned mma_issued = 0;   // issuer threads: 1 + the last unit this thread issued
+  bool tc_prewaited = false; // issuer threads: the next phase's first unit needs no waits
   int warp, lane, tid;
   uint64_t kv_written = 0;  // layers whose new K/V row this CTA wrote this step
 
@@ -759,44 +774,48 @@ struct Consumer {
   __device__ __forceinline__ bool live() const { return *c.abort_flag == 0; }
 
   // Slots (N / 16) of a GEMV kind.
-  template <int KIND>
-  __host__ __device__ static constexpr int tc_slots() {
-    return (KIND == kTcHalf) ? 2 : (KIND == kTcQuarter) ? 3 : 1;
-  }
+  __device__ static int tc_slots(int kind) { return (kind == kTcHalf) ? 2 : (kind == kTcQuarter) ? 3 : 1; }
 
   // Issue the 4 MMAs of M block hp of ring tile `tl` (tensor-core unit
   // number seq) into TMEM buffer seq % kTmemBufs, against the B operand at
-  // bop.  Layout of A, B and D: see the GEMV section above.
-  template <int KIND>
-  __device__ bool tc_issue_unit(uint32_t tl, int hp, unsigned seq, const uint8_t *bop) {
-    constexpr int S = tc_slots<KIND>();
-    constexpr uint32_t kIdesc = mma_idesc_bf16(128, 16 * S);
+  // bop with S slots.  Layout of A, B and D: see the GEMV section above.
+  __device__ bool tc_issue_unit(uint32_t tl, int hp, unsigned seq, const uint8_t *bop, int S, bool waited) {
+    const uint32_t idesc = mma_idesc_bf16(128, 16 * S);
     const unsigned b = seq % kTmemBufs;
-    const uint32_t tk0 = tl - c.trace_tile0;
-    if (c.trace && hp == 0 && tk0 < (uint32_t)kTraceTiles) c.trace[kTraceTileBase + 9 * kTraceTiles + tk0] = clock64();
-    if (seq >= (unsigned)kTmemBufs) {
-      // the unit that used this buffer before must have been read out
-      const unsigned par = ((seq / kTmemBufs) - 1u) & 1u;
-      Waiter w;
-      while (!mbar_try_wait(&c.tmem_free[b], par))
-        if (!w.keep_going(c, kSiteMma)) return false;
-    }
-    if (c.trace && hp == 0 && tk0 < (uint32_t)kTraceTiles) c.trace[kTraceTileBase + 10 * kTraceTiles + tk0] = clock64();
-    if (!wait_full_one(c, tl)) return false;
+    if (!waited && !tc_unit_waits(tl, seq)) return false;
     tc_fence_after_sync();
-    const uint32_t tk = tl - c.trace_tile0;
-    const bool tstamp = c.trace && hp == 0 && tk < (uint32_t)kTraceTiles;
-    if (tstamp) c.trace[kTraceTileBase + 6 * kTraceTiles + tk] = clock64();
     const uint32_t a0 = smem_addr(slot_ptr(c, tl)) + 1024u * (uint32_t)hp;
-    const uint32_t b0 = smem_addr(bop) + 2048u * S * (uint32_t)hp;
+    const uint32_t b0 = smem_addr(bop) + 2048u * (uint32_t)(S * hp);
     const uint32_t d = c.tmem + (uint32_t)kTmemBufCols * b;
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk)
-      tc_mma_bf16(d, smem_desc_sw128(a0 + 32u * kk, 2048u), smem_desc_sw128(b0 + 32u * kk, 1024u), kIdesc, kk > 0);
+      tc_mma_bf16(d, smem_desc_sw128(a0 + 32u * kk, 2048u), smem_desc_sw128(b0 + 32u * kk, 1024u), idesc, kk > 0);
     tc_commit(&c.mma_bar[b]);
-    if (tstamp) c.trace[kTraceTileBase + 7 * kTraceTiles + tk] = clock64();
     mma_issued = seq + 1u;
     return true;
+  }
+
+  // What a unit needs before its MMAs: its TMEM buffer read out by the
+  // readers of the unit that used it before, and its ring tile landed.
+  __device__ bool tc_unit_waits(uint32_t tl, unsigned seq) {
+    if (seq >= (unsigned)kTmemBufs) {
+      const unsigned par = ((seq / kTmemBufs) - 1u) & 1u;
+      Waiter w;
+      while (!mbar_try_wait(&c.tmem_free[seq % kTmemBufs], par))
+        if (!w.keep_going(c, kSiteMma)) return false;
+    }
+    return wait_full_one(c, tl);
+  }
+
+  // Issuers, before the phase's input is staged: the waits of the first unit
+  // each issues, so that its MMAs can start as soon as the B operand is ready.
+  __device__ void tc_prewait(int r0, int r1, int tile_rows) {
+    tc_prewaited = false;
+    if (warp >= 4 && lane == 0 && live()) {
+      const int u = warp - 4;
+      const int ntiles = (r1 - r0 + tile_rows - 1) / tile_rows;
+      if (u < 2 * ntiles) tc_prewaited = tc_unit_waits(tile + (uint32_t)(u >> 1), mma_seq + (unsigned)u);
+    }
   }
 
   // Reader side: wait (bounded) for tensor-core unit seq.
@@ -808,35 +827,74 @@ struct Consumer {
     return true;
   }
 
-  // GEMV phase over `ntiles` consecutive ring tiles on the tensor cores.
+  // One GEMV phase on the tensor cores (see tc_phase).
+  struct TcJob {
+    int kind;       // TcKind: tile layout
+    int out;        // TcOut: what the rows produce
+    int r0, r1;     // this CTA's rows
+    int tile_rows;  // rows per ring tile
+    float scale;    // 1/rms of a normalized input (1 otherwise)
+    unsigned E;     // epoch of the output words
+  };
+
+  // Row `row` of a phase, value v (and v2: the up projection of kOutGU).
+  __device__ void tc_emit(const TcJob &job, int row, float v, float v2) {
+    switch (job.out) {
+      case kOutQKV:
+        put(c.wQKV + row, ll_pack(v * job.scale, job.E));
+        break;
+      case kOutO:
+        put(c.wA + row, ll_pack(v + sX[row], job.E));
+        break;
+      case kOutGU: {
+        const float gs = v * job.scale, us = v2 * job.scale;
+        const float silu = gs * fast_rcp(1.0f + fast_exp2(-gs * kLog2e));
+        put(c.wM + row, ll_pack(silu * us, job.E));
+        break;
+      }
+      case kOutDown:
+        put(c.wX + row, ll_pack(v + sA[row], job.E));
+        break;
+      default: {  // kOutLM
+        const float y = v * job.scale;
+        if (y > lm_best || (y == lm_best && row < lm_best_i)) {
+          lm_best = y;
+          lm_best_i = row;
+        }
+        if (lm_logits) lm_logits[row] = y;
+        break;
+      }
+    }
+  }
+
+  // GEMV phase over the ring tiles of rows [r0, r1) on the tensor cores.
   // A unit is one M block (4 MMAs); lane 0 of warps 4-6 issue the units
   // round-robin (a single issuing thread is limited by the issue latency of
   // tcgen05.mma), up to kTmemBufs units in flight; warps 0-3 read both units
   // of a tile (one TMEM lane each), add the diagonal entries of every output
-  // row with warp shuffles and call emit(tile, row, value, value2) from one
-  // lane per row.
+  // row with warp shuffles and emit each row from one lane.
   //   kTcRow     K = 1024, 16 rows
   //   kTcGU      K = 1024, tile rows 2k (gate) and 2k+1 (up) of output row
-  //              k (8 rows); emit gets (gate, up)
+  //              k (8 rows)
   //   kTcHalf    K = 2048, 8 rows
   //   kTcQuarter K = 3072, 4 rows at an 8 KB pitch
-  template <int KIND, typename Emit>
-  __device__ void tc_phase(int ntiles, const uint8_t *bop, Emit emit) {
-    constexpr int S = tc_slots<KIND>();
+  __device__ __forceinline__ void tc_phase(const TcJob &job, const uint8_t *bop) {
+    const int S = tc_slots(job.kind);
+    const int ntiles = (job.r1 - job.r0 + job.tile_rows - 1) / job.tile_rows;
     constexpr int kIssuers = kConsumerWarps - 4;
     const unsigned seq0 = mma_seq;
     const int nunits = 2 * ntiles;
-    if (tid == 0 && c.trace && tile - c.trace_tile0 < (uint32_t)kTraceTiles)
-      c.trace[kTraceTileBase + 11 * kTraceTiles + (tile - c.trace_tile0)] = clock64();
     if (warp >= 4 && lane == 0) {
       bool ok = live();
       for (int u = warp - 4; u < nunits && ok; u += kIssuers)
-        ok = tc_issue_unit<KIND>(tile + (uint32_t)(u >> 1), u & 1, seq0 + (unsigned)u, bop);
+        ok = tc_issue_unit(tile + (uint32_t)(u >> 1), u & 1, seq0 + (unsigned)u, bop, S,
+                           u == warp - 4 && tc_prewaited);
+      tc_prewaited = false;
     }
     if (warp < 4) {
       const int q = lane & 7;
       const int j = (32 * warp + lane) >> 3;  // segment of this lane
-      const int slot = (KIND == kTcHalf) ? (j & 1) : (KIND == kTcQuarter) ? (j & 3) : 0;
+      const int slot = (job.kind == kTcHalf) ? (j & 1) : (job.kind == kTcQuarter) ? (j & 3) : 0;
       const bool valid = slot < S;            // K = 3072: quarter 3 of a row is unused
       for (int t = 0; t < ntiles; ++t) {
         const unsigned seq = seq0 + 2u * (unsigned)t;
@@ -844,7 +902,6 @@ struct Consumer {
         got = __all_sync(0xffffffffu, got);
         const uint32_t tk = tile + (uint32_t)t - c.trace_tile0;
         const bool tstamp = c.trace && tid == 0 && tk < (uint32_t)kTraceTiles;
-        if (tstamp) c.trace[kTraceTileBase + 8 * kTraceTiles + tk] = clock64();
         if (got && tid == 0) {
           // both units' MMAs have read the tile: hand the ring slot back
           if (tstamp) c.trace[kTraceTileBase + 3 * kTraceTiles + tk] = global_timer_ns();
@@ -858,26 +915,23 @@ struct Consumer {
           for (int hp = 0; hp < 2; ++hp) {
             const uint32_t taddr =
                 c.tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)kTmemBufCols * ((seq + (unsigned)hp) % kTmemBufs);
-            if (S == 1) {
-              uint32_t r[16];
-              tmem_ld16(taddr, r);
+            // this lane's diagonal pair: columns 16*slot + q (hi) and + 8 (lo)
+            for (int s0 = 0; s0 < S; s0 += 2) {
+              if (S - s0 >= 2) {
+                uint32_t r[32];
+                tmem_ld32(taddr + 16u * (uint32_t)s0, r);
 #pragma unroll
-              for (int col = 0; col < 8; ++col)
-                if (col == q) v += __uint_as_float(r[col]) + __uint_as_float(r[8 + col]);
-            } else {
-              uint32_t r[32];
-              tmem_ld32(taddr, r);
+                for (int ss = 0; ss < 2; ++ss)
 #pragma unroll
-              for (int ss = 0; ss < 2; ++ss)
-#pragma unroll
-                for (int col = 0; col < 8; ++col)
-                  if (ss == slot && col == q) v += __uint_as_float(r[16 * ss + col]) + __uint_as_float(r[16 * ss + 8 + col]);
-              if (S == 3) {
-                uint32_t r2[16];
-                tmem_ld16(taddr + 32u, r2);
+                  for (int col = 0; col < 8; ++col)
+                    if (s0 + ss == slot && col == q)
+                      v += __uint_as_float(r[16 * ss + col]) + __uint_as_float(r[16 * ss + 8 + col]);
+              } else {
+                uint32_t r[16];
+                tmem_ld16(taddr + 16u * (uint32_t)s0, r);
 #pragma unroll
                 for (int col = 0; col < 8; ++col)
-                  if (slot == 2 && col == q) v += __uint_as_float(r2[col]) + __uint_as_float(r2[8 + col]);
+                  if (s0 == slot && col == q) v += __uint_as_float(r[col]) + __uint_as_float(r[8 + col]);
               }
             }
           }
@@ -888,19 +942,19 @@ struct Consumer {
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         v += __shfl_xor_sync(0xffffffffu, v, 4);
-        if (KIND == kTcRow) {
-          if (got && q == 0) emit(t, j, v, 0.f);
-        } else if (KIND == kTcGU) {
-          const float up = __shfl_down_sync(0xffffffffu, v, 8);
-          if (got && (lane & 15) == 0) emit(t, j >> 1, v, up);
-        } else if (KIND == kTcHalf) {
-          v += __shfl_xor_sync(0xffffffffu, v, 8);
-          if (got && (lane & 15) == 0) emit(t, j >> 1, v, 0.f);
-        } else {
-          v += __shfl_xor_sync(0xffffffffu, v, 8);
-          v += __shfl_xor_sync(0xffffffffu, v, 16);
-          if (got && lane == 0) emit(t, warp, v, 0.f);
+        if (job.kind == kTcHalf || job.kind == kTcQuarter) v += __shfl_xor_sync(0xffffffffu, v, 8);
+        if (job.kind == kTcQuarter) v += __shfl_xor_sync(0xffffffffu, v, 16);
+        const float up = __shfl_down_sync(0xffffffffu, v, 8);
+        int lrow = -1;
+        if (job.kind == kTcRow) {
+          if (q == 0) lrow = j;
+        } else if (job.kind == kTcQuarter) {
+          if (lane == 0) lrow = warp;
+        } else if ((lane & 15) == 0) {
+          lrow = j >> 1;
         }
+        const int row = job.r0 + t * job.tile_rows + lrow;
+        if (got && lrow >= 0 && row < job.r1) tc_emit(job, row, v, up);
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&c.tmem_free[seq % kTmemBufs]);
@@ -947,20 +1001,21 @@ struct Consumer {
   // x_flag: epoch of the X words to stage, or 0 when sX already holds the
   // layer input (the embedding row of layer 0) and x_ss its sum of squares.
   __device__ void phase_qkv(const LDGLayerWeights &w, unsigned E, int l, unsigned x_flag, float x_ss) {
-    NormPrefetch<kHidden> nw;
-    nw.load((const __nv_bfloat16 *)w.input_layernorm_weight, tid);
-    if (x_flag) x_ss = stage_vec<kHidden, kStageSumSq>(c, sX, nullptr, c.wX, x_flag, kSiteX, red_x);
-    trace_stamp(c, tid == 0, l * 16 + 0);
+    const NormPairs nw = load_norm_pairs((const __nv_bfloat16 *)w.input_layernorm_weight, tid);
     uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
-    build_norm_bop<kHidden>(bop, sX, rsqrtf(x_ss / (float)kHidden + kRmsEps), nw, tid);
-    consumer_sync();
     const Range R = qkv_rows(c.cta, c.ncta);
-    tc_phase<kTcRow>((R.end - R.begin + kQKVTileRows - 1) / kQKVTileRows, bop, [&](int t, int r, float v, float) {
-      const int row = R.begin + t * kQKVTileRows + r;
-      if (row < R.end) put(c.wQKV + row, ll_pack(v, E));
-    });
+    tc_prewait(R.begin, R.end, kQKVTileRows);
+    if (x_flag) {
+      x_ss = stage_vec<kHidden, kStageNormFrag>(c, sX, bop, c.wX, x_flag, kSiteX, red_x, nw);
+    } else {
+      build_norm_bop(bop, sX, nw, tid);
+      consumer_sync();
+    }
+    trace_stamp(c, tid == 0, l * 16 + 0);
+    const TcJob job{kTcRow, kOutQKV, R.begin, R.end, kQKVTileRows, rsqrtf(x_ss / (float)kHidden + kRmsEps), E};
+    tc_phase(job, bop);
     flush();
-    consumer_sync();  // the fragments in sU are overwritten by the next phase
+    consumer_sync();  // the B operand in sU is overwritten by the next phase
     trace_stamp(c, tid == 0, l * 16 + 1);
   }
 
@@ -1209,52 +1264,43 @@ struct Consumer {
   // P3: O-projection rows + residual -> A words.
   __device__ void phase_o(const LDGLayerWeights &w, unsigned E, bool stall, int l) {
     uint8_t *bop = reinterpret_cast<uint8_t *>(sAtt);
-    // Test hook: 0xFFFFFFFF is never an epoch, so this wait can only expire.
-    stage_vec<kQSize, kStageFrag>(c, nullptr, bop, c.wAtt, stall ? 0xFFFFFFFFu : E, kSiteAtt, nullptr);
-    trace_stamp(c, tid == 0, l * 16 + 6);
     const Range R = o_rows(c.cta, c.ncta);
-    tc_phase<kTcHalf>((R.end - R.begin + kOTileRows - 1) / kOTileRows, bop, [&](int t, int r, float v, float) {
-      const int row = R.begin + t * kOTileRows + r;
-      if (row < R.end) put(c.wA + row, ll_pack(v + sX[row], E));
-    });
+    tc_prewait(R.begin, R.end, kOTileRows);
+    // Test hook: 0xFFFFFFFF is never an epoch, so this wait can only expire.
+    stage_vec<kQSize, kStageFrag>(c, nullptr, bop, c.wAtt, stall ? 0xFFFFFFFFu : E, kSiteAtt, nullptr, NormPairs{});
+    trace_stamp(c, tid == 0, l * 16 + 6);
+    const TcJob job{kTcHalf, kOutO, R.begin, R.end, kOTileRows, 1.f, E};
+    tc_phase(job, bop);
     flush();
     trace_stamp(c, tid == 0, l * 16 + 7);
   }
 
   // P4: RMSNorm(a) then gate/up rows, SiLU(gate) * up -> M words.
   __device__ void phase_gate_up(const LDGLayerWeights &w, unsigned E, int l) {
-    NormPrefetch<kHidden> nw;
-    nw.load((const __nv_bfloat16 *)w.post_attn_layernorm_weight, tid);
-    const float ss = stage_vec<kHidden, kStageSumSq>(c, sA, nullptr, c.wA, E, kSiteA, red_a);
-    trace_stamp(c, tid == 0, l * 16 + 8);
+    const NormPairs nw = load_norm_pairs((const __nv_bfloat16 *)w.post_attn_layernorm_weight, tid);
     uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
-    build_norm_bop<kHidden>(bop, sA, rsqrtf(ss / (float)kHidden + kRmsEps), nw, tid);
-    consumer_sync();
     const Range R = gu_rows(c.cta, c.ncta);
-    tc_phase<kTcGU>((R.end - R.begin + kGUTileRows - 1) / kGUTileRows, bop, [&](int t, int r, float gs, float us) {
-      const int row = R.begin + t * kGUTileRows + r;
-      if (row < R.end) {
-        const float silu = gs * fast_rcp(1.0f + fast_exp2(-gs * kLog2e));
-        put(c.wM + row, ll_pack(silu * us, E));
-      }
-    });
+    tc_prewait(R.begin, R.end, kGUTileRows);
+    const float ss = stage_vec<kHidden, kStageNormFrag>(c, sA, bop, c.wA, E, kSiteA, red_a, nw);
+    trace_stamp(c, tid == 0, l * 16 + 8);
+    const TcJob job{kTcGU, kOutGU, R.begin, R.end, kGUTileRows, rsqrtf(ss / (float)kHidden + kRmsEps), E};
+    tc_phase(job, bop);
     flush();
-    consumer_sync();  // the fragments in sU are overwritten by the next phase
+    consumer_sync();  // the B operand in sU is overwritten by the next phase
     trace_stamp(c, tid == 0, l * 16 + 9);
   }
 
   // P5: down rows + residual -> X words (next layer's input).
   __device__ void phase_down(const LDGLayerWeights &w, unsigned E, int l) {
     uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
-    stage_vec<kInter, kStageFrag>(c, nullptr, bop, c.wM, E, kSiteM, nullptr);
-    trace_stamp(c, tid == 0, l * 16 + 10);
     const Range R = d_rows(c.cta, c.ncta);
-    tc_phase<kTcQuarter>((R.end - R.begin + kDTileRows - 1) / kDTileRows, bop, [&](int t, int r, float v, float) {
-      const int row = R.begin + t * kDTileRows + r;
-      if (row < R.end) put(c.wX + row, ll_pack(v + sA[row], E));
-    });
+    tc_prewait(R.begin, R.end, kDTileRows);
+    stage_vec<kInter, kStageFrag>(c, nullptr, bop, c.wM, E, kSiteM, nullptr, NormPairs{});
+    trace_stamp(c, tid == 0, l * 16 + 10);
+    const TcJob job{kTcQuarter, kOutDown, R.begin, R.end, kDTileRows, 1.f, E};
+    tc_phase(job, bop);
     flush();
-    consumer_sync();  // sU (fragments) is reused by the next phase
+    consumer_sync();  // sU (B operand) is reused by the next phase
     trace_stamp(c, tid == 0, l * 16 + 11);
   }
 
@@ -1271,32 +1317,24 @@ struct Consumer {
           st_release_u32(&c.ctrl->kv_ready[l * kNumKVHeads + g], epoch_of(c, step, l, p.num_layers));
     }
     kv_written = 0;
-    NormPrefetch<kHidden> nw;
-    nw.load(p.final_norm, tid);
-    const float ss = stage_vec<kHidden, kStageSumSq>(c, sX, nullptr, c.wX, E_x, kSiteX, red_lm);
+    const NormPairs nw = load_norm_pairs(p.final_norm, tid);
+    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
+    const Range R = lm_rows(c.cta, c.ncta);
+    tc_prewait(R.begin, R.end, kLMTileRows);
+    const float ss = stage_vec<kHidden, kStageNormFrag>(c, sX, bop, c.wX, E_x, kSiteX, red_lm, nw);
     trace_stamp(c, tid == 0, p.num_layers * 16 + 0);
     const float rstd = rsqrtf(ss / (float)kHidden + kRmsEps);
-    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
-    build_norm_bop<kHidden>(bop, sX, rstd, nw, tid);
     if (p.final_hidden && c.cta == 0 && step == p.num_steps - 1 && live()) {
       for (int i = tid; i < kHidden; i += kConsumerThreads)
         p.final_hidden[i] = (sX[i] * rstd) * __bfloat162float(p.final_norm[i]);
     }
-    consumer_sync();
-    float best = -INFINITY;
-    int best_i = 0x7fffffff;
-    float *logits = p.logits ? (p.logits + (size_t)step * kVocab) : nullptr;
-    const Range R = lm_rows(c.cta, c.ncta);
-    tc_phase<kTcRow>((R.end - R.begin + kLMTileRows - 1) / kLMTileRows, bop, [&](int t, int r, float v, float) {
-      const int row = R.begin + t * kLMTileRows + r;
-      if (row < R.end) {
-        if (v > best || (v == best && row < best_i)) {
-          best = v;
-          best_i = row;
-        }
-        if (logits) logits[row] = v;
-      }
-    });
+    lm_best = -INFINITY;
+    lm_best_i = 0x7fffffff;
+    lm_logits = p.logits ? (p.logits + (size_t)step * kVocab) : nullptr;
+    const TcJob job{kTcRow, kOutLM, R.begin, R.end, kLMTileRows, rstd, E};
+    tc_phase(job, bop);
+    float best = lm_best;
+    int best_i = lm_best_i;
     // warp argmax (largest value, lowest row on ties)
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
