@@ -415,6 +415,29 @@ def run_ours(args):
     return 0
 
 
+def run_profile_case(steps: int) -> int:
+    """Small case for ncu captures: the bench model and prompt, one prefill
+    launch (positions 0..1022), then ONE decode launch of `steps` tokens at
+    ctx ~1k (the launch to capture: ncu -k regex:decode_kernel -s 1 -c 1)."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from qwen_megakernel_b200 import Decoder
+    from qwen_megakernel_b200.weights import random_weights
+
+    weights = random_weights(seed=0, device="cuda", max_seq_len=2048)
+    dec = Decoder(weights, max_seq_len=2048)
+    prompt = prompt_for_rank(0)
+    dec.prefill(prompt[:-1])
+    first = torch.tensor([prompt[-1]], dtype=torch.int32, device=dev)
+    log = torch.empty(steps, dtype=torch.int32, device=dev)
+    dec.decode_steps(steps, forced_tokens=first, start_position=PROMPT_LEN - 1, output_log=log)
+    torch.cuda.synchronize(dev)
+    dec.check_status()
+    print(json.dumps({"profile_case": {"steps": steps, "tokens": log[:4].tolist(),
+                                       "max_memory_gb": round(torch.cuda.max_memory_allocated() / 1e9, 3)}}))
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -422,7 +445,11 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", type=int, default=0, metavar="STEPS",
+                    help="run only the small ncu case: one decode launch of STEPS tokens")
     args = ap.parse_args(argv)
+    if args.profile_case:
+        return run_profile_case(args.profile_case)
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_ours(args)
