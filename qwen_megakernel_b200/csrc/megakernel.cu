@@ -353,6 +353,36 @@ __device__ __forceinline__ void store_bop_pair(uint8_t *bop, int e, float v0, fl
   *reinterpret_cast<uint32_t *>(q + 1024) = lo;
 }
 
+// r[q] for a per-lane q in [0, 8), as a tree of selects (no local memory).
+__device__ __forceinline__ float sel8(const uint32_t *r, int q) {
+  const uint32_t a0 = (q & 1) ? r[1] : r[0], a1 = (q & 1) ? r[3] : r[2];
+  const uint32_t a2 = (q & 1) ? r[5] : r[4], a3 = (q & 1) ? r[7] : r[6];
+  const uint32_t b0 = (q & 2) ? a1 : a0, b1 = (q & 2) ? a3 : a2;
+  return __uint_as_float((q & 4) ? b1 : b0);
+}
+
+// This lane's diagonal entry pair (hi + lo) of a GEMV accumulator with S
+// slots at TMEM address taddr: columns 16*slot + q and 16*slot + 8 + q.
+// All columns a warp needs are loaded with one wait.
+template <int S>
+__device__ __forceinline__ float tc_read(uint32_t taddr, int slot, int q) {
+  if (S == 1) {
+    uint32_t r[16];
+    tmem_ld16(taddr, r);
+    return sel8(r, q) + sel8(r + 8, q);
+  } else {
+    uint32_t r[32];
+    tmem_ld32(taddr, r);
+    float v = (slot == 0) ? sel8(r, q) + sel8(r + 8, q) : sel8(r + 16, q) + sel8(r + 24, q);
+    if (S == 3) {
+      uint32_t r2[16];
+      tmem_ld16(taddr + 32u, r2);
+      if (slot == 2) v = sel8(r2, q) + sel8(r2 + 8, q);
+    }
+    return v;
+  }
+}
+
 // ------------------------------------------------------------- LL staging
 enum StageMode : int {
   kStageSumSq = 1,     // fp32 copy into dst, returns sum of squares of the vector
@@ -915,25 +945,7 @@ struct Consumer {
           for (int hp = 0; hp < 2; ++hp) {
             const uint32_t taddr =
                 c.tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)kTmemBufCols * ((seq + (unsigned)hp) % kTmemBufs);
-            // this lane's diagonal pair: columns 16*slot + q (hi) and + 8 (lo)
-            for (int s0 = 0; s0 < S; s0 += 2) {
-              if (S - s0 >= 2) {
-                uint32_t r[32];
-                tmem_ld32(taddr + 16u * (uint32_t)s0, r);
-#pragma unroll
-                for (int ss = 0; ss < 2; ++ss)
-#pragma unroll
-                  for (int col = 0; col < 8; ++col)
-                    if (s0 + ss == slot && col == q)
-                      v += __uint_as_float(r[16 * ss + col]) + __uint_as_float(r[16 * ss + 8 + col]);
-              } else {
-                uint32_t r[16];
-                tmem_ld16(taddr + 16u * (uint32_t)s0, r);
-#pragma unroll
-                for (int col = 0; col < 8; ++col)
-                  if (s0 == slot && col == q) v += __uint_as_float(r[col]) + __uint_as_float(r[8 + col]);
-              }
-            }
+            v += (S == 1) ? tc_read<1>(taddr, slot, q) : (S == 2) ? tc_read<2>(taddr, slot, q) : tc_read<3>(taddr, slot, q);
           }
           if (!valid) v = 0.f;
         }
