@@ -783,6 +783,7 @@ struct Consumer {
   float *lm_logits = nullptr;
   unsigned mma_issued = 0;   // issuer threads: 1 + the last unit this thread issued
   bool tc_prewaited = false; // issuer threads: the next phase's first unit needs no waits
+  NormPairs nw_pref;         // RMSNorm weights of the next normalized GEMV input
   int warp, lane, tid;
   uint64_t kv_written = 0;  // layers whose new K/V row this CTA wrote this step
 
@@ -1013,7 +1014,7 @@ struct Consumer {
   // x_flag: epoch of the X words to stage, or 0 when sX already holds the
   // layer input (the embedding row of layer 0) and x_ss its sum of squares.
   __device__ void phase_qkv(const LDGLayerWeights &w, unsigned E, int l, unsigned x_flag, float x_ss) {
-    const NormPairs nw = load_norm_pairs((const __nv_bfloat16 *)w.input_layernorm_weight, tid);
+    const NormPairs nw = nw_pref;  // fetched one phase ahead
     uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
     const Range R = qkv_rows(c.cta, c.ncta);
     tc_prewait(R.begin, R.end, kQKVTileRows);
@@ -1275,6 +1276,8 @@ struct Consumer {
 
   // P3: O-projection rows + residual -> A words.
   __device__ void phase_o(const LDGLayerWeights &w, unsigned E, bool stall, int l) {
+    // RMSNorm weights of P4, fetched now so that their latency is hidden.
+    nw_pref = load_norm_pairs((const __nv_bfloat16 *)w.post_attn_layernorm_weight, tid);
     uint8_t *bop = reinterpret_cast<uint8_t *>(sAtt);
     const Range R = o_rows(c.cta, c.ncta);
     tc_prewait(R.begin, R.end, kOTileRows);
@@ -1289,7 +1292,7 @@ struct Consumer {
 
   // P4: RMSNorm(a) then gate/up rows, SiLU(gate) * up -> M words.
   __device__ void phase_gate_up(const LDGLayerWeights &w, unsigned E, int l) {
-    const NormPairs nw = load_norm_pairs((const __nv_bfloat16 *)w.post_attn_layernorm_weight, tid);
+    const NormPairs nw = nw_pref;  // fetched in P3
     uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
     const Range R = gu_rows(c.cta, c.ncta);
     tc_prewait(R.begin, R.end, kGUTileRows);
@@ -1304,6 +1307,9 @@ struct Consumer {
 
   // P5: down rows + residual -> X words (next layer's input).
   __device__ void phase_down(const LDGLayerWeights &w, unsigned E, int l) {
+    // RMSNorm weights of the next P1 (or of the final norm), fetched now.
+    nw_pref = load_norm_pairs(
+        (l + 1 < p.num_layers) ? (const __nv_bfloat16 *)p.layers[l + 1].input_layernorm_weight : p.final_norm, tid);
     uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
     const Range R = d_rows(c.cta, c.ncta);
     tc_prewait(R.begin, R.end, kDTileRows);
@@ -1329,7 +1335,7 @@ struct Consumer {
           st_release_u32(&c.ctrl->kv_ready[l * kNumKVHeads + g], epoch_of(c, step, l, p.num_layers));
     }
     kv_written = 0;
-    const NormPairs nw = load_norm_pairs(p.final_norm, tid);
+    const NormPairs nw = nw_pref;  // fetched in the last P5
     uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
     const Range R = lm_rows(c.cta, c.ncta);
     tc_prewait(R.begin, R.end, kLMTileRows);
@@ -1414,6 +1420,7 @@ struct Consumer {
         const int prev = read_argmax(c, epoch_of(c, t - 1, L, L));
         if (tid == 0 && live() && p.out_log) p.out_log[t - 1] = prev;
       }
+      nw_pref = load_norm_pairs((const __nv_bfloat16 *)p.layers[0].input_layernorm_weight, tid);
       const int tok = step_token(t);
       // Layer-0 input: the embedding row (bf16 -> fp32) and its sum of squares.
       float x_ss;
