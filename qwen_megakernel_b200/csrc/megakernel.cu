@@ -1127,38 +1127,55 @@ struct Consumer {
     }
     float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
     float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
-    // Online softmax over cache positions; two positions per step so their
-    // dot-product reductions and exponentials overlap.  `wb` = 0 disables
-    // the second position.
-    auto accumulate2 = [&](const float (&ka)[4], const float (&va)[4], const float (&kb)[4],
-                           const float (&vb)[4], bool has_b) {
-      float sa0 = q0[0] * ka[0] + q0[1] * ka[1] + q0[2] * ka[2] + q0[3] * ka[3];
-      float sa1 = q1[0] * ka[0] + q1[1] * ka[1] + q1[2] * ka[2] + q1[3] * ka[3];
-      float sb0 = q0[0] * kb[0] + q0[1] * kb[1] + q0[2] * kb[2] + q0[3] * kb[3];
-      float sb1 = q1[0] * kb[0] + q1[1] * kb[1] + q1[2] * kb[2] + q1[3] * kb[3];
+    // Online softmax over cache positions; NP positions per step so that
+    // their dot-product reductions and exponentials overlap.  Positions
+    // p >= nv of a step are masked.
+    auto accumulate = [&](auto &kk, auto &vv, int nv) {
+      constexpr int NP = sizeof(kk) / sizeof(kk[0]);
+      float sc[NP][2];
+#pragma unroll
+      for (int q = 0; q < NP; ++q) {
+        sc[q][0] = q0[0] * kk[q][0] + q0[1] * kk[q][1] + q0[2] * kk[q][2] + q0[3] * kk[q][3];
+        sc[q][1] = q1[0] * kk[q][0] + q1[1] * kk[q][1] + q1[2] * kk[q][2] + q1[3] * kk[q][3];
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
-        sa0 += __shfl_xor_sync(0xffffffffu, sa0, o);
-        sa1 += __shfl_xor_sync(0xffffffffu, sa1, o);
-        sb0 += __shfl_xor_sync(0xffffffffu, sb0, o);
-        sb1 += __shfl_xor_sync(0xffffffffu, sb1, o);
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+          sc[q][0] += __shfl_xor_sync(0xffffffffu, sc[q][0], o);
+          sc[q][1] += __shfl_xor_sync(0xffffffffu, sc[q][1], o);
+        }
       }
-      if (!has_b) {
-        sb0 = -INFINITY;
-        sb1 = -INFINITY;
+      float n0 = m0, n1 = m1;
+#pragma unroll
+      for (int q = 0; q < NP; ++q) {
+        if (q >= nv) sc[q][0] = sc[q][1] = -INFINITY;
+        n0 = fmaxf(n0, sc[q][0]);
+        n1 = fmaxf(n1, sc[q][1]);
       }
-      const float n0 = fmaxf(m0, fmaxf(sa0, sb0)), n1 = fmaxf(m1, fmaxf(sa1, sb1));
       const float c0 = fast_exp2(m0 - n0), c1 = fast_exp2(m1 - n1);
-      const float pa0 = fast_exp2(sa0 - n0), pa1 = fast_exp2(sa1 - n1);
-      const float pb0 = fast_exp2(sb0 - n0), pb1 = fast_exp2(sb1 - n1);
-      l0 = l0 * c0 + pa0 + pb0;
-      l1 = l1 * c1 + pa1 + pb1;
+      float pr[NP][2];
+      l0 *= c0;
+      l1 *= c1;
+#pragma unroll
+      for (int q = 0; q < NP; ++q) {
+        pr[q][0] = fast_exp2(sc[q][0] - n0);
+        pr[q][1] = fast_exp2(sc[q][1] - n1);
+        l0 += pr[q][0];
+        l1 += pr[q][1];
+      }
       m0 = n0;
       m1 = n1;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        o0[e] = o0[e] * c0 + pa0 * va[e] + pb0 * vb[e];
-        o1[e] = o1[e] * c1 + pa1 * va[e] + pb1 * vb[e];
+        float a0 = o0[e] * c0, a1 = o1[e] * c1;
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+          a0 = fmaf(pr[q][0], vv[q][e], a0);
+          a1 = fmaf(pr[q][1], vv[q][e], a1);
+        }
+        o0[e] = a0;
+        o1[e] = a1;
       }
     };
     auto load_kv = [&](const uint8_t *kt, const uint8_t *vt, int j, float (&kf)[4], float (&vf)[4]) {
@@ -1173,26 +1190,26 @@ struct Consumer {
       if (ok) {
         const uint8_t *kt = slot_ptr(c, tile);
         const uint8_t *vt = kt + kKVTileVOffset;
-        for (int j = warp; j < n; j += 2 * kConsumerWarps) {
-          const int jb = j + kConsumerWarps;
-          const bool has_b = jb < n;
-          float ka[4], va[4], kb[4], vb[4];
-          load_kv(kt, vt, j, ka, va);
-          load_kv(kt, vt, has_b ? jb : j, kb, vb);
-          accumulate2(ka, va, kb, vb, has_b);
+        constexpr int NP = 4;
+        for (int j = warp; j < n; j += NP * kConsumerWarps) {
+          float kk[NP][4], vv[NP][4];
+          const int nv = min(NP, (n - j + kConsumerWarps - 1) / kConsumerWarps);
+#pragma unroll
+          for (int q = 0; q < NP; ++q) load_kv(kt, vt, (q < nv) ? j + q * kConsumerWarps : j, kk[q], vv[q]);
+          accumulate(kk, vv, nv);
         }
       }
       release_tile(c, tile, ok);
       ++tile;
     }
     if (last && warp == 0) {
-      float kf[4], vf[4];
+      float kf[1][4], vf[1][4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        kf[e] = sU[kUKn + d0 + e];
-        vf[e] = sU[kUVn + d0 + e];
+        kf[0][e] = sU[kUKn + d0 + e];
+        vf[0][e] = sU[kUVn + d0 + e];
       }
-      accumulate2(kf, vf, kf, vf, false);
+      accumulate(kf, vf, 1);
     }
     // Cross-warp merge of the online-softmax states -> PART words.
     float *pw = sPW + warp * kPartWords;
