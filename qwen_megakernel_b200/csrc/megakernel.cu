@@ -1341,17 +1341,6 @@ struct Consumer {
 
   // Final RMSNorm + LM head rows + CTA argmax -> ARG words.
   __device__ void phase_lm_head(int step, unsigned E_x, unsigned E) {
-    // Publish this step's K/V rows for the next step's TMA reads: one
-    // gpu-scope fence orders every row written since (the CTA synchronized
-    // with their writers at the named barriers in between), then the flags.
-    if (kv_written && tid == 0 && live()) {
-      __threadfence();
-      const int g = item_of_cta(c.cta, p.splits) / p.splits;
-      for (int l = 0; l < p.num_layers; ++l)
-        if (kv_written & (1ull << l))
-          st_release_u32(&c.ctrl->kv_ready[l * kNumKVHeads + g], epoch_of(c, step, l, p.num_layers));
-    }
-    kv_written = 0;
     const NormPairs nw = nw_pref;  // fetched in the last P5
     uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
     const Range R = lm_rows(c.cta, c.ncta);
@@ -1406,6 +1395,18 @@ struct Consumer {
     }
     flush();
     consumer_sync();
+    // Publish this step's K/V rows for the next step's TMA reads, after the
+    // ARG words (off the step's critical path): one gpu-scope fence orders
+    // every row written since (the CTA synchronized with their writers at
+    // the named barriers in between), then the flags as relaxed stores.
+    if (kv_written && tid == 0 && live()) {
+      __threadfence();
+      const int g = item_of_cta(c.cta, p.splits) / p.splits;
+      for (int l = 0; l < p.num_layers; ++l)
+        if (kv_written & (1ull << l))
+          st_relaxed_u32(&c.ctrl->kv_ready[l * kNumKVHeads + g], epoch_of(c, step, l, p.num_layers));
+    }
+    kv_written = 0;
     trace_stamp(c, tid == 0, p.num_layers * 16 + 1);
   }
 

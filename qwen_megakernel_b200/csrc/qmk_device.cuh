@@ -207,6 +207,9 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
 __device__ __forceinline__ void st_release_u32(unsigned *p, unsigned v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_relaxed_u32(unsigned *p, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ unsigned ld_volatile_u32(const unsigned *p) {
   return *reinterpret_cast<const volatile unsigned *>(p);
 }
