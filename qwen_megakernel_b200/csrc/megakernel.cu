@@ -119,8 +119,8 @@ static_assert(kSmBytes <= 232448, "shared memory plan exceeds the sm_100 per-blo
 constexpr int kUQ = 0;      // q, 2 heads [256]
 constexpr int kUK = 256;    // k [128]
 constexpr int kUV = 384;    // v [128]
-constexpr int kUKn = 512;   // new k after norm/RoPE, bf16-rounded [128]
-constexpr int kUVn = 640;   // new v, bf16-rounded [128]
+constexpr int kUKn = 512;   // new k after norm/RoPE, one bf16 cache row (256 B)
+constexpr int kUVn = 640;   // new v, one bf16 cache row (256 B)
 constexpr int kUPW = 768;   // per-warp partials [8][260]
 static_assert(kUPW + kConsumerWarps * kPartWords <= kInter, "attention scratch too large");
 static_assert(kMaxSplits * kMergeWordsPerSplit <= kInter, "merge scratch too large");
@@ -810,18 +810,22 @@ struct Consumer {
   // Issue the 4 MMAs of M block hp of ring tile `tl` (tensor-core unit
   // number seq) into TMEM buffer seq % kTmemBufs, against the B operand at
   // bop with S slots.  Layout of A, B and D: see the GEMV section above.
+  // Called by a whole issuer warp: lane 0 waits (unless `waited`: its
+  // pre-wait already did), one elected lane issues.  A K step of 16 moves
+  // both descriptors' start address by 32 bytes (2 in the 16-byte field).
   __device__ bool tc_issue_unit(uint32_t tl, int hp, unsigned seq, const uint8_t *bop, int S, bool waited) {
     const uint32_t idesc = mma_idesc_bf16(128, 16 * S);
     const unsigned b = seq % kTmemBufs;
-    if (!waited && !tc_unit_waits(tl, seq)) return false;
+    bool ok = true;
+    if (lane == 0 && !waited) ok = tc_unit_waits(tl, seq);
+    if (!__shfl_sync(0xffffffffu, (int)ok, 0)) return false;
     tc_fence_after_sync();
-    const uint32_t a0 = smem_addr(slot_ptr(c, tl)) + 1024u * (uint32_t)hp;
-    const uint32_t b0 = smem_addr(bop) + 2048u * (uint32_t)(S * hp);
+    const uint64_t ad = smem_desc_sw128(smem_addr(slot_ptr(c, tl)) + 1024u * (uint32_t)hp, 2048u);
+    const uint64_t bd = smem_desc_sw128(smem_addr(bop) + 2048u * (uint32_t)(S * hp), 1024u);
     const uint32_t d = c.tmem + (uint32_t)kTmemBufCols * b;
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
-      tc_mma_bf16(d, smem_desc_sw128(a0 + 32u * kk, 2048u), smem_desc_sw128(b0 + 32u * kk, 1024u), idesc, kk > 0);
-    tc_commit(&c.mma_bar[b]);
+    for (int kk = 0; kk < 4; ++kk) tc_mma_bf16_warp(d, ad + 2u * kk, bd + 2u * kk, idesc, kk > 0);
+    tc_commit_warp(&c.mma_bar[b]);
     mma_issued = seq + 1u;
     return true;
   }
@@ -899,9 +903,9 @@ struct Consumer {
   }
 
   // GEMV phase over the ring tiles of rows [r0, r1) on the tensor cores.
-  // A unit is one M block (4 MMAs); lane 0 of warps 4-6 issue the units
-  // round-robin (a single issuing thread is limited by the issue latency of
-  // tcgen05.mma), up to kTmemBufs units in flight; warps 0-3 read both units
+  // A unit is one M block (4 MMAs); warps 4-6 issue the units round-robin
+  // (one issuer is limited by the issue latency of tcgen05.mma), up to
+  // kTmemBufs units in flight; warps 0-3 read both units
   // of a tile (one TMEM lane each), add the diagonal entries of every output
   // row with warp shuffles and emit each row from one lane.
   //   kTcRow     K = 1024, 16 rows
@@ -915,7 +919,7 @@ struct Consumer {
     constexpr int kIssuers = kConsumerWarps - 4;
     const unsigned seq0 = mma_seq;
     const int nunits = 2 * ntiles;
-    if (warp >= 4 && lane == 0) {
+    if (warp >= 4) {
       bool ok = live();
       for (int u = warp - 4; u < nunits && ok; u += kIssuers)
         ok = tc_issue_unit(tile + (uint32_t)(u >> 1), u & 1, seq0 + (unsigned)u, bop, S,
@@ -1093,24 +1097,23 @@ struct Consumer {
 #pragma unroll
         for (int e = 0; e < 4; ++e) vec[d0 + e] = y[e] * qs;
       } else {
-        // New K/V row of this position: bf16 into the cache and (rounded) into smem.
+        // New K/V row of this position, bf16: into the cache and, in the
+        // cache's row format, into smem for this step's softmax.
         const size_t off =
             (((size_t)layer * kNumKVHeads + g) * (size_t)p.max_seq_len + pos) * kHeadDim + d0;
         unsigned kbits[4], vbits[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const __nv_bfloat16 kb = __float2bfloat16(y[e]);
-          const __nv_bfloat16 vb = __float2bfloat16(sU[kUV + d0 + e]);
-          kbits[e] = __bfloat16_as_ushort(kb);
-          vbits[e] = __bfloat16_as_ushort(vb);
-          sU[kUKn + d0 + e] = __bfloat162float(kb);
-          sU[kUVn + d0 + e] = __bfloat162float(vb);
+          kbits[e] = __bfloat16_as_ushort(__float2bfloat16(y[e]));
+          vbits[e] = __bfloat16_as_ushort(__float2bfloat16(sU[kUV + d0 + e]));
         }
+        const uint2 kw = make_uint2(kbits[0] | (kbits[1] << 16), kbits[2] | (kbits[3] << 16));
+        const uint2 vw = make_uint2(vbits[0] | (vbits[1] << 16), vbits[2] | (vbits[3] << 16));
+        reinterpret_cast<uint2 *>(sU + kUKn)[lane] = kw;
+        reinterpret_cast<uint2 *>(sU + kUVn)[lane] = vw;
         if (live()) {
-          *reinterpret_cast<uint2 *>(p.k_cache + off) =
-              make_uint2(kbits[0] | (kbits[1] << 16), kbits[2] | (kbits[3] << 16));
-          *reinterpret_cast<uint2 *>(p.v_cache + off) =
-              make_uint2(vbits[0] | (vbits[1] << 16), vbits[2] | (vbits[3] << 16));
+          *reinterpret_cast<uint2 *>(p.k_cache + off) = kw;
+          *reinterpret_cast<uint2 *>(p.v_cache + off) = vw;
         }
       }
     }
@@ -1119,132 +1122,192 @@ struct Consumer {
     // phase, off the critical path: only the next step's producers read it.
     if (last) kv_written |= 1ull << layer;
 
-    float q0[4], q1[4];
+    // Online softmax over cache positions.  Group gq = lane / 8 of a warp
+    // takes one position per step; lane r8 = lane % 8 of the group holds dims
+    // [8 r8, 8 r8 + 8) and [64 + 8 r8, 64 + 8 r8 + 8) of both q heads
+    // (16-byte shared-memory reads, one 128-byte line per 8 lanes), so a
+    // score is 16 FMAs per head and a 3-level butterfly.  Of a tile, warp w
+    // takes positions 28 t + 4 w + gq (t < kSteps) and moves its running max
+    // once; the four groups share that max, so their sums add without
+    // rescaling at the end.
+    const int gq = lane >> 3, r8 = lane & 7;
+    float qv[2][16];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      q0[e] = sQ[d0 + e];
-      q1[e] = sQ[kHeadDim + d0 + e];
+    for (int h = 0; h < 2; ++h) {
+      const float4 *qa = reinterpret_cast<const float4 *>(sQ + h * kHeadDim + 8 * r8);
+      const float4 *qb = reinterpret_cast<const float4 *>(sQ + h * kHeadDim + 64 + 8 * r8);
+      const float4 v4[4] = {qa[0], qa[1], qb[0], qb[1]};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        qv[h][4 * k + 0] = v4[k].x;
+        qv[h][4 * k + 1] = v4[k].y;
+        qv[h][4 * k + 2] = v4[k].z;
+        qv[h][4 * k + 3] = v4[k].w;
+      }
     }
-    float m0 = -INFINITY, l0 = 0.f, m1 = -INFINITY, l1 = 0.f;
-    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
-    // Online softmax over cache positions; NP positions per step so that
-    // their dot-product reductions and exponentials overlap.  Positions
-    // p >= nv of a step are masked.
-    auto accumulate = [&](auto &kk, auto &vv, int nv) {
-      constexpr int NP = sizeof(kk) / sizeof(kk[0]);
-      float sc[NP][2];
+    float mrun[2] = {-INFINITY, -INFINITY}, lrun[2] = {0.f, 0.f};
+    float oacc[2][16];
 #pragma unroll
-      for (int q = 0; q < NP; ++q) {
-        sc[q][0] = q0[0] * kk[q][0] + q0[1] * kk[q][1] + q0[2] * kk[q][2] + q0[3] * kk[q][3];
-        sc[q][1] = q1[0] * kk[q][0] + q1[1] * kk[q][1] + q1[2] * kk[q][2] + q1[3] * kk[q][3];
-      }
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
+      for (int e = 0; e < 16; ++e) oacc[h][e] = 0.f;
+    constexpr int kStride = 4 * kConsumerWarps;
+    constexpr int kSteps = (kKVTilePos + kStride - 1) / kStride;
+    // Rows j < n: K at kt + 256 j, V at vt + 256 j (bf16, 128 dims each).
+    auto absorb = [&](const uint8_t *kt, const uint8_t *vt, int n) {
+      if (4 * warp >= n) return;  // warp-uniform: no position of this warp
+      int jr[kSteps];
+      bool ok[kSteps];
+      float s[kSteps][2];
 #pragma unroll
-        for (int q = 0; q < NP; ++q) {
-          sc[q][0] += __shfl_xor_sync(0xffffffffu, sc[q][0], o);
-          sc[q][1] += __shfl_xor_sync(0xffffffffu, sc[q][1], o);
+      for (int t = 0; t < kSteps; ++t) {
+        const int j = kStride * t + 4 * warp + gq;
+        ok[t] = j < n;
+        jr[t] = ok[t] ? j : 4 * warp;
+        const uint8_t *row = kt + (size_t)jr[t] * (kHeadDim * 2) + 16 * r8;
+        const uint4 a = *reinterpret_cast<const uint4 *>(row);
+        const uint4 b = *reinterpret_cast<const uint4 *>(row + kHeadDim);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float *q = qv[h];
+          float s0 = q[0] * bf_lo(a.x), s1 = q[1] * bf_hi(a.x);
+          s0 = fmaf(q[2], bf_lo(a.y), s0);
+          s1 = fmaf(q[3], bf_hi(a.y), s1);
+          s0 = fmaf(q[4], bf_lo(a.z), s0);
+          s1 = fmaf(q[5], bf_hi(a.z), s1);
+          s0 = fmaf(q[6], bf_lo(a.w), s0);
+          s1 = fmaf(q[7], bf_hi(a.w), s1);
+          s0 = fmaf(q[8], bf_lo(b.x), s0);
+          s1 = fmaf(q[9], bf_hi(b.x), s1);
+          s0 = fmaf(q[10], bf_lo(b.y), s0);
+          s1 = fmaf(q[11], bf_hi(b.y), s1);
+          s0 = fmaf(q[12], bf_lo(b.z), s0);
+          s1 = fmaf(q[13], bf_hi(b.z), s1);
+          s0 = fmaf(q[14], bf_lo(b.w), s0);
+          s1 = fmaf(q[15], bf_hi(b.w), s1);
+          s[t][h] = s0 + s1;
         }
       }
-      float n0 = m0, n1 = m1;
+      uint4 va[kSteps], vb[kSteps];
 #pragma unroll
-      for (int q = 0; q < NP; ++q) {
-        if (q >= nv) sc[q][0] = sc[q][1] = -INFINITY;
-        n0 = fmaxf(n0, sc[q][0]);
-        n1 = fmaxf(n1, sc[q][1]);
+      for (int t = 0; t < kSteps; ++t) {
+        const uint8_t *row = vt + (size_t)jr[t] * (kHeadDim * 2) + 16 * r8;
+        va[t] = *reinterpret_cast<const uint4 *>(row);
+        vb[t] = *reinterpret_cast<const uint4 *>(row + kHeadDim);
       }
-      const float c0 = fast_exp2(m0 - n0), c1 = fast_exp2(m1 - n1);
-      float pr[NP][2];
-      l0 *= c0;
-      l1 *= c1;
 #pragma unroll
-      for (int q = 0; q < NP; ++q) {
-        pr[q][0] = fast_exp2(sc[q][0] - n0);
-        pr[q][1] = fast_exp2(sc[q][1] - n1);
-        l0 += pr[q][0];
-        l1 += pr[q][1];
-      }
-      m0 = n0;
-      m1 = n1;
+      for (int o = 1; o < 8; o <<= 1)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float a0 = o0[e] * c0, a1 = o1[e] * c1;
-#pragma unroll
-        for (int q = 0; q < NP; ++q) {
-          a0 = fmaf(pr[q][0], vv[q][e], a0);
-          a1 = fmaf(pr[q][1], vv[q][e], a1);
+        for (int t = 0; t < kSteps; ++t) {
+          s[t][0] += __shfl_xor_sync(0xffffffffu, s[t][0], o);
+          s[t][1] += __shfl_xor_sync(0xffffffffu, s[t][1], o);
         }
-        o0[e] = a0;
-        o1[e] = a1;
+      float mn[2] = {mrun[0], mrun[1]};
+#pragma unroll
+      for (int t = 0; t < kSteps; ++t) {
+        if (!ok[t]) s[t][0] = s[t][1] = -INFINITY;
+        mn[0] = fmaxf(mn[0], s[t][0]);
+        mn[1] = fmaxf(mn[1], s[t][1]);
       }
-    };
-    auto load_kv = [&](const uint8_t *kt, const uint8_t *vt, int j, float (&kf)[4], float (&vf)[4]) {
-      const uint2 kw = *reinterpret_cast<const uint2 *>(kt + (size_t)j * 256 + 8 * lane);
-      const uint2 vw = *reinterpret_cast<const uint2 *>(vt + (size_t)j * 256 + 8 * lane);
-      kf[0] = bf_lo(kw.x); kf[1] = bf_hi(kw.x); kf[2] = bf_lo(kw.y); kf[3] = bf_hi(kw.y);
-      vf[0] = bf_lo(vw.x); vf[1] = bf_hi(vw.x); vf[2] = bf_lo(vw.y); vf[3] = bf_hi(vw.y);
+#pragma unroll
+      for (int o = 8; o < 32; o <<= 1) {
+        mn[0] = fmaxf(mn[0], __shfl_xor_sync(0xffffffffu, mn[0], o));
+        mn[1] = fmaxf(mn[1], __shfl_xor_sync(0xffffffffu, mn[1], o));
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float corr = fast_exp2(mrun[h] - mn[h]);  // 0 while mrun is -inf
+        float pt[kSteps];
+        float l = lrun[h] * corr;
+#pragma unroll
+        for (int t = 0; t < kSteps; ++t) {
+          pt[t] = fast_exp2(s[t][h] - mn[h]);  // 0 for masked positions
+          l += pt[t];
+        }
+        lrun[h] = l;
+        mrun[h] = mn[h];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) oacc[h][e] *= corr;
+#pragma unroll
+        for (int t = 0; t < kSteps; ++t) {
+          const unsigned w[8] = {va[t].x, va[t].y, va[t].z, va[t].w, vb[t].x, vb[t].y, vb[t].z, vb[t].w};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            oacc[h][2 * k] = fmaf(pt[t], bf_lo(w[k]), oacc[h][2 * k]);
+            oacc[h][2 * k + 1] = fmaf(pt[t], bf_hi(w[k]), oacc[h][2 * k + 1]);
+          }
+        }
+      }
     };
     for (int j0 = ch.begin; j0 < ch.end; j0 += kKVTilePos) {
       const int n = min(kKVTilePos, ch.end - j0);
       const bool ok = wait_full(c, tile);
       if (ok) {
         const uint8_t *kt = slot_ptr(c, tile);
-        const uint8_t *vt = kt + kKVTileVOffset;
-        constexpr int NP = 4;
-        for (int j = warp; j < n; j += NP * kConsumerWarps) {
-          float kk[NP][4], vv[NP][4];
-          const int nv = min(NP, (n - j + kConsumerWarps - 1) / kConsumerWarps);
-#pragma unroll
-          for (int q = 0; q < NP; ++q) load_kv(kt, vt, (q < nv) ? j + q * kConsumerWarps : j, kk[q], vv[q]);
-          accumulate(kk, vv, nv);
-        }
+        absorb(kt, kt + kKVTileVOffset, n);
       }
       release_tile(c, tile, ok);
       ++tile;
     }
-    if (last && warp == 0) {
-      float kf[1][4], vf[1][4];
+    // The new position (last split): its bf16 K/V rows were staged in smem.
+    if (last) absorb(reinterpret_cast<const uint8_t *>(sU + kUKn), reinterpret_cast<const uint8_t *>(sU + kUVn), 1);
+
+    // Groups -> warp by a reduce-scatter: afterwards lane (gq, r8) holds
+    // head gq & 1, dims [base, base + 8) with base = 8 r8 + 64 (gq >> 1).
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        kf[0][e] = sU[kUKn + d0 + e];
-        vf[0][e] = sU[kUVn + d0 + e];
-      }
-      accumulate(kf, vf, 1);
+    for (int o = 8; o < 32; o <<= 1) {
+      lrun[0] += __shfl_xor_sync(0xffffffffu, lrun[0], o);
+      lrun[1] += __shfl_xor_sync(0xffffffffu, lrun[1], o);
+    }
+    const bool hb = (gq & 1) != 0, db = (gq >> 1) != 0;
+    float keep[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float send = hb ? oacc[0][k] : oacc[1][k];
+      keep[k] = (hb ? oacc[1][k] : oacc[0][k]) + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float fin[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float send = db ? keep[k] : keep[8 + k];
+      fin[k] = (db ? keep[8 + k] : keep[k]) + __shfl_xor_sync(0xffffffffu, send, 16);
     }
     // Cross-warp merge of the online-softmax states -> PART words.
     float *pw = sPW + warp * kPartWords;
     if (lane == 0) {
-      pw[0] = m0;
-      pw[1] = l0;
-      pw[2] = m1;
-      pw[3] = l1;
+      pw[0] = mrun[0];
+      pw[1] = lrun[0];
+      pw[2] = mrun[1];
+      pw[3] = lrun[1];
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      pw[4 + d0 + e] = o0[e];
-      pw[4 + kHeadDim + d0 + e] = o1[e];
-    }
+    float4 *dst = reinterpret_cast<float4 *>(pw + 4 + (gq & 1) * kHeadDim + 64 * (gq >> 1) + 8 * r8);
+    dst[0] = make_float4(fin[0], fin[1], fin[2], fin[3]);
+    dst[1] = make_float4(fin[4], fin[5], fin[6], fin[7]);
     consumer_sync();
-    for (int i = tid; i < 2 * kHeadDim; i += kConsumerThreads) {
-      const int hh = i >> 7, d = i & 127;
+    // Thread i < 128: q head i / 64, dims 2 (i % 64) and 2 (i % 64) + 1.
+    if (tid < kHeadDim) {
+      const int hh = tid >> 6, d = 2 * (tid & 63);
       float M = -INFINITY;
 #pragma unroll
       for (int q = 0; q < kConsumerWarps; ++q) M = fmaxf(M, sPW[q * kPartWords + 2 * hh]);
-      float L = 0.f, O = 0.f;
+      float L = 0.f, O0 = 0.f, O1 = 0.f;
       if (M != -INFINITY) {
 #pragma unroll
         for (int q = 0; q < kConsumerWarps; ++q) {
           const float mq = sPW[q * kPartWords + 2 * hh];
           if (mq != -INFINITY) {
             const float f = fast_exp2(mq - M);
+            const float2 o = *reinterpret_cast<const float2 *>(sPW + q * kPartWords + 4 + hh * kHeadDim + d);
             L += sPW[q * kPartWords + 2 * hh + 1] * f;
-            O += sPW[q * kPartWords + 4 + hh * kHeadDim + d] * f;
+            O0 += o.x * f;
+            O1 += o.y * f;
           }
         }
       }
       if (live()) {
         uint64_t *part = c.wPart + (size_t)item * kPartWords;
-        put(part + 4 + hh * kHeadDim + d, ll_pack(O, E));
+        put(part + 4 + hh * kHeadDim + d, ll_pack(O0, E));
+        put(part + 4 + hh * kHeadDim + d + 1, ll_pack(O1, E));
         if (d == 0) {
           put(part + 2 * hh, ll_pack(M, E));
           put(part + 2 * hh + 1, ll_pack(L, E));
