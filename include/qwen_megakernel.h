@@ -248,6 +248,75 @@ int qmk_generate_static(int first_token_id, int num_steps, const void *embed_wei
  * block used by qmk_generate_static; either pointer may be NULL. */
 int qmk_static_scratch_ptrs(int **output_log, QmkStatus **status);
 
+/* ---- token-parallel path: prefill and batched decode ---------------------
+ * No counterpart in the reference, which processes a prompt one decode step
+ * per token (qwen_megakernel/model.py:210-211) and decodes batch 1 only.
+ * One call runs the whole model over `num_rows` rows at once: row r feeds
+ * token tokens[r] of sequence row_seq[r] at position row_pos[r], writes its
+ * K/V at that position of that sequence's cache and attends to positions
+ * [0, row_pos[r]] of it.  Rows of one sequence at consecutive positions are
+ * a causal prefill (every row sees the K/V the earlier rows write in the same
+ * call); one row per sequence is a batched decode step.  The projections are
+ * tensor-core GEMMs (cuBLAS, bf16 operands: activations as a bf16 hi + lo
+ * pair, fp32 accumulate, so they keep the decode kernel's fp32 precision);
+ * norms, QK-norm + RoPE + K/V append, attention, SiLU and argmax are this
+ * library's kernels.  Output rows out_rows[i] (i < num_out) get the final
+ * RMSNorm, the LM head and the greedy argmax (lowest index on ties).
+ *
+ * Caches: sequence s uses k_cache + s * kv_seq_stride (elements), layout
+ * bf16 [num_layers, 8, max_seq_len, 128] as above.  Token ids outside
+ * [0, vocab) read token 0, rows whose sequence or position is out of range
+ * are skipped; either sets a bit in *status (device uint32, optional):
+ * QMK_BATCH_BAD_TOKEN / QMK_BATCH_BAD_ROW.  All launches are stream-ordered
+ * and capturable in a CUDA graph (no allocation, no host sync). */
+#define QMK_BATCH_BAD_TOKEN 1u
+#define QMK_BATCH_BAD_ROW 2u
+
+typedef struct QmkBatchArgs {
+  const void *embed_weight;              /* bf16 [151936, 1024]                 */
+  const void *const *layer_ptrs;         /* HOST array [num_layers * 11] of the */
+                                         /* device pointers, LDGLayerWeights   */
+                                         /* order (the GEMMs are launched from */
+                                         /* the host)                          */
+  const void *const *fused_ptrs;         /* HOST array [num_layers * 2] or NULL:*/
+                                         /* per layer a bf16 [4096, 1024] copy  */
+                                         /* of q|k|v and a [6144, 1024] copy of */
+                                         /* gate|up (one GEMM each; NULL: the   */
+                                         /* separate matrices, 5 GEMMs)         */
+  const void *final_norm_weight;         /* bf16 [1024]                         */
+  const void *lm_head_weight;            /* bf16 [151936, 1024]                 */
+  const void *cos_table;                 /* bf16 [max_seq_len, 128]             */
+  const void *sin_table;
+  void *k_cache;                         /* bf16, see above                     */
+  void *v_cache;
+  long long kv_seq_stride;               /* elements between sequences' caches  */
+  int num_seqs;
+  int num_layers;
+  int max_seq_len;
+  float attn_scale;
+  int num_rows;                          /* 1 .. QMK_BATCH_MAX_ROWS             */
+  const int *tokens;                     /* device int32 [num_rows]             */
+  const int *row_seq;                    /* device int32 [num_rows]             */
+  const int *row_pos;                    /* device int32 [num_rows]             */
+  int num_out;                           /* 0 .. num_rows                       */
+  const int *out_rows;                   /* device int32 [num_out]              */
+  int *out_tokens;                       /* device int32 [num_out] or NULL      */
+  float *logits;                         /* device fp32 [num_out, 151936] or NULL*/
+  void *workspace;                       /* device, qmk_batch_workspace_bytes() */
+  size_t workspace_bytes;
+  unsigned int *status;                  /* device uint32 [1] or NULL           */
+} QmkBatchArgs;
+
+#define QMK_BATCH_MAX_ROWS 4096
+
+/* Device workspace bytes for num_rows rows and num_out output rows
+ * (256-byte aligned start required). */
+size_t qmk_batch_workspace_bytes(int num_rows, int num_out);
+
+/* Queue the forward pass on `stream`.  Returns QMK_OK or a host-side error
+ * (QMK_ERR_ARGS, QMK_ERR_WORKSPACE, QMK_ERR_CUDA). */
+int qmk_batch_forward(const QmkBatchArgs *args, cudaStream_t stream);
+
 /* Library version string. */
 const char *qmk_version(void);
 

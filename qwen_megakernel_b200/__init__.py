@@ -9,7 +9,20 @@ The native libraries are loaded on first use (``Decoder(...)`` or
 """
 
 from .model import Decoder, DecodeError, generate, load_weights, random_weights  # noqa: F401
+from .batch import BatchDecoder, BatchError, BatchForward  # noqa: F401
 from .weights import rope_tables  # noqa: F401
 from ._native import ops, cdll  # noqa: F401
 
-__all__ = ["load_weights", "random_weights", "rope_tables", "Decoder", "DecodeError", "generate", "ops", "cdll"]
+__all__ = [
+    "load_weights",
+    "random_weights",
+    "rope_tables",
+    "Decoder",
+    "DecodeError",
+    "BatchDecoder",
+    "BatchError",
+    "BatchForward",
+    "generate",
+    "ops",
+    "cdll",
+]

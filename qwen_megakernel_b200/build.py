@@ -1,7 +1,8 @@
 """In-tree build of the native libraries (sm_100a only, no JIT cache).
 
 Outputs, next to this file:
-  libqwen_megakernel.so   the C-ABI library (kernel + launchers), nvcc, static cudart
+  libqwen_megakernel.so   the C-ABI library (kernels + launchers), nvcc, static
+                          cudart, cuBLAS for the token-parallel path's GEMMs
   qwen_megakernel_C.so    the torch operator library (TORCH_LIBRARY qwen_megakernel_C)
 
 Mirrors the role of the reference's qwen_megakernel/build.py (JIT
@@ -44,6 +45,7 @@ NVCC_FLAGS = ARCH_FLAGS + [
 
 KERNEL_SOURCES = [
     os.path.join(CSRC, "megakernel.cu"),
+    os.path.join(CSRC, "batch.cu"),
 ]
 KERNEL_DEPS = KERNEL_SOURCES + [
     os.path.join(CSRC, "qmk_device.cuh"),
@@ -103,12 +105,20 @@ def _run(cmd: list[str], verbose: bool) -> None:
         raise RuntimeError(f"build command failed ({res.returncode}): {' '.join(cmd)}\n{msg}")
 
 
+def _link_flags() -> list[str]:
+    """cuBLAS (the token-parallel path's GEMMs).  torch loads its own
+    libcublas.so.12 first when it is imported; the rpath covers ctypes-only
+    use of the library."""
+    lib64 = os.path.join(_cuda_home(), "lib64")
+    return [f"-L{lib64}", "-lcublas", "-Xlinker", f"-rpath={lib64}"]
+
+
 def build_kernel_library(force: bool = False, verbose: bool = False) -> str:
-    if force or _stale(LIB_PATH, KERNEL_DEPS, NVCC_FLAGS):
+    if force or _stale(LIB_PATH, KERNEL_DEPS, NVCC_FLAGS + _link_flags()):
         tmp = LIB_PATH + ".tmp"
-        _run([_nvcc()] + NVCC_FLAGS + KERNEL_SOURCES + ["-o", tmp], verbose)
+        _run([_nvcc()] + NVCC_FLAGS + KERNEL_SOURCES + ["-o", tmp] + _link_flags(), verbose)
         os.replace(tmp, LIB_PATH)
-        _stamp(LIB_PATH, KERNEL_DEPS, NVCC_FLAGS)
+        _stamp(LIB_PATH, KERNEL_DEPS, NVCC_FLAGS + _link_flags())
     return LIB_PATH
 
 

@@ -1,0 +1,725 @@
+// Token-parallel forward pass (prefill of a prompt, batched decode of several
+// sequences) for Qwen3-0.6B on sm_100a.  Entry point: qmk_batch_forward
+// (include/qwen_megakernel.h).
+//
+// The decode megakernel streams every weight once per token; with M rows in
+// flight the projections become GEMMs [M, K] x [K, N] that reuse each weight
+// M times, so they go to the tensor cores through cuBLAS (plain GEMMs, bf16
+// operands, fp32 accumulation).  The fp32 activations are fed as a bf16 pair
+// x = hi + lo (lo = rounding remainder of hi): two GEMMs per projection keep
+// the products exact and the activation error at ~2^-17, the precision the
+// decode kernel keeps, so both paths agree with the fp32 oracle within the
+// same tolerance.  Everything between the GEMMs is fused into one kernel per
+// step: RMSNorm + split, QK-norm + RoPE + K/V append, attention (+ split of
+// its output), SiLU(gate) * up (+ split), final norm + argmax.
+//
+// Reference steps these kernels restate (AlpinDale/qwen_megakernel):
+//   RMSNorm eps 1e-6              csrc/kernel.cu:168-292 (ldg_matvec_qkv)
+//   QK-norm, RoPE, K/V append     csrc/kernel.cu:316-400
+//   GQA attention, online softmax csrc/kernel.cu:400-643
+//   O-proj + residual, post-norm, SiLU(gate) * up, down + residual
+//                                 csrc/kernel.cu:649-865
+//   final norm, LM head, argmax   csrc/kernel.cu:1020-1183, 1386-1423
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cublas_v2.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "qwen_megakernel.h"
+
+int qmk_internal_set_error(int code, const char *msg);
+int qmk_internal_clear_error();
+
+namespace qmb {
+
+constexpr int kHidden = QMK_HIDDEN;
+constexpr int kInter = QMK_INTERMEDIATE;
+constexpr int kHeadDim = QMK_HEAD_DIM;
+constexpr int kNumQHeads = QMK_NUM_Q_HEADS;
+constexpr int kNumKVHeads = QMK_NUM_KV_HEADS;
+constexpr int kQSize = kNumQHeads * kHeadDim;    // 2048
+constexpr int kKVSize = kNumKVHeads * kHeadDim;  // 1024
+constexpr int kQKV = kQSize + 2 * kKVSize;       // 4096
+constexpr int kVocab = QMK_VOCAB;
+constexpr float kRmsEps = 1e-6f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float bf_lo(unsigned u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(unsigned u) { return __uint_as_float(u & 0xffff0000u); }
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// v ~= hi + lo with hi = bf16(v), lo = bf16(v - hi): four elements at once.
+__device__ __forceinline__ void split4(const float (&v)[4], uint2 &hi, uint2 &lo) {
+  const __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]);
+  const __nv_bfloat162 h1 = __floats2bfloat162_rn(v[2], v[3]);
+  const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+  const __nv_bfloat162 l0 = __floats2bfloat162_rn(v[0] - f0.x, v[1] - f0.y);
+  const __nv_bfloat162 l1 = __floats2bfloat162_rn(v[2] - f1.x, v[3] - f1.y);
+  hi = make_uint2(*reinterpret_cast<const unsigned *>(&h0), *reinterpret_cast<const unsigned *>(&h1));
+  lo = make_uint2(*reinterpret_cast<const unsigned *>(&l0), *reinterpret_cast<const unsigned *>(&l1));
+}
+
+// Block (256 threads) sum; every thread gets the total.  red: 8 floats.
+__device__ __forceinline__ float block_sum256(float v, float *red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5;
+  __syncthreads();  // red may still be read by a previous call
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t += red[i];
+  return t;
+}
+
+// ---------------------------------------------------------------- kernels
+// x[r] = embed[tokens[r]] (bf16 -> fp32).  Grid: rows, 256 threads, 4 each.
+__global__ void __launch_bounds__(256) embed_kernel(const __nv_bfloat16 *__restrict__ embed,
+                                                   const int *__restrict__ tokens, float *__restrict__ x,
+                                                   unsigned *status) {
+  const int r = blockIdx.x;
+  int tok = tokens[r];
+  if (tok < 0 || tok >= kVocab) {
+    if (threadIdx.x == 0 && status) atomicOr(status, QMK_BATCH_BAD_TOKEN);
+    tok = 0;
+  }
+  const uint2 v = __ldg(reinterpret_cast<const uint2 *>(embed + (size_t)tok * kHidden) + threadIdx.x);
+  reinterpret_cast<float4 *>(x + (size_t)r * kHidden)[threadIdx.x] =
+      make_float4(bf_lo(v.x), bf_hi(v.x), bf_lo(v.y), bf_hi(v.y));
+}
+
+// Residual add + RMSNorm (eps 1e-6) times w, split into the bf16 GEMM input.
+// GEMM inputs and outputs are "stacked": for n rows the hi halves fill rows
+// [0, n) and the lo halves rows [n, 2n), so ONE GEMM over 2n rows reads each
+// weight once for both halves; the consumer of its fp32 output adds row r
+// and row n + r.  Here: v = x[r] + c2[r] + c2[num_in + r] (c2 = the stacked
+// output of the previous projection, or null), with r = rows ? rows[i] : i;
+// without `rows` v is written back to x (the residual stream).  Output row i
+// of n_out = gridDim.x: hi at a2 row i, lo at a2 row n_out + i (stride 1024).
+__global__ void __launch_bounds__(256) residual_norm_split_kernel(float *__restrict__ x,
+                                                                  const float *__restrict__ c2,
+                                                                  const int *__restrict__ rows, int num_in,
+                                                                  const __nv_bfloat16 *__restrict__ w,
+                                                                  __nv_bfloat16 *__restrict__ a2) {
+  __shared__ float red[8];
+  const int i = blockIdx.x, n_out = gridDim.x;
+  int r = rows ? rows[i] : i;
+  if (r < 0 || r >= num_in) r = 0;  // validated on the host; never read out of bounds
+  float4 v = reinterpret_cast<const float4 *>(x + (size_t)r * kHidden)[threadIdx.x];
+  if (c2) {
+    const float4 h = reinterpret_cast<const float4 *>(c2 + (size_t)r * kHidden)[threadIdx.x];
+    const float4 l = reinterpret_cast<const float4 *>(c2 + (size_t)(num_in + r) * kHidden)[threadIdx.x];
+    v.x += h.x + l.x;
+    v.y += h.y + l.y;
+    v.z += h.z + l.z;
+    v.w += h.w + l.w;
+    if (!rows) reinterpret_cast<float4 *>(x + (size_t)r * kHidden)[threadIdx.x] = v;
+  }
+  const float ss = block_sum256(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w, red);
+  const float rstd = rsqrtf(ss / (float)kHidden + kRmsEps);
+  const uint2 wv = __ldg(reinterpret_cast<const uint2 *>(w) + threadIdx.x);
+  const float y[4] = {v.x * rstd * bf_lo(wv.x), v.y * rstd * bf_hi(wv.x), v.z * rstd * bf_lo(wv.y),
+                      v.w * rstd * bf_hi(wv.y)};
+  uint2 h, l;
+  split4(y, h, l);
+  reinterpret_cast<uint2 *>(a2 + (size_t)i * kHidden)[threadIdx.x] = h;
+  reinterpret_cast<uint2 *>(a2 + (size_t)(n_out + i) * kHidden)[threadIdx.x] = l;
+}
+
+// Per-head RMSNorm of q and k (weights [128]) of the stacked QKV GEMM output
+// [2 rows, 4096], RoPE (rotate-half, bf16 tables) at the row's position, K/V rounded to bf16 into the sequence's
+// cache, q scaled by attn_scale * log2(e) (scores in log2 units).  Grid:
+// rows, 256 threads: warp w takes q heads w and w + 8, K/V head w; lane l
+// holds dims 4l .. 4l + 3, the rotation partner (d +- 64) sits in lane l ^ 16.
+__global__ void __launch_bounds__(256) qk_rope_kv_kernel(
+    const float *__restrict__ qkv, const __nv_bfloat16 *__restrict__ q_norm,
+    const __nv_bfloat16 *__restrict__ k_norm, const __nv_bfloat16 *__restrict__ cos_t,
+    const __nv_bfloat16 *__restrict__ sin_t, const int *__restrict__ row_seq, const int *__restrict__ row_pos,
+    __nv_bfloat16 *__restrict__ k_cache, __nv_bfloat16 *__restrict__ v_cache, long long kv_seq_stride,
+    int num_seqs, int layer, int max_seq_len, float q_scale, float *__restrict__ q_out, unsigned *status) {
+  const int r = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int seq = row_seq[r], pos = row_pos[r];
+  if (seq < 0 || seq >= num_seqs || pos < 0 || pos >= max_seq_len) {
+    if (threadIdx.x == 0 && status) atomicOr(status, QMK_BATCH_BAD_ROW);
+    return;
+  }
+  const int d0 = 4 * lane;
+  const uint2 cv = __ldg(reinterpret_cast<const uint2 *>(cos_t + (size_t)pos * kHeadDim + d0));
+  const uint2 sv = __ldg(reinterpret_cast<const uint2 *>(sin_t + (size_t)pos * kHeadDim + d0));
+  const float cf[4] = {bf_lo(cv.x), bf_hi(cv.x), bf_lo(cv.y), bf_hi(cv.y)};
+  const float sf[4] = {bf_lo(sv.x), bf_hi(sv.x), bf_lo(sv.y), bf_hi(sv.y)};
+  const float *row = qkv + (size_t)r * kQKV;
+  const float *row_lo = qkv + (size_t)(gridDim.x + r) * kQKV;  // stacked GEMM output: hi + lo rows
+  auto load4 = [&](int col) {
+    const float4 h = *reinterpret_cast<const float4 *>(row + col);
+    const float4 l = *reinterpret_cast<const float4 *>(row_lo + col);
+    return make_float4(h.x + l.x, h.y + l.y, h.z + l.z, h.w + l.w);
+  };
+  auto norm_rope = [&](int col, const __nv_bfloat16 *nw, float (&y)[4]) {
+    const float4 x4 = load4(col + d0);
+    float x[4] = {x4.x, x4.y, x4.z, x4.w};
+    const float rr = rsqrtf(warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]) / (float)kHeadDim + kRmsEps);
+    const uint2 wv = __ldg(reinterpret_cast<const uint2 *>(nw + d0));
+    const float wf[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x[e] = (x[e] * rr) * wf[e];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
+      y[e] = (lane < 16) ? (x[e] * cf[e] - partner * sf[e]) : (x[e] * cf[e] + partner * sf[e]);
+    }
+  };
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int h = warp + 8 * k;
+    float y[4];
+    norm_rope(h * kHeadDim, q_norm, y);
+    *reinterpret_cast<float4 *>(q_out + (size_t)r * kQSize + h * kHeadDim + d0) =
+        make_float4(y[0] * q_scale, y[1] * q_scale, y[2] * q_scale, y[3] * q_scale);
+  }
+  float ky[4];
+  norm_rope(kQSize + warp * kHeadDim, k_norm, ky);
+  const float4 v4 = load4(kQSize + kKVSize + warp * kHeadDim + d0);
+  const size_t off = (size_t)seq * (size_t)kv_seq_stride +
+                     (((size_t)layer * kNumKVHeads + warp) * (size_t)max_seq_len + pos) * kHeadDim + d0;
+  const __nv_bfloat162 k01 = __floats2bfloat162_rn(ky[0], ky[1]), k23 = __floats2bfloat162_rn(ky[2], ky[3]);
+  const __nv_bfloat162 v01 = __floats2bfloat162_rn(v4.x, v4.y), v23 = __floats2bfloat162_rn(v4.z, v4.w);
+  *reinterpret_cast<uint2 *>(k_cache + off) =
+      make_uint2(*reinterpret_cast<const unsigned *>(&k01), *reinterpret_cast<const unsigned *>(&k23));
+  *reinterpret_cast<uint2 *>(v_cache + off) =
+      make_uint2(*reinterpret_cast<const unsigned *>(&v01), *reinterpret_cast<const unsigned *>(&v23));
+}
+
+// GQA attention of row r over positions [0, row_pos[r]] of its sequence's
+// cache for the q heads 2g, 2g+1 of KV head g (grid (g, r, split), 256
+// threads; split s of `splits` takes the s-th of equal position chunks, so
+// small batches still fill the GPU).
+// Group gq = lane / 8 of a warp takes one position per round; lane r8 of
+// the group holds dims [8 r8, 8 r8 + 8) and [64 + 8 r8, 64 + 8 r8 + 8) of
+// both heads (two 16-byte reads cover a 256-byte cache row per group), so a
+// score is 16 FMAs per head plus a 3-level butterfly.  A round covers 32
+// positions (8 warps x 4 groups); one online-softmax update absorbs two
+// rounds.  The warps' states merge through shared memory.  With one split
+// the output is written as the stacked bf16 hi/lo O-projection input (rows
+// r and R + r, R = gridDim.y); with several, the CTA's unnormalized state
+// (m0, l0, m1, l1, o0[128], o1[128]) goes to `partial` for merge_kernel.
+constexpr int kAttRounds = 2;
+constexpr int kAttPartWords = 4 + 2 * kHeadDim;
+constexpr int kAttMaxSplits = 16;
+constexpr int kAttSplitRows = 64;  // splits > 1 only for up to this many rows
+
+// Normalized attention output of dims d..d+3 of q head h, row r -> the
+// stacked O-projection input (hi row r, lo row R + r).
+__device__ __forceinline__ void store_att(__nv_bfloat16 *a2, int R, int r, int h, int d, const float (&y)[4]) {
+  uint2 hi, lo;
+  split4(y, hi, lo);
+  *reinterpret_cast<uint2 *>(a2 + (size_t)r * kQSize + h * kHeadDim + d) = hi;
+  *reinterpret_cast<uint2 *>(a2 + (size_t)(R + r) * kQSize + h * kHeadDim + d) = lo;
+}
+
+__global__ void __launch_bounds__(256) attention_kernel(
+    const float *__restrict__ q, const __nv_bfloat16 *__restrict__ k_cache,
+    const __nv_bfloat16 *__restrict__ v_cache, long long kv_seq_stride, int num_seqs, int layer, int max_seq_len,
+    const int *__restrict__ row_seq, const int *__restrict__ row_pos, int splits, float *__restrict__ partial,
+    __nv_bfloat16 *__restrict__ a2) {
+  __shared__ __align__(16) float part[8 * kAttPartWords];
+  const int g = blockIdx.x, r = blockIdx.y, sp = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = lane >> 3, r8 = lane & 7;
+  const int seq = row_seq[r], pos = row_pos[r];
+  const bool valid = seq >= 0 && seq < num_seqs && pos >= 0 && pos < max_seq_len;
+  const int n = valid ? pos + 1 : 0;
+  const int chunk = (n + splits - 1) / splits;
+  const int j_lo = min(n, sp * chunk), j_hi = min(n, j_lo + chunk);
+  float qv[2][16];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float *qh = q + (size_t)r * kQSize + (2 * g + h) * kHeadDim;
+    const float4 a = *reinterpret_cast<const float4 *>(qh + 8 * r8);
+    const float4 b = *reinterpret_cast<const float4 *>(qh + 8 * r8 + 4);
+    const float4 c = *reinterpret_cast<const float4 *>(qh + 64 + 8 * r8);
+    const float4 d = *reinterpret_cast<const float4 *>(qh + 64 + 8 * r8 + 4);
+    const float t[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+    for (int e = 0; e < 16; ++e) qv[h][e] = t[e];
+  }
+  const size_t head_off =
+      (size_t)(valid ? seq : 0) * (size_t)kv_seq_stride + ((size_t)layer * kNumKVHeads + g) * (size_t)max_seq_len * kHeadDim;
+  const uint8_t *kbase = reinterpret_cast<const uint8_t *>(k_cache + head_off) + 16 * r8;
+  const uint8_t *vbase = reinterpret_cast<const uint8_t *>(v_cache + head_off) + 16 * r8;
+  float mrun[2] = {-INFINITY, -INFINITY}, lrun[2] = {0.f, 0.f};
+  float oacc[2][16];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int e = 0; e < 16; ++e) oacc[h][e] = 0.f;
+
+  for (int base = j_lo; base < j_hi; base += 32 * kAttRounds) {
+    if (base + 4 * warp >= j_hi) continue;  // warp-uniform: no position of this warp in this update
+    int jr[kAttRounds];
+    bool ok[kAttRounds];
+    uint4 ka[kAttRounds], kb[kAttRounds], va[kAttRounds], vb[kAttRounds];
+#pragma unroll
+    for (int t = 0; t < kAttRounds; ++t) {
+      const int j = base + 32 * t + 4 * warp + gq;
+      ok[t] = j < j_hi;
+      jr[t] = ok[t] ? j : base + 4 * warp;  // an in-range row, masked below
+      const uint8_t *kr = kbase + (size_t)jr[t] * (kHeadDim * 2);
+      const uint8_t *vr = vbase + (size_t)jr[t] * (kHeadDim * 2);
+      ka[t] = __ldg(reinterpret_cast<const uint4 *>(kr));
+      kb[t] = __ldg(reinterpret_cast<const uint4 *>(kr + kHeadDim));
+      va[t] = __ldg(reinterpret_cast<const uint4 *>(vr));
+      vb[t] = __ldg(reinterpret_cast<const uint4 *>(vr + kHeadDim));
+    }
+    float s[kAttRounds][2];
+#pragma unroll
+    for (int t = 0; t < kAttRounds; ++t)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float *qq = qv[h];
+        const unsigned w[8] = {ka[t].x, ka[t].y, ka[t].z, ka[t].w, kb[t].x, kb[t].y, kb[t].z, kb[t].w};
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          s0 = fmaf(qq[2 * k], bf_lo(w[k]), s0);
+          s1 = fmaf(qq[2 * k + 1], bf_hi(w[k]), s1);
+        }
+        s[t][h] = s0 + s1;
+      }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+      for (int t = 0; t < kAttRounds; ++t) {
+        s[t][0] += __shfl_xor_sync(0xffffffffu, s[t][0], o);
+        s[t][1] += __shfl_xor_sync(0xffffffffu, s[t][1], o);
+      }
+    float mn[2] = {mrun[0], mrun[1]};
+#pragma unroll
+    for (int t = 0; t < kAttRounds; ++t) {
+      if (!ok[t]) s[t][0] = s[t][1] = -INFINITY;
+      mn[0] = fmaxf(mn[0], s[t][0]);
+      mn[1] = fmaxf(mn[1], s[t][1]);
+    }
+#pragma unroll
+    for (int o = 8; o < 32; o <<= 1) {
+      mn[0] = fmaxf(mn[0], __shfl_xor_sync(0xffffffffu, mn[0], o));
+      mn[1] = fmaxf(mn[1], __shfl_xor_sync(0xffffffffu, mn[1], o));
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float corr = fast_exp2(mrun[h] - mn[h]);  // 0 while mrun is -inf
+      float pt[kAttRounds];
+      float l = lrun[h] * corr;
+#pragma unroll
+      for (int t = 0; t < kAttRounds; ++t) {
+        pt[t] = fast_exp2(s[t][h] - mn[h]);  // 0 for masked positions
+        l += pt[t];
+      }
+      lrun[h] = l;
+      mrun[h] = mn[h];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) oacc[h][e] *= corr;
+#pragma unroll
+      for (int t = 0; t < kAttRounds; ++t) {
+        const unsigned w[8] = {va[t].x, va[t].y, va[t].z, va[t].w, vb[t].x, vb[t].y, vb[t].z, vb[t].w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          oacc[h][2 * k] = fmaf(pt[t], bf_lo(w[k]), oacc[h][2 * k]);
+          oacc[h][2 * k + 1] = fmaf(pt[t], bf_hi(w[k]), oacc[h][2 * k + 1]);
+        }
+      }
+    }
+  }
+  // Groups -> warp (same running max in every group): reduce-scatter, then
+  // lane (gq, r8) holds head gq & 1, dims [base, base + 8), base = 8 r8 + 64 (gq >> 1).
+#pragma unroll
+  for (int o = 8; o < 32; o <<= 1) {
+    lrun[0] += __shfl_xor_sync(0xffffffffu, lrun[0], o);
+    lrun[1] += __shfl_xor_sync(0xffffffffu, lrun[1], o);
+  }
+  const bool hb = (gq & 1) != 0, db = (gq >> 1) != 0;
+  float keep[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float send = hb ? oacc[0][k] : oacc[1][k];
+    keep[k] = (hb ? oacc[1][k] : oacc[0][k]) + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float fin[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float send = db ? keep[k] : keep[8 + k];
+    fin[k] = (db ? keep[8 + k] : keep[k]) + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  float *pw = part + warp * kAttPartWords;
+  if (lane == 0) {
+    pw[0] = mrun[0];
+    pw[1] = lrun[0];
+    pw[2] = mrun[1];
+    pw[3] = lrun[1];
+  }
+  float4 *dst = reinterpret_cast<float4 *>(pw + 4 + (gq & 1) * kHeadDim + 64 * (gq >> 1) + 8 * r8);
+  dst[0] = make_float4(fin[0], fin[1], fin[2], fin[3]);
+  dst[1] = make_float4(fin[4], fin[5], fin[6], fin[7]);
+  __syncthreads();
+  // Thread i < 64: head i / 32, dims 4 (i % 32) .. + 3.
+  if (threadIdx.x < 64) {
+    const int hh = threadIdx.x >> 5, d = 4 * (threadIdx.x & 31);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, part[w * kAttPartWords + 2 * hh]);
+    float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const float mw = part[w * kAttPartWords + 2 * hh];
+        if (mw != -INFINITY) {
+          const float f = fast_exp2(mw - M);
+          const float4 ow = *reinterpret_cast<const float4 *>(part + w * kAttPartWords + 4 + hh * kHeadDim + d);
+          L += part[w * kAttPartWords + 2 * hh + 1] * f;
+          o[0] += ow.x * f;
+          o[1] += ow.y * f;
+          o[2] += ow.z * f;
+          o[3] += ow.w * f;
+        }
+      }
+    }
+    if (splits == 1) {
+      const float inv = (L > 0.f) ? fast_rcp(L) : 0.f;
+      const float y[4] = {o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv};
+      store_att(a2, gridDim.y, r, 2 * g + hh, d, y);
+    } else {
+      float *pp = partial + (((size_t)r * kNumKVHeads + g) * splits + sp) * kAttPartWords;
+      if ((threadIdx.x & 31) == 0) {
+        pp[2 * hh] = M;
+        pp[2 * hh + 1] = L;
+      }
+      *reinterpret_cast<float4 *>(pp + 4 + hh * kHeadDim + d) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// Merge of the split states of (row r, KV head g): grid (g, r), 64 threads,
+// thread i: q head 2g + i / 32, dims 4 (i % 32) .. + 3.
+__global__ void __launch_bounds__(64) merge_kernel(const float *__restrict__ partial, int splits,
+                                                   __nv_bfloat16 *__restrict__ a2) {
+  const int g = blockIdx.x, r = blockIdx.y;
+  const int hh = threadIdx.x >> 5, d = 4 * (threadIdx.x & 31);
+  const float *pp = partial + ((size_t)r * kNumKVHeads + g) * splits * kAttPartWords;
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, pp[s * kAttPartWords + 2 * hh]);
+  float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+  if (M != -INFINITY) {
+    for (int s = 0; s < splits; ++s) {
+      const float ms = pp[s * kAttPartWords + 2 * hh];
+      if (ms != -INFINITY) {
+        const float f = fast_exp2(ms - M);
+        const float4 os = *reinterpret_cast<const float4 *>(pp + s * kAttPartWords + 4 + hh * kHeadDim + d);
+        L += pp[s * kAttPartWords + 2 * hh + 1] * f;
+        o[0] += os.x * f;
+        o[1] += os.y * f;
+        o[2] += os.z * f;
+        o[3] += os.w * f;
+      }
+    }
+  }
+  const float inv = (L > 0.f) ? fast_rcp(L) : 0.f;
+  const float y[4] = {o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv};
+  store_att(a2, gridDim.y, r, 2 * g + hh, d, y);
+}
+
+// m = SiLU(gate) * up from the stacked gate|up GEMM output gu2 [2R, 6144],
+// split into the stacked down-projection input a2 [2R, 3072].  Grid: rows
+// (R = gridDim.x), 256 threads, 12 elements each.
+__global__ void __launch_bounds__(256) silu_split_kernel(const float *__restrict__ gu2,
+                                                         __nv_bfloat16 *__restrict__ a2) {
+  const int r = blockIdx.x, R = gridDim.x;
+  const float *hi_row = gu2 + (size_t)r * (2 * kInter);
+  const float *lo_row = gu2 + (size_t)(R + r) * (2 * kInter);
+  for (int c = threadIdx.x; c < kInter / 4; c += 256) {
+    const float4 gh = reinterpret_cast<const float4 *>(hi_row)[c], gl = reinterpret_cast<const float4 *>(lo_row)[c];
+    const float4 uh = reinterpret_cast<const float4 *>(hi_row + kInter)[c];
+    const float4 ul = reinterpret_cast<const float4 *>(lo_row + kInter)[c];
+    const float gg[4] = {gh.x + gl.x, gh.y + gl.y, gh.z + gl.z, gh.w + gl.w};
+    const float uu[4] = {uh.x + ul.x, uh.y + ul.y, uh.z + ul.z, uh.w + ul.w};
+    float y[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y[e] = gg[e] * fast_rcp(1.0f + fast_exp2(-gg[e] * kLog2e)) * uu[e];
+    uint2 h, l;
+    split4(y, h, l);
+    reinterpret_cast<uint2 *>(a2 + (size_t)r * kInter)[c] = h;
+    reinterpret_cast<uint2 *>(a2 + (size_t)(R + r) * kInter)[c] = l;
+  }
+}
+
+// Logits of output row i = row i + row O + i of the stacked LM-head GEMM
+// output (O = gridDim.x), written to `logits` if given; greedy token:
+// largest value, lowest index on ties.  1024 threads.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ logits2, float *__restrict__ logits,
+                                                      int *__restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int i = blockIdx.x, O = gridDim.x;
+  const float *hi = logits2 + (size_t)i * kVocab;
+  const float *lo = logits2 + (size_t)(O + i) * kVocab;
+  float *dst = logits ? logits + (size_t)i * kVocab : nullptr;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int c = threadIdx.x; c < kVocab; c += 1024) {
+    const float v = hi[c] + lo[c];
+    if (dst) dst[c] = v;
+    if (v > best) {  // c increases per thread: strict > keeps the lowest index
+      best = v;
+      bi = c;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    best = sv[threadIdx.x];
+    bi = si[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (threadIdx.x == 0 && out) out[i] = (bi == 0x7fffffff) ? 0 : bi;
+  }
+}
+
+}  // namespace qmb
+
+// =============================================================================
+// Host side
+// =============================================================================
+namespace {
+
+int fail(int code, const char *fmt, ...) {
+  char msg[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(msg, sizeof(msg), fmt, ap);
+  va_end(ap);
+  return qmk_internal_set_error(code, msg);
+}
+
+constexpr size_t kAlign = 256;
+constexpr size_t kCublasWorkspace = 32u << 20;
+
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Workspace regions for R rows and O output rows, in order (GEMM inputs and
+// outputs stacked: 2R or 2O rows, hi halves then lo halves).
+struct Layout {
+  size_t x, a2, qkv2, q, c2, gu2, partial, lm2, logits2, cublas, total;
+};
+
+Layout layout(int R, int O) {
+  using namespace qmb;
+  Layout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes);
+    return at;
+  };
+  L.x = take((size_t)R * kHidden * 4);
+  L.a2 = take((size_t)2 * R * kInter * 2);  // largest GEMM input: K = 3072
+  L.qkv2 = take((size_t)2 * R * kQKV * 4);
+  L.q = take((size_t)R * kQSize * 4);
+  L.c2 = take((size_t)2 * R * kHidden * 4);  // O and down outputs
+  L.gu2 = take((size_t)2 * R * 2 * kInter * 4);
+  // split states (used up to kAttSplitRows rows; sized so that the total
+  // grows with R: a workspace for R rows serves every smaller call)
+  L.partial = take((size_t)(R < kAttSplitRows ? R : kAttSplitRows) * kNumKVHeads * kAttMaxSplits * kAttPartWords * 4);
+  L.lm2 = take((size_t)2 * O * kHidden * 2);
+  L.logits2 = take((size_t)2 * O * kVocab * 4);
+  L.cublas = take(kCublasWorkspace);
+  L.total = off;
+  return L;
+}
+
+// Position splits of the attention for R rows: enough CTAs (8 R splits) to
+// cover the 148 SMs twice when the batch is small, one split otherwise.
+int attention_splits(int R) {
+  using namespace qmb;
+  if (R > kAttSplitRows) return 1;
+  const int s = (2 * 148 + kNumKVHeads * R - 1) / (kNumKVHeads * R);
+  return s < 1 ? 1 : (s > kAttMaxSplits ? kAttMaxSplits : s);
+}
+
+constexpr int kMaxDevices = 64;
+cublasHandle_t g_handles[kMaxDevices] = {};
+std::mutex g_batch_mutex;
+
+const char *cublas_name(cublasStatus_t s) {
+  switch (s) {
+    case CUBLAS_STATUS_SUCCESS: return "success";
+    case CUBLAS_STATUS_NOT_INITIALIZED: return "not initialized";
+    case CUBLAS_STATUS_ALLOC_FAILED: return "alloc failed";
+    case CUBLAS_STATUS_INVALID_VALUE: return "invalid value";
+    case CUBLAS_STATUS_ARCH_MISMATCH: return "arch mismatch";
+    case CUBLAS_STATUS_EXECUTION_FAILED: return "execution failed";
+    case CUBLAS_STATUS_NOT_SUPPORTED: return "not supported";
+    default: return "error";
+  }
+}
+
+// C[rows, n] (fp32, row stride ldc) = A[rows, k] W[n, k]^T with bf16 A (row
+// stride k) and W (row-major [n, k]): one cuBLAS call, fp32 accumulation.
+// cuBLAS is column-major: this is C^T = W * A^T, i.e. op(W) = T, op(A) = N.
+cublasStatus_t gemm(cublasHandle_t h, int rows, int n, int k, const void *W, const void *A, float *C, int ldc) {
+  const float one = 1.f, zero = 0.f;
+  return cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, n, rows, k, &one, W, CUDA_R_16BF, k, A, CUDA_R_16BF, k, &zero, C,
+                      CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+}
+
+}  // namespace
+
+extern "C" size_t qmk_batch_workspace_bytes(int num_rows, int num_out) {
+  if (num_rows < 1 || num_rows > QMK_BATCH_MAX_ROWS || num_out < 0 || num_out > num_rows) return 0;
+  return layout(num_rows, num_out).total;
+}
+
+extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
+  using namespace qmb;
+  qmk_internal_clear_error();
+  if (!a) return fail(QMK_ERR_ARGS, "qmk_batch_forward: null args");
+  if (!a->embed_weight || !a->layer_ptrs || !a->final_norm_weight || !a->lm_head_weight || !a->cos_table ||
+      !a->sin_table || !a->k_cache || !a->v_cache || !a->tokens || !a->row_seq || !a->row_pos)
+    return fail(QMK_ERR_ARGS, "qmk_batch_forward: null weight/table/cache/row pointer");
+  if (a->num_rows < 1 || a->num_rows > QMK_BATCH_MAX_ROWS)
+    return fail(QMK_ERR_ARGS, "qmk_batch_forward: num_rows=%d outside [1, %d]", a->num_rows, QMK_BATCH_MAX_ROWS);
+  if (a->num_out < 0 || a->num_out > a->num_rows)
+    return fail(QMK_ERR_ARGS, "qmk_batch_forward: num_out=%d outside [0, num_rows=%d]", a->num_out, a->num_rows);
+  if (a->num_out > 0 && !a->out_rows) return fail(QMK_ERR_ARGS, "qmk_batch_forward: num_out > 0 needs out_rows");
+  if (a->num_layers < 1 || a->num_layers > QMK_MAX_LAYERS)
+    return fail(QMK_ERR_ARGS, "qmk_batch_forward: num_layers=%d outside [1, %d]", a->num_layers, QMK_MAX_LAYERS);
+  if (a->max_seq_len < 1 || a->num_seqs < 1)
+    return fail(QMK_ERR_ARGS, "qmk_batch_forward: max_seq_len=%d num_seqs=%d", a->max_seq_len, a->num_seqs);
+  const long long per_seq = (long long)a->num_layers * kNumKVHeads * a->max_seq_len * kHeadDim;
+  if (a->num_seqs > 1 && a->kv_seq_stride < per_seq)
+    return fail(QMK_ERR_ARGS, "qmk_batch_forward: kv_seq_stride=%lld < one cache (%lld elements)", a->kv_seq_stride,
+                per_seq);
+  for (int i = 0; i < a->num_layers * 11; ++i)
+    if (!a->layer_ptrs[i]) return fail(QMK_ERR_ARGS, "qmk_batch_forward: layer pointer %d is null", i);
+  const Layout Lw = layout(a->num_rows, a->num_out);
+  if (!a->workspace || a->workspace_bytes < Lw.total || (reinterpret_cast<uintptr_t>(a->workspace) % kAlign))
+    return fail(QMK_ERR_WORKSPACE, "qmk_batch_forward: workspace needs %zu bytes, 256-byte aligned", Lw.total);
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(QMK_ERR_CUDA, "qmk_batch_forward: cudaGetDevice: %s", cudaGetErrorString(e));
+
+  std::lock_guard<std::mutex> lock(g_batch_mutex);
+  cublasHandle_t h = g_handles[dev];
+  if (!h) {
+    const cublasStatus_t s = cublasCreate(&h);
+    if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublasCreate: %s", cublas_name(s));
+    g_handles[dev] = h;
+  }
+  uint8_t *ws = static_cast<uint8_t *>(a->workspace);
+  cublasStatus_t s = cublasSetStream(h, stream);
+  if (s == CUBLAS_STATUS_SUCCESS) s = cublasSetWorkspace(h, ws + Lw.cublas, kCublasWorkspace);
+  if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublas setup: %s", cublas_name(s));
+
+  const int R = a->num_rows, O = a->num_out, R2 = 2 * R;
+  float *x = reinterpret_cast<float *>(ws + Lw.x);
+  auto *a2 = reinterpret_cast<__nv_bfloat16 *>(ws + Lw.a2);
+  float *qkv2 = reinterpret_cast<float *>(ws + Lw.qkv2);
+  float *q = reinterpret_cast<float *>(ws + Lw.q);
+  float *c2 = reinterpret_cast<float *>(ws + Lw.c2);
+  float *gu2 = reinterpret_cast<float *>(ws + Lw.gu2);
+  float *partial = reinterpret_cast<float *>(ws + Lw.partial);
+  auto *lm2 = reinterpret_cast<__nv_bfloat16 *>(ws + Lw.lm2);
+  float *logits2 = reinterpret_cast<float *>(ws + Lw.logits2);
+  auto *kc = static_cast<__nv_bfloat16 *>(a->k_cache);
+  auto *vc = static_cast<__nv_bfloat16 *>(a->v_cache);
+  const auto *cos_t = static_cast<const __nv_bfloat16 *>(a->cos_table);
+  const auto *sin_t = static_cast<const __nv_bfloat16 *>(a->sin_table);
+  auto bf = [](const void *p) { return static_cast<const __nv_bfloat16 *>(p); };
+  const int splits = attention_splits(R);
+  const float *resid = nullptr;  // stacked output of the last down projection
+
+  embed_kernel<<<R, 256, 0, stream>>>(bf(a->embed_weight), a->tokens, x, a->status);
+  for (int l = 0; l < a->num_layers && s == CUBLAS_STATUS_SUCCESS; ++l) {
+    const void *const *P = a->layer_ptrs + 11 * l;
+    const void *const *F = a->fused_ptrs ? a->fused_ptrs + 2 * l : nullptr;
+    residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, resid, nullptr, R, bf(P[0]), a2);
+    if (F) {
+      s = gemm(h, R2, kQKV, kHidden, F[0], a2, qkv2, kQKV);
+    } else {
+      s = gemm(h, R2, kQSize, kHidden, P[1], a2, qkv2, kQKV);
+      if (s == CUBLAS_STATUS_SUCCESS) s = gemm(h, R2, kKVSize, kHidden, P[2], a2, qkv2 + kQSize, kQKV);
+      if (s == CUBLAS_STATUS_SUCCESS) s = gemm(h, R2, kKVSize, kHidden, P[3], a2, qkv2 + kQSize + kKVSize, kQKV);
+    }
+    if (s != CUBLAS_STATUS_SUCCESS) break;
+    qk_rope_kv_kernel<<<R, 256, 0, stream>>>(qkv2, bf(P[4]), bf(P[5]), cos_t, sin_t, a->row_seq, a->row_pos, kc, vc,
+                                            a->kv_seq_stride, a->num_seqs, l, a->max_seq_len,
+                                            a->attn_scale * kLog2e, q, a->status);
+    attention_kernel<<<dim3(kNumKVHeads, R, splits), 256, 0, stream>>>(
+        q, kc, vc, a->kv_seq_stride, a->num_seqs, l, a->max_seq_len, a->row_seq, a->row_pos, splits, partial, a2);
+    if (splits > 1) merge_kernel<<<dim3(kNumKVHeads, R), 64, 0, stream>>>(partial, splits, a2);
+    s = gemm(h, R2, kHidden, kQSize, P[6], a2, c2, kHidden);
+    if (s != CUBLAS_STATUS_SUCCESS) break;
+    residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, c2, nullptr, R, bf(P[7]), a2);  // x += O-proj
+    if (F) {
+      s = gemm(h, R2, 2 * kInter, kHidden, F[1], a2, gu2, 2 * kInter);
+    } else {
+      s = gemm(h, R2, kInter, kHidden, P[8], a2, gu2, 2 * kInter);
+      if (s == CUBLAS_STATUS_SUCCESS) s = gemm(h, R2, kInter, kHidden, P[9], a2, gu2 + kInter, 2 * kInter);
+    }
+    if (s != CUBLAS_STATUS_SUCCESS) break;
+    silu_split_kernel<<<R, 256, 0, stream>>>(gu2, a2);
+    s = gemm(h, R2, kHidden, kInter, P[10], a2, c2, kHidden);
+    resid = c2;  // added to x by the next norm
+  }
+  if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublasGemmEx: %s", cublas_name(s));
+  if (O > 0) {
+    residual_norm_split_kernel<<<O, 256, 0, stream>>>(x, resid, a->out_rows, R, bf(a->final_norm_weight), lm2);
+    s = gemm(h, 2 * O, kVocab, kHidden, a->lm_head_weight, lm2, logits2, kVocab);
+    if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublasGemmEx (LM head): %s", cublas_name(s));
+    argmax_kernel<<<O, 1024, 0, stream>>>(logits2, a->logits, a->out_tokens);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(QMK_ERR_CUDA, "qmk_batch_forward launch: %s", cudaGetErrorString(e));
+  return QMK_OK;
+}

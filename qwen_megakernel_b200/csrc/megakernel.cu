@@ -1683,6 +1683,17 @@ int clear_error() {
   return QMK_OK;
 }
 
+}  // namespace
+
+// Error reporting shared with the library's other translation units (not
+// part of the exported C ABI).
+__attribute__((visibility("hidden"))) int qmk_internal_set_error(int code, const char *msg) {
+  return set_error(code, "%s", msg);
+}
+__attribute__((visibility("hidden"))) int qmk_internal_clear_error() { return clear_error(); }
+
+namespace {
+
 struct DeviceState {
   bool attr_set = false;
   int num_sms = 0;

@@ -299,6 +299,102 @@ void run(torch::Tensor workspace, torch::Tensor embed_weight, torch::Tensor laye
   raise_if_error(qmk_run(&a, c10::cuda::getCurrentCUDAStream().stream()));
 }
 
+// Token-parallel forward (prefill / batched decode): qmk_batch_forward.
+// layer_ptrs: the num_layers * 11 device pointers in LDGLayerWeights order
+// (the GEMMs are launched from the host, so the table is passed by value).
+void batch_forward(torch::Tensor workspace, torch::Tensor embed_weight, std::vector<int64_t> layer_ptrs,
+                   std::vector<int64_t> fused_ptrs, torch::Tensor final_norm_weight, torch::Tensor lm_head_weight, torch::Tensor cos_table,
+                   torch::Tensor sin_table, torch::Tensor k_cache, torch::Tensor v_cache, int64_t kv_seq_stride,
+                   int64_t num_seqs, int64_t num_layers, int64_t max_seq_len, double attn_scale,
+                   torch::Tensor tokens, torch::Tensor row_seq, torch::Tensor row_pos,
+                   std::optional<torch::Tensor> out_rows, std::optional<torch::Tensor> out_tokens,
+                   std::optional<torch::Tensor> logits, std::optional<torch::Tensor> status) {
+  check_cuda(embed_weight, "embed_weight");
+  for (const auto *t : {&workspace, &final_norm_weight, &lm_head_weight, &cos_table, &sin_table, &k_cache, &v_cache,
+                        &tokens, &row_seq, &row_pos}) {
+    QMK_CHECK(t->is_cuda() && t->device() == embed_weight.device(), "all tensors must be on the weights' device");
+    QMK_CHECK(t->is_contiguous(), "tensors must be contiguous");
+  }
+  check_dtype(embed_weight, torch::kBFloat16, "embed_weight", "bfloat16");
+  check_dtype(k_cache, torch::kBFloat16, "k_cache", "bfloat16");
+  check_dtype(v_cache, torch::kBFloat16, "v_cache", "bfloat16");
+  check_dtype(cos_table, torch::kBFloat16, "cos_table", "bfloat16");
+  check_dtype(sin_table, torch::kBFloat16, "sin_table", "bfloat16");
+  check_dtype(tokens, torch::kInt32, "tokens", "int32");
+  check_dtype(row_seq, torch::kInt32, "row_seq", "int32");
+  check_dtype(row_pos, torch::kInt32, "row_pos", "int32");
+  const int64_t R = tokens.numel();
+  QMK_CHECK(row_seq.numel() == R && row_pos.numel() == R, "tokens, row_seq and row_pos must have equal length");
+  QMK_CHECK((int64_t)layer_ptrs.size() == num_layers * 11, "layer_ptrs must hold num_layers * 11 pointers");
+  QMK_CHECK(fused_ptrs.empty() || (int64_t)fused_ptrs.size() == num_layers * 2,
+            "fused_ptrs must be empty or hold num_layers * 2 pointers");
+  QMK_CHECK(cos_table.size(0) >= max_seq_len && sin_table.size(0) >= max_seq_len,
+            "RoPE tables need >= max_seq_len rows");
+  const int64_t per_seq = num_layers * QMK_NUM_KV_HEADS * max_seq_len * QMK_HEAD_DIM;
+  QMK_CHECK(k_cache.numel() >= (num_seqs - 1) * kv_seq_stride + per_seq && v_cache.numel() == k_cache.numel(),
+            "caches too small for num_seqs sequences at kv_seq_stride");
+  QmkBatchArgs a;
+  memset(&a, 0, sizeof(a));
+  int64_t O = 0;
+  if (out_rows.has_value()) {
+    check_dtype(*out_rows, torch::kInt32, "out_rows", "int32");
+    check_same_device(*out_rows, embed_weight, "out_rows");
+    O = out_rows->numel();
+    a.out_rows = static_cast<const int *>(out_rows->data_ptr());
+  }
+  if (out_tokens.has_value()) {
+    check_dtype(*out_tokens, torch::kInt32, "out_tokens", "int32");
+    check_same_device(*out_tokens, embed_weight, "out_tokens");
+    QMK_CHECK(out_tokens->numel() >= O, "out_tokens must have >= len(out_rows) elements");
+    a.out_tokens = static_cast<int *>(out_tokens->data_ptr());
+  }
+  if (logits.has_value()) {
+    check_dtype(*logits, torch::kFloat32, "logits", "float32");
+    check_same_device(*logits, embed_weight, "logits");
+    QMK_CHECK(logits->is_contiguous() && logits->numel() >= O * QMK_VOCAB,
+              "logits must be contiguous with >= len(out_rows) * %d elements", QMK_VOCAB);
+    a.logits = static_cast<float *>(logits->data_ptr());
+  }
+  if (status.has_value()) {
+    check_dtype(*status, torch::kInt32, "status", "int32");
+    check_same_device(*status, embed_weight, "status");
+    a.status = reinterpret_cast<unsigned *>(status->data_ptr());
+  }
+  std::vector<const void *> ptrs(layer_ptrs.size());
+  for (size_t i = 0; i < ptrs.size(); ++i) ptrs[i] = reinterpret_cast<const void *>(layer_ptrs[i]);
+  std::vector<const void *> fptrs(fused_ptrs.size());
+  for (size_t i = 0; i < fptrs.size(); ++i) fptrs[i] = reinterpret_cast<const void *>(fused_ptrs[i]);
+  a.fused_ptrs = fptrs.empty() ? nullptr : fptrs.data();
+  a.embed_weight = embed_weight.data_ptr();
+  a.layer_ptrs = ptrs.data();
+  a.final_norm_weight = final_norm_weight.data_ptr();
+  a.lm_head_weight = lm_head_weight.data_ptr();
+  a.cos_table = cos_table.data_ptr();
+  a.sin_table = sin_table.data_ptr();
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.kv_seq_stride = kv_seq_stride;
+  a.num_seqs = (int)num_seqs;
+  a.num_layers = (int)num_layers;
+  a.max_seq_len = (int)max_seq_len;
+  a.attn_scale = (float)attn_scale;
+  a.num_rows = (int)R;
+  a.tokens = static_cast<const int *>(tokens.data_ptr());
+  a.row_seq = static_cast<const int *>(row_seq.data_ptr());
+  a.row_pos = static_cast<const int *>(row_pos.data_ptr());
+  a.num_out = (int)O;
+  a.workspace = workspace.data_ptr();
+  a.workspace_bytes = workspace.nbytes();
+  c10::cuda::CUDAGuard guard(embed_weight.device());
+  raise_if_error(qmk_batch_forward(&a, c10::cuda::getCurrentCUDAStream().stream()));
+}
+
+int64_t batch_workspace_bytes(int64_t num_rows, int64_t num_out) {
+  const size_t n = qmk_batch_workspace_bytes((int)num_rows, (int)num_out);
+  QMK_CHECK(n > 0, "batch_workspace_bytes: num_rows=%lld num_out=%lld out of range", (ll)num_rows, (ll)num_out);
+  return (int64_t)n;
+}
+
 int64_t workspace_bytes() { return (int64_t)qmk_workspace_bytes(); }
 
 void workspace_init(torch::Tensor workspace) {
@@ -363,6 +459,16 @@ TORCH_LIBRARY(qwen_megakernel_C, ops) {
       "Tensor? status, int timeout_ns=0, int debug_stall=0, Tensor? trace=None, "
       "int trace_step=0, int poll_backoff_ns=0, int tuning=0) -> ()");
   ops.impl("run", torch::kCUDA, &run);
+
+  ops.def(
+      "batch_forward(Tensor workspace, Tensor embed_weight, int[] layer_ptrs, int[] fused_ptrs, "
+      "Tensor final_norm_weight, "
+      "Tensor lm_head_weight, Tensor cos_table, Tensor sin_table, Tensor k_cache, Tensor v_cache, "
+      "int kv_seq_stride, int num_seqs, int num_layers, int max_seq_len, float attn_scale, "
+      "Tensor tokens, Tensor row_seq, Tensor row_pos, Tensor? out_rows, Tensor? out_tokens, "
+      "Tensor? logits, Tensor? status) -> ()");
+  ops.impl("batch_forward", torch::kCUDA, &batch_forward);
+  ops.def("batch_workspace_bytes(int num_rows, int num_out) -> int", &batch_workspace_bytes);
 
   ops.def("workspace_bytes() -> int", &workspace_bytes);
   ops.def("workspace_init(Tensor workspace) -> ()");

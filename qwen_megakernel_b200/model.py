@@ -275,6 +275,39 @@ class Decoder:
         self._position += n
         return tok
 
+    def prefill_batched(self, token_ids, logits: torch.Tensor | None = None) -> int:
+        """Like prefill(), but token-parallel: the prompt runs as rows of one
+        causal forward pass (tensor-core GEMMs over all tokens at once,
+        ``qmk_batch_forward``) instead of one decode step per token.  Same
+        cache contents and logits within the parity tolerance; returns the
+        argmax after the last token (its fp32 logits into ``logits`` [vocab]
+        if given)."""
+        from .batch import MAX_ROWS, BatchForward, _int32
+
+        ids = [int(t) for t in token_ids]
+        n = len(ids)
+        if n == 0:
+            raise ValueError("prefill needs at least one token")
+        start = self._position
+        if start + n > self.max_seq_len:
+            raise ValueError(f"positions [{start}, {start + n}) exceed max_seq_len {self.max_seq_len}")
+        if getattr(self, "_batch_fw", None) is None:
+            self._batch_fw = BatchForward(self._weights, self.max_seq_len)
+        fw = self._batch_fw
+        for c0 in range(0, n, MAX_ROWS):
+            c1 = min(n, c0 + MAX_ROWS)
+            last = c1 == n
+            tokens = _int32(ids[c0:c1], self.device)
+            row_pos = torch.arange(start + c0, start + c1, dtype=torch.int32, device=self.device)
+            row_seq = torch.zeros(c1 - c0, dtype=torch.int32, device=self.device)
+            out_rows = torch.full((1,), c1 - c0 - 1, dtype=torch.int32, device=self.device) if last else None
+            fw.forward(self._k_cache, self._v_cache, 1, tokens, row_seq, row_pos, out_rows,
+                       self._out_token if last else None, logits if last else None)
+        tok = int(self._out_token.item())
+        fw.check_status()
+        self._position += n
+        return tok
+
     def generate_from(self, token_id: int, max_tokens: int, position: int | None = None) -> list[int]:
         """Greedy continuation from the current KV cache: consume ``token_id`` at
         ``position`` (default: the decoder's position) and return ``max_tokens``
