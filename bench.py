@@ -438,6 +438,142 @@ def run_profile_case(steps: int) -> int:
     return 0
 
 
+def run_batch(args) -> int:
+    """BASELINE config 4 (not the headline line): B independent sequences,
+    1024-token random prompts (token-parallel prefill, untimed), then
+    args.steps batched greedy decode steps (CUDA-graph replays, B tokens each)
+    through BatchDecoder.generate.  One JSON line."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from qwen_megakernel_b200 import BatchDecoder
+    from qwen_megakernel_b200._native import loaded_library_paths
+    from qwen_megakernel_b200.weights import random_weights
+
+    B, K, W = args.batch, args.steps, args.warmup
+    weights = random_weights(seed=0, device="cuda", max_seq_len=2048)
+    bd = BatchDecoder(weights, B, max_seq_len=2048)
+    prompts = [prompt_for_rank(100 + s) for s in range(B)]
+    first = bd.prefill(prompts)
+    pos0 = bd.positions[0]
+    bd.generate(first, W)  # capture + warm-up (advances positions by W)
+    torch.cuda.synchronize(dev)
+    p_start = bd.positions[0]
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(0)
+    sampler.start()
+    e0.record(stream)
+    log = bd.generate(first, K)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    # end to end: host tokens in, host token log out
+    bd2_first = first
+    t0 = time.perf_counter()
+    out = bd.generate(bd2_first, K).cpu()
+    e2e_ms = (time.perf_counter() - t0) * 1000.0
+    bd.fw.check_status()
+    step_bytes = [WEIGHT_BYTES + B * KV_BYTES_PER_POS * (p + 1) for p in range(p_start, p_start + K)]
+    achieved = sum(step_bytes) / (ms / 1000.0) / 1e9
+    peak, peak_kind = measured_peak()
+    line = {
+        "metric": f"batched decode tok/s (Qwen3-0.6B bf16, ctx 1k, B={B})",
+        "value": round(B * K / (ms / 1000.0), 1),
+        "unit": "tok/s",
+        "n_gpus": 1,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(ms / K, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
+        "config": {"workload": f"configs[4]-style: {B} sequences, 1024-token prompts, {K} greedy steps "
+                               f"(cache positions {p_start}..{p_start + K - 1})", "batch": B,
+                   "path": "token-parallel (qmk_batch_forward), CUDA-graph step"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_step": int(sum(step_bytes) / K)},
+        "e2e": {"value": round(B * K / (e2e_ms / 1000.0), 1), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 4 * B},
+        "prefill_positions": pos0,
+        "clocks": clocks,
+        "tokens_sample": out[:2, :4].tolist(),
+        "native_libraries": [os.path.basename(p) for p in loaded_library_paths()],
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_profile_batch(B: int) -> int:
+    """Small case for ncu launch lists of the token-parallel path: B
+    sequences prefilled with 1024-token prompts, 2 warm-up steps, then ONE
+    eager batched decode step between cudaProfilerStart/Stop (capture with
+    ncu --profile-from-start off)."""
+    torch.cuda.set_device(0)
+    from qwen_megakernel_b200 import BatchDecoder
+    from qwen_megakernel_b200.weights import random_weights
+
+    weights = random_weights(seed=0, device="cuda", max_seq_len=2048)
+    bd = BatchDecoder(weights, B, max_seq_len=2048, use_graphs=False)
+    first = bd.prefill([prompt_for_rank(100 + s) for s in range(B)])
+    bd.generate(first, 2)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    bd.generate(first, 1)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    bd.fw.check_status()
+    print(json.dumps({"profile_batch": {"batch": B, "positions": bd.positions[:2]}}))
+    return 0
+
+
+def run_prefill(args) -> int:
+    """Token-parallel prompt prefill (not the headline line): a 1024-token
+    prompt through Decoder.prefill_batched, args.steps timed repetitions."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from qwen_megakernel_b200 import Decoder
+    from qwen_megakernel_b200.weights import random_weights
+
+    weights = random_weights(seed=0, device="cuda", max_seq_len=2048)
+    dec = Decoder(weights, max_seq_len=2048)
+    prompt = prompt_for_rank(0)
+    for _ in range(max(1, args.warmup)):
+        dec.reset()
+        dec.prefill_batched(prompt)
+    torch.cuda.synchronize(dev)
+    times = []
+    for _ in range(args.steps):
+        dec.reset()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        tok = dec.prefill_batched(prompt)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    flops = 2 * 2 * 595_984_384 * PROMPT_LEN  # stacked hi/lo GEMMs: twice the model's 2 N flops per token
+    peak_tf = 1590.0
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak_tf = float(json.load(f).get("bf16_tflops", peak_tf))
+    except (OSError, ValueError):
+        pass
+    print(json.dumps({
+        "metric": "prefill tok/s (Qwen3-0.6B bf16, 1024-token prompt, token-parallel)",
+        "value": round(PROMPT_LEN / (ms / 1000.0), 1), "unit": "tok/s", "ms_per_prompt": round(ms, 3),
+        "steps": args.steps, "warmup": args.warmup, "dtype": "bf16",
+        "roofline": {"bound": "tensor", "achieved": round(flops / (ms / 1000.0) / 1e12, 1), "peak": peak_tf,
+                     "unit": "TFLOP/s", "frac": round(flops / (ms / 1000.0) / 1e12 / peak_tf, 4),
+                     "flops_per_prompt": flops},
+        "next_token": tok}), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -447,7 +583,18 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", type=int, default=0, metavar="STEPS",
                     help="run only the small ncu case: one decode launch of STEPS tokens")
+    ap.add_argument("--batch", type=int, default=0, metavar="B",
+                    help="config 4 instead of the headline: B sequences decoded together (token-parallel path)")
+    ap.add_argument("--prefill", action="store_true", help="time the token-parallel 1024-token prefill instead")
+    ap.add_argument("--profile-batch", type=int, default=0, metavar="B",
+                    help="run only the small ncu case of the token-parallel path: one batched step of B rows")
     args = ap.parse_args(argv)
+    if args.profile_batch:
+        return run_profile_batch(args.profile_batch)
+    if args.batch:
+        return run_batch(args)
+    if args.prefill:
+        return run_prefill(args)
     if args.profile_case:
         return run_profile_case(args.profile_case)
     if args.impl == "reference":
