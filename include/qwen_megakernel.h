@@ -169,6 +169,17 @@ typedef struct QmkRunArgs {
                                          /* store kind of dataflow words (0 red.max */
                                          /* atomic, 1 st.relaxed, 2 st.relaxed +   */
                                          /* fence per phase, 3 atom.exch)          */
+  /* Sampling and stopping (no reference counterpart; zero = the reference's
+   * greedy, fixed-length behaviour). */
+  float temperature;                     /* 0: greedy argmax; > 0: sample from    */
+                                         /* softmax(logits / temperature) by the */
+                                         /* Gumbel-max trick, noise keyed by     */
+                                         /* (seed, position, vocab index)        */
+  unsigned long long seed;
+  int stop_at_eos;                       /* nonzero: end the launch after the     */
+  int eos_token;                         /* first GENERATED token == eos_token    */
+                                         /* (forced tokens never stop it)         */
+  int *steps_done;                       /* device int32 [1] or NULL: steps run   */
 } QmkRunArgs;
 
 /* Bytes of device workspace one decoder needs (flags, dataflow buffers). */

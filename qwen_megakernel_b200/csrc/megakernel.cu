@@ -94,6 +94,10 @@ struct Params {
   int trace_step;
   unsigned poll_backoff_ns;
   unsigned tuning;
+  float inv_temp;       // sampling: 1 / temperature, 0 = greedy
+  unsigned long long seed;
+  int eos_token;        // stop after a generated token equal to this (-1: never)
+  int *steps_done;      // optional: steps executed (< num_steps after an EOS stop)
 };
 
 // Dynamic shared memory plan (bytes).
@@ -147,6 +151,7 @@ struct Ctx {
   uint64_t *full;
   uint64_t *empty;
   volatile int *abort_flag;
+  volatile int *stop_step;  // first step not to run (EOS seen), INT_MAX = none
   float *warp_best_v;
   int *warp_best_i;
   int *token_slot;
@@ -181,6 +186,24 @@ __device__ __forceinline__ float fast_rcp(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Standard Gumbel noise of vocabulary row `idx` at cache position `pos` for
+// sampling seed `seed`: u from the splitmix64 finalizer (Steele, Lea and
+// Flood 2014) of a (seed, position, index) key, 24 bits in (0, 1), then
+// -log(-log(u)).  argmax_i(logit_i / T + g_i) is an exact draw from
+// softmax(logits / T) (the Gumbel-max trick), so sampling reuses the greedy
+// argmax exchange unchanged; the key depends on the position, not on the
+// launch, so a sequence samples the same tokens however it is split into
+// launches.
+__device__ __forceinline__ float gumbel_noise(unsigned long long seed, int pos, int idx) {
+  unsigned long long z = seed ^ (((unsigned long long)(unsigned)pos << 20) | (unsigned)idx);
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  const float u = ((float)(unsigned)(z >> 40) + 0.5f) * (1.0f / 16777216.0f);
+  return -logf(-logf(u));
 }
 
 __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned *p) {
@@ -602,6 +625,7 @@ struct Producer {
   uint64_t pol;
   uint32_t tile = 0;
   bool alive = true;
+  int cur_step = 0;  // decode step the tiles being issued belong to
 
   __device__ Producer(Ctx &c_, const Params &p_) : c(c_), p(p_) { pol = l2_policy_evict_first(); }
 
@@ -612,7 +636,9 @@ struct Producer {
     if (use > 0) {
       Waiter w;
       while (!mbar_try_wait(&c.empty[slot], (use & 1u) ^ 1u)) {
-        if (!w.keep_going(c, kSiteEmpty)) {
+        // the consumers stopped (EOS) before the step this tile belongs to:
+        // its slot will not be released, stop issuing
+        if (*c.stop_step <= cur_step || !w.keep_going(c, kSiteEmpty)) {
           alive = false;
           return nullptr;
         }
@@ -711,7 +737,7 @@ struct Producer {
       while (true) {
         const unsigned v = ld_acquire_u32(flag);
         if (v == e_prev || v == e_cur) break;
-        if (!w.keep_going(c, kSiteKVReady)) {
+        if (*c.stop_step <= step || !w.keep_going(c, kSiteKVReady)) {
           alive = false;
           return;
         }
@@ -732,7 +758,8 @@ struct Producer {
 
   __device__ void run() {
     const int item = item_of_cta(c.cta, p.splits);
-    for (int t = 0; t < p.num_steps && alive; ++t) {
+    for (int t = 0; t < p.num_steps && alive && *c.stop_step > t; ++t) {
+      cur_step = t;
       const int pos = p.start_pos + t;
       c.trace = (p.trace && t == p.trace_step) ? p.trace + (size_t)c.cta * kTraceStride : nullptr;
       c.trace_tile0 = tile;
@@ -781,6 +808,7 @@ struct Consumer {
   float lm_best = -INFINITY;  // LM head: this thread's best logit and row
   int lm_best_i = 0x7fffffff;
   float *lm_logits = nullptr;
+  int lm_pos = 0;             // LM head: cache position of the step (sampling key)
   unsigned mma_issued = 0;   // issuer threads: 1 + the last unit this thread issued
   bool tc_prewaited = false; // issuer threads: the next phase's first unit needs no waits
   NormPairs nw_pref;         // RMSNorm weights of the next normalized GEMV input
@@ -892,8 +920,10 @@ struct Consumer {
         break;
       default: {  // kOutLM
         const float y = v * job.scale;
-        if (y > lm_best || (y == lm_best && row < lm_best_i)) {
-          lm_best = y;
+        // greedy: the logit; sampling: logit / T + Gumbel noise
+        const float key = (p.inv_temp > 0.f) ? fmaf(y, p.inv_temp, gumbel_noise(p.seed, lm_pos, row)) : y;
+        if (key > lm_best || (key == lm_best && row < lm_best_i)) {
+          lm_best = key;
           lm_best_i = row;
         }
         if (lm_logits) lm_logits[row] = y;
@@ -1418,6 +1448,7 @@ struct Consumer {
     lm_best = -INFINITY;
     lm_best_i = 0x7fffffff;
     lm_logits = p.logits ? (p.logits + (size_t)step * kVocab) : nullptr;
+    lm_pos = p.start_pos + step;
     const TcJob job{kTcRow, kOutLM, R.begin, R.end, kLMTileRows, rstd, E};
     tc_phase(job, bop);
     float best = lm_best;
@@ -1490,8 +1521,11 @@ struct Consumer {
     return tok;
   }
 
+  int steps_run = 0;  // steps executed (num_steps unless stopped at EOS)
+
   __device__ void run() {
     const int L = p.num_layers;
+    steps_run = p.num_steps;
     for (int t = 0; t < p.num_steps; ++t) {
       c.trace = (p.trace && t == p.trace_step) ? p.trace + (size_t)c.cta * kTraceStride : nullptr;
       c.trace_tile0 = tile;
@@ -1503,6 +1537,15 @@ struct Consumer {
       }
       nw_pref = load_norm_pairs((const __nv_bfloat16 *)p.layers[0].input_layernorm_weight, tid);
       const int tok = step_token(t);
+      // EOS stop: the token step t would consume was generated (not forced)
+      // and is the end-of-sequence id.  Every consumer thread read the same
+      // token, so all leave here; the producer warp sees the stop step and
+      // stops issuing (it drains what it issued for this step).
+      if (p.eos_token >= 0 && t > 0 && t >= p.n_forced && tok == p.eos_token) {
+        steps_run = t;
+        if (tid == 0) *c.stop_step = t;
+        break;
+      }
       // Layer-0 input: the embedding row (bf16 -> fp32) and its sum of squares.
       float x_ss;
       {
@@ -1538,10 +1581,12 @@ struct Consumer {
       phase_lm_head(t, epoch_of(c, t, L - 1, L), epoch_of(c, t, L, L));
     }
     if (c.cta == 0) {
-      const int last = read_argmax(c, epoch_of(c, p.num_steps - 1, L, L));
+      // After an EOS stop the last step's token (the EOS) is already in the log.
+      const int last = (steps_run == p.num_steps) ? read_argmax(c, epoch_of(c, p.num_steps - 1, L, L)) : p.eos_token;
       if (tid == 0 && live()) {
-        if (p.out_log) p.out_log[p.num_steps - 1] = last;
+        if (p.out_log && steps_run == p.num_steps) p.out_log[p.num_steps - 1] = last;
         if (p.out_token) *p.out_token = last;
+        if (p.steps_done) *p.steps_done = steps_run;
       }
       if (tid == 0 && !live() && p.out_token) *p.out_token = -1;
     }
@@ -1551,6 +1596,7 @@ struct Consumer {
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ int s_abort;
+  __shared__ int s_stop;
   __shared__ unsigned s_epoch;
   Ctx c;
   c.ring = smem + kSmRing;
@@ -1559,6 +1605,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   c.warp_best_v = reinterpret_cast<float *>(smem + kSmMisc + 16 * kNumSlots);
   c.warp_best_i = reinterpret_cast<int *>(smem + kSmMisc + 16 * kNumSlots + 4 * kConsumerWarps);
   c.abort_flag = &s_abort;
+  c.stop_step = &s_stop;
   c.ctrl = reinterpret_cast<Ctrl *>(p.ws);
   c.wX = reinterpret_cast<uint64_t *>(p.ws + kOffX);
   c.wQKV = reinterpret_cast<uint64_t *>(p.ws + kOffQKV);
@@ -1590,6 +1637,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
     fence_mbar_init();
     s_abort = 0;
+    s_stop = 0x7fffffff;
     s_epoch = ld_relaxed_u32(&c.ctrl->epoch);
     // The tensor-core operands use 1 KB swizzle atoms: refuse to run on a
     // misaligned dynamic shared memory window instead of computing garbage.
@@ -1827,6 +1875,10 @@ int qmk_run(const QmkRunArgs *a, cudaStream_t stream) {
     return set_error(QMK_ERR_ARGS, "qmk_run: token id %d outside [0, %d)", a->first_token, QMK_VOCAB);
   if (!(a->attn_scale == a->attn_scale) || a->attn_scale <= 0.f)
     return set_error(QMK_ERR_ARGS, "qmk_run: attn_scale must be positive");
+  if (!(a->temperature >= 0.f) || a->temperature > 1e30f)
+    return set_error(QMK_ERR_ARGS, "qmk_run: temperature must be finite and >= 0");
+  if (a->stop_at_eos && (a->eos_token < 0 || a->eos_token >= QMK_VOCAB))
+    return set_error(QMK_ERR_ARGS, "qmk_run: eos_token %d outside [0, %d)", a->eos_token, QMK_VOCAB);
   const void *ptrs[] = {a->embed_weight, a->final_norm_weight, a->lm_head_weight, a->cos_table,
                         a->sin_table,    a->k_cache,           a->v_cache};
   for (const void *q : ptrs)
@@ -1875,6 +1927,10 @@ int qmk_run(const QmkRunArgs *a, cudaStream_t stream) {
   p.trace_step = a->trace_step;
   p.poll_backoff_ns = a->poll_backoff_ns > 4096u ? 4096u : a->poll_backoff_ns;
   p.tuning = a->tuning;
+  p.inv_temp = a->temperature > 0.f ? 1.0f / a->temperature : 0.f;
+  p.seed = a->seed;
+  p.eos_token = a->stop_at_eos ? a->eos_token : -1;
+  p.steps_done = a->steps_done;
 
   void *kargs[] = {&p};
   cudaError_t e = cudaLaunchCooperativeKernel((const void *)qmk::decode_kernel, dim3(ncta),

@@ -209,7 +209,8 @@ void run(torch::Tensor workspace, torch::Tensor embed_weight, torch::Tensor laye
          std::optional<torch::Tensor> logits, std::optional<torch::Tensor> final_hidden,
          std::optional<torch::Tensor> status, int64_t timeout_ns, int64_t debug_stall,
          std::optional<torch::Tensor> trace, int64_t trace_step, int64_t poll_backoff_ns,
-         int64_t tuning) {
+         int64_t tuning, double temperature, int64_t seed, int64_t stop_at_eos, int64_t eos_token,
+         std::optional<torch::Tensor> steps_done) {
   QMK_CHECK(num_steps >= 1, "num_steps must be >= 1");
   QMK_CHECK(start_position >= 0, "start_position must be >= 0");
   check_model(embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight, cos_table,
@@ -295,6 +296,15 @@ void run(torch::Tensor workspace, torch::Tensor embed_weight, torch::Tensor laye
   a.debug_stall = (int)debug_stall;
   a.poll_backoff_ns = (unsigned)std::min<int64_t>(std::max<int64_t>(poll_backoff_ns, 0), 4096);
   a.tuning = (unsigned)tuning;
+  a.temperature = (float)temperature;
+  a.seed = (unsigned long long)seed;
+  a.stop_at_eos = stop_at_eos ? 1 : 0;
+  a.eos_token = (int)eos_token;
+  if (steps_done.has_value()) {
+    check_dtype(*steps_done, torch::kInt32, "steps_done", "int32");
+    check_same_device(*steps_done, embed_weight, "steps_done");
+    a.steps_done = static_cast<int *>(steps_done->data_ptr());
+  }
   c10::cuda::CUDAGuard guard(embed_weight.device());
   raise_if_error(qmk_run(&a, c10::cuda::getCurrentCUDAStream().stream()));
 }
@@ -457,7 +467,8 @@ TORCH_LIBRARY(qwen_megakernel_C, ops) {
       "int start_position, int num_steps, int num_layers, int max_seq_len, float attn_scale, "
       "Tensor? output_log, Tensor? output_token, Tensor? logits, Tensor? final_hidden, "
       "Tensor? status, int timeout_ns=0, int debug_stall=0, Tensor? trace=None, "
-      "int trace_step=0, int poll_backoff_ns=0, int tuning=0) -> ()");
+      "int trace_step=0, int poll_backoff_ns=0, int tuning=0, float temperature=0.0, int seed=0, "
+      "int stop_at_eos=0, int eos_token=0, Tensor? steps_done=None) -> ()");
   ops.impl("run", torch::kCUDA, &run);
 
   ops.def(

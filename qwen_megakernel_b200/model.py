@@ -137,6 +137,7 @@ class Decoder:
         self._workspace = torch.zeros(self._ops.workspace_bytes(), dtype=torch.uint8, device=self.device)
         self._status = torch.zeros(4, dtype=torch.int32).pin_memory()
         self._out_token = torch.empty(1, dtype=torch.int32, device=self.device)
+        self._steps_done = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     # ------------------------------------------------------------------ core
     @property
@@ -188,13 +189,21 @@ class Decoder:
         trace_step: int = 0,
         poll_backoff_ns: int | None = None,
         tuning: int | None = None,
+        temperature: float = 0.0,
+        seed: int = 0,
+        eos_token: int | None = None,
+        steps_done: torch.Tensor | None = None,
     ) -> None:
         """Queue one launch of ``num_steps`` decode steps (no host sync).
 
         Step t consumes ``forced_tokens[t]`` while t < len(forced_tokens),
         else ``first_token`` (t == 0) or the previous step's argmax, at
         position ``start_position + t``; it writes its argmax to
-        ``output_log[t]`` and its fp32 logits to ``logits[t]`` if given."""
+        ``output_log[t]`` and its fp32 logits to ``logits[t]`` if given.
+        ``temperature`` > 0 samples instead of taking the argmax (Gumbel-max,
+        reproducible per (seed, position)); with ``eos_token`` the launch ends
+        after the first generated token equal to it, and ``steps_done``
+        (device int32 [1]) receives the number of steps run."""
         start = self._position if start_position is None else int(start_position)
         if start < 0 or start + num_steps > self.max_seq_len:
             raise ValueError(f"positions [{start}, {start + num_steps}) exceed max_seq_len {self.max_seq_len}")
@@ -228,6 +237,11 @@ class Decoder:
             int(trace_step),
             int(self.poll_backoff_ns if poll_backoff_ns is None else poll_backoff_ns),
             int(self.tuning if tuning is None else tuning),
+            float(temperature),
+            int(seed),
+            0 if eos_token is None else 1,
+            0 if eos_token is None else int(eos_token),
+            steps_done,
         )
 
     # ------------------------------------------------------- reference API
@@ -245,8 +259,10 @@ class Decoder:
         if self.tokenizer is None:
             raise RuntimeError("generate(prompt) needs a tokenizer; use generate_ids for token ids")
         ids = self.tokenizer.encode(prompt, add_special_tokens=True)
-        out = self.generate_ids(ids, max_tokens)
         eos = self.tokenizer.eos_token_id
+        # the kernel stops at EOS (the reference generates max_tokens and
+        # truncates on the host, model.py:242-244: same text)
+        out = self.generate_ids(ids, max_tokens, eos_token=eos)
         if eos in out:
             out = out[: out.index(eos)]
         return self.tokenizer.decode(out, skip_special_tokens=True)
@@ -308,26 +324,38 @@ class Decoder:
         self._position += n
         return tok
 
-    def generate_from(self, token_id: int, max_tokens: int, position: int | None = None) -> list[int]:
-        """Greedy continuation from the current KV cache: consume ``token_id`` at
+    def generate_from(self, token_id: int, max_tokens: int, position: int | None = None,
+                      temperature: float = 0.0, seed: int = 0, eos_token: int | None = None) -> list[int]:
+        """Continuation from the current KV cache: consume ``token_id`` at
         ``position`` (default: the decoder's position) and return ``max_tokens``
         generated ids -- the semantics of the reference's ``generate_nosync``
-        operator (csrc/torch_bindings.cpp:93-127), with host ids in and out."""
+        operator (csrc/torch_bindings.cpp:93-127), with host ids in and out.
+        Additions: ``temperature`` > 0 samples on the device; with
+        ``eos_token`` the launch stops after generating it (the returned list
+        ends with it and may be shorter)."""
         pos = self._position if position is None else int(position)
+        n = int(max_tokens)
         host_tok = torch.tensor([int(token_id)], dtype=torch.int32).pin_memory()
         dev_tok = host_tok.to(self.device, non_blocking=True)
-        log = torch.empty(int(max_tokens), dtype=torch.int32, device=self.device)
-        self.decode_steps(int(max_tokens), forced_tokens=dev_tok, start_position=pos, output_log=log)
-        host = torch.empty(int(max_tokens), dtype=torch.int32).pin_memory()
-        host.copy_(log, non_blocking=True)
+        log = torch.empty(n, dtype=torch.int32, device=self.device)
+        done = self._steps_done
+        self.decode_steps(n, forced_tokens=dev_tok, start_position=pos, output_log=log, temperature=temperature,
+                          seed=seed, eos_token=eos_token, steps_done=done)
+        host = torch.empty(n + 1, dtype=torch.int32).pin_memory()
+        host[:n].copy_(log, non_blocking=True)
+        host[n:].copy_(done, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
         self.check_status()
-        self._position = pos + int(max_tokens)
-        return host.tolist()
+        ran = int(host[n])
+        self._position = pos + ran
+        return host[:ran].tolist()
 
-    def generate_ids(self, prompt_ids, max_tokens: int = 100, reset: bool = True) -> list[int]:
+    def generate_ids(self, prompt_ids, max_tokens: int = 100, reset: bool = True, temperature: float = 0.0,
+                     seed: int = 0, eos_token: int | None = None) -> list[int]:
         """Token-id version of generate(): one launch runs the prompt (forced
-        tokens) and ``max_tokens`` greedy steps with on-device feedback."""
+        tokens) and ``max_tokens`` greedy (or, with ``temperature`` > 0,
+        sampled) steps with on-device feedback, stopping after ``eos_token``
+        if given."""
         if reset:
             self.reset()
         ids = [int(t) for t in prompt_ids]
@@ -336,10 +364,12 @@ class Decoder:
         n_steps = len(ids) - 1 + int(max_tokens)
         forced = torch.tensor(ids, dtype=torch.int32).pin_memory().to(self.device, non_blocking=True)
         log = torch.empty(n_steps, dtype=torch.int32, device=self.device)
-        self.decode_steps(n_steps, forced_tokens=forced, output_log=log)
-        out = log[len(ids) - 1 :].cpu().tolist()
+        self.decode_steps(n_steps, forced_tokens=forced, output_log=log, temperature=temperature, seed=seed,
+                          eos_token=eos_token, steps_done=self._steps_done)
+        ran = int(self._steps_done.item())
+        out = log[len(ids) - 1 : ran].cpu().tolist()
         self.check_status()
-        self._position += n_steps
+        self._position += ran
         return out
 
 

@@ -129,6 +129,11 @@ class QmkRunArgs(ctypes.Structure):
         ("trace_step", ctypes.c_int),
         ("poll_backoff_ns", ctypes.c_uint),
         ("tuning", ctypes.c_uint),
+        ("temperature", ctypes.c_float),
+        ("seed", ctypes.c_ulonglong),
+        ("stop_at_eos", ctypes.c_int),
+        ("eos_token", ctypes.c_int),
+        ("steps_done", ctypes.c_void_p),
     ]
 
 
@@ -164,6 +169,9 @@ def _valid_args(lib) -> QmkRunArgs:
         ("attn_scale", 0.0, 1),
         ("n_forced", 3, 1),  # forced count without a pointer
         ("k_cache", 0x10001, 1),  # misaligned tensor
+        ("temperature", -1.0, 1),
+        ("temperature", float("nan"), 1),
+        ("temperature", float("inf"), 1),
     ],
 )
 def test_qmk_run_rejects_bad_arguments(lib, field, value, code):
@@ -180,6 +188,15 @@ def test_qmk_run_rejects_positions_past_max_seq_len(lib):
     a.start_position = 2040
     a.num_steps = 9  # positions 2040..2048 > max_seq_len - 1
     assert lib.qmk_run(ctypes.byref(a), None) == 1
+
+
+def test_qmk_run_rejects_bad_eos_token(lib):
+    a = _valid_args(lib)
+    a.stop_at_eos = 1
+    for bad in (-1, 151936):
+        a.eos_token = bad
+        assert lib.qmk_run(ctypes.byref(a), None) == 1
+        assert b"eos_token" in lib.qmk_get_last_error_message()
 
 
 def test_workspace_init_rejects_small_buffer(lib):
