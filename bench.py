@@ -530,6 +530,61 @@ def run_profile_batch(B: int) -> int:
     return 0
 
 
+def run_long_context(args) -> int:
+    """BASELINE config 3 (not the headline line): the K/V cache holds bf16
+    N(0, 1) at positions [0, L) (seed 2), then one launch of args.steps
+    greedy decode steps at positions L, L+1, ... through the megakernel."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from qwen_megakernel_b200 import Decoder
+    from qwen_megakernel_b200.weights import random_weights, rope_tables
+
+    L, K, W = args.ctx, args.steps, args.warmup
+    msl = L + K + 8
+    weights = random_weights(seed=0, device="cuda", max_seq_len=2048)
+    weights["cos_table"], weights["sin_table"] = rope_tables(msl, device="cuda")
+    dec = Decoder(weights, max_seq_len=msl)
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    dec.k_cache[:, :, :L].normal_(generator=gen)
+    dec.v_cache[:, :, :L].normal_(generator=gen)
+    first = torch.tensor([17], dtype=torch.int32, device=dev)
+    log = torch.empty(K, dtype=torch.int32, device=dev)
+
+    def launch():
+        dec.decode_steps(K, forced_tokens=first, start_position=L, output_log=log)
+
+    for _ in range(W):
+        launch()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(0)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record()
+    for _ in range(reps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    dec.check_status()
+    ms = e0.elapsed_time(e1) / reps
+    launch_b = K * WEIGHT_BYTES + kv_bytes(L, K)
+    achieved = launch_b / (ms / 1000.0) / 1e9
+    peak, peak_kind = measured_peak()
+    print(json.dumps({
+        "metric": f"batch-1 decode tok/s (Qwen3-0.6B bf16, ctx {L})", "value": round(K / (ms / 1000.0), 2),
+        "unit": "tok/s", "n_gpus": 1, "steps": reps, "warmup": W, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights, K/V cache N(0,1) at positions [0, L))",
+        "config": {"workload": f"configs[3]-style: {K} greedy steps at positions {L}..{L + K - 1}, one launch",
+                   "ctx": L, "attention_splits_per_kv_head": 18},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": launch_b},
+        "per_token_us": round(ms / K * 1000.0, 2), "clocks": clocks}), flush=True)
+    return 0
+
+
 def run_prefill(args) -> int:
     """Token-parallel prompt prefill (not the headline line): a 1024-token
     prompt through Decoder.prefill_batched, args.steps timed repetitions."""
@@ -586,6 +641,8 @@ def main(argv=None) -> int:
     ap.add_argument("--batch", type=int, default=0, metavar="B",
                     help="config 4 instead of the headline: B sequences decoded together (token-parallel path)")
     ap.add_argument("--prefill", action="store_true", help="time the token-parallel 1024-token prefill instead")
+    ap.add_argument("--ctx", type=int, default=0, metavar="L",
+                    help="config 3 instead of the headline: batch-1 decode after L cached positions of random K/V")
     ap.add_argument("--profile-batch", type=int, default=0, metavar="B",
                     help="run only the small ncu case of the token-parallel path: one batched step of B rows")
     args = ap.parse_args(argv)
@@ -593,6 +650,8 @@ def main(argv=None) -> int:
         return run_profile_batch(args.profile_batch)
     if args.batch:
         return run_batch(args)
+    if args.ctx:
+        return run_long_context(args)
     if args.prefill:
         return run_prefill(args)
     if args.profile_case:

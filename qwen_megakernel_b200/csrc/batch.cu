@@ -576,12 +576,13 @@ Layout layout(int R, int O) {
   return L;
 }
 
-// Position splits of the attention for R rows: enough CTAs (8 R splits) to
-// cover the 148 SMs twice when the batch is small, one split otherwise.
+// Position splits of the attention for R rows: as many CTAs (8 R splits) as
+// fit resident at once (2 per SM on 148 SMs: one wave, no tail) when the
+// batch is small, one split otherwise.
 int attention_splits(int R) {
   using namespace qmb;
   if (R > kAttSplitRows) return 1;
-  const int s = (2 * 148 + kNumKVHeads * R - 1) / (kNumKVHeads * R);
+  const int s = (2 * 148) / (kNumKVHeads * R);
   return s < 1 ? 1 : (s > kAttMaxSplits ? kAttMaxSplits : s);
 }
 
