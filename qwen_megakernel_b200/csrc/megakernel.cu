@@ -231,7 +231,7 @@ __device__ __forceinline__ void raise_error(Ctx &c, unsigned code, unsigned site
   raise_error_at(c.abort_flag, c.ctrl, code, site, c.cta, c.cur_layer);
 }
 
-// Every 64th failed poll: abort / deadline / foreign-error checks (no sleep:
+// Every 16th failed poll: abort / deadline / foreign-error checks (no sleep:
 // a waiting warp only spins on its own poll, and a sleep would delay the
 // wake-up).  Returns
 // the (possibly newly set) deadline, or 0 when the wait must give up.
@@ -259,7 +259,7 @@ struct Waiter {
   unsigned it = 0;
   __device__ __forceinline__ bool keep_going(Ctx &c, unsigned site) {
     ++it;
-    if ((it & 63u) != 0u) return true;
+    if ((it & 15u) != 0u) return true;
     deadline = wait_checkpoint(c.abort_flag, c.ctrl, deadline, it, c.timeout_ns, site, c.cta, c.cur_layer);
     return deadline != 0;
   }
