@@ -24,16 +24,19 @@ def _rows(n, start=0, seq=0):
             torch.arange(start, start + n, dtype=torch.int32, device=dev))
 
 
-def test_batched_prefill_matches_oracle_small():
+@pytest.mark.parametrize("n_rows", [40, 150])
+def test_batched_prefill_matches_oracle_small(n_rows):
     """2-layer model, random norm weights: every prompt row's logits and the
-    K/V cache against the oracle's causal prefill."""
+    K/V cache against the oracle's causal prefill (40 rows: attention with
+    position splits and the split merge; 150 rows: one CTA per row and KV
+    head)."""
     from oracle.qwen3_mirror import MirrorDecoder
     from qwen_megakernel_b200 import BatchForward
 
     w = small_model(2)
     fw = BatchForward(w, 256)
     g = torch.Generator().manual_seed(3)
-    toks = torch.randint(0, V, (40,), generator=g, dtype=torch.int32)
+    toks = torch.randint(0, V, (n_rows,), generator=g, dtype=torch.int32)
     n = toks.numel()
     kc = torch.zeros(fw.cache_shape(), dtype=torch.bfloat16, device="cuda")
     vc = torch.zeros_like(kc)
