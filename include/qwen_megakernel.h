@@ -316,7 +316,15 @@ typedef struct QmkBatchArgs {
   void *workspace;                       /* device, qmk_batch_workspace_bytes() */
   size_t workspace_bytes;
   unsigned int *status;                  /* device uint32 [1] or NULL           */
+  int causal_run;                        /* nonzero: the caller guarantees that */
+                                         /* row r is position r of sequence 0  */
+                                         /* (a fresh prompt); for 64 < rows <= */
+                                         /* QMK_BATCH_GEMM_ATTN_MAX_ROWS the   */
+                                         /* attention then runs as two batched */
+                                         /* tensor-core GEMMs per layer        */
 } QmkBatchArgs;
+
+#define QMK_BATCH_GEMM_ATTN_MAX_ROWS 2048
 
 #define QMK_BATCH_MAX_ROWS 4096
 

@@ -76,9 +76,11 @@ class BatchForward:
         return (self.num_layers, NUM_KV_HEADS, self.max_seq_len, HEAD_DIM)
 
     def forward(self, k_cache, v_cache, num_seqs, tokens, row_seq, row_pos, out_rows=None, out_tokens=None,
-                logits=None, workspace=None) -> None:
+                logits=None, workspace=None, causal_run: bool = False) -> None:
         """Queue one forward pass (no host sync).  Caches: [num_seqs, L, 8, S, 128]
-        or, for one sequence, [L, 8, S, 128]."""
+        or, for one sequence, [L, 8, S, 128].  ``causal_run``: the caller
+        guarantees row r is position r of sequence 0 (a fresh prompt), which
+        lets the attention run as tensor-core GEMMs."""
         rows = int(tokens.numel())
         out = 0 if out_rows is None else int(out_rows.numel())
         ws = self.workspace(rows, out) if workspace is None else workspace
@@ -86,7 +88,7 @@ class BatchForward:
         self._ops.batch_forward(
             ws, self.embed, self.layer_ptrs, self.fused_ptrs, self.final_norm, self.lm_head, self.cos, self.sin, k_cache, v_cache,
             stride, int(num_seqs), self.num_layers, self.max_seq_len, self.attn_scale, tokens, row_seq, row_pos,
-            out_rows, out_tokens, logits, self.status)
+            out_rows, out_tokens, logits, self.status, 1 if causal_run else 0)
 
     def check_status(self) -> None:
         """Raise BatchError if a device-side check fired (after a sync)."""

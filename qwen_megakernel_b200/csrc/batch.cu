@@ -449,6 +449,99 @@ __global__ void __launch_bounds__(64) merge_kernel(const float *__restrict__ par
   store_att(a2, gridDim.y, r, 2 * g + hh, d, y);
 }
 
+// Prompt attention on the tensor cores (QmkBatchArgs.causal_run: the rows
+// are positions 0 .. R-1 of sequence 0).  Per KV head g the two q heads'
+// rows are stacked with their bf16 hi/lo halves, qs_g = [q_2g hi; q_2g+1 hi;
+// q_2g lo; q_2g+1 lo] (4R x 128), so scores = qs_g K_g^T and out = P_g V_g
+// are two batched GEMMs over the 8 heads (cuBLAS, fp32 accumulate) reading
+// the cache in place; between them one kernel adds the hi/lo score rows,
+// applies the causal mask and the softmax (exp2: q carries log2 e) and
+// writes P as a stacked bf16 hi/lo pair.
+constexpr int kGemmAttnMaxRows = 2048;
+
+// qs[g][hh R + r] (hi) and qs[g][2R + hh R + r] (lo) <- q[r][(2g + hh) 128 + :]
+__global__ void __launch_bounds__(256) qsplit_kernel(const float *__restrict__ q, __nv_bfloat16 *__restrict__ qs) {
+  const int r = blockIdx.x, R = gridDim.x;
+  const int c = 8 * threadIdx.x;  // 8 of the row's 2048 values
+  const int h = c >> 7, d = c & 127, g = h >> 1, hh = h & 1;
+  const float4 a = *reinterpret_cast<const float4 *>(q + (size_t)r * kQSize + c);
+  const float4 b = *reinterpret_cast<const float4 *>(q + (size_t)r * kQSize + c + 4);
+  const float va[4] = {a.x, a.y, a.z, a.w}, vb[4] = {b.x, b.y, b.z, b.w};
+  uint2 h0, l0, h1, l1;
+  split4(va, h0, l0);
+  split4(vb, h1, l1);
+  __nv_bfloat16 *hi = qs + ((size_t)g * 4 * R + (size_t)hh * R + r) * kHeadDim + d;
+  __nv_bfloat16 *lo = qs + ((size_t)g * 4 * R + 2 * (size_t)R + (size_t)hh * R + r) * kHeadDim + d;
+  *reinterpret_cast<uint4 *>(hi) = make_uint4(h0.x, h0.y, h1.x, h1.y);
+  *reinterpret_cast<uint4 *>(lo) = make_uint4(l0.x, l0.y, l1.x, l1.y);
+}
+
+// Softmax of score row i (< 2R: q head 2g + i / R, position r = i % R) over
+// keys j <= r: s_j = S[g][i][j] + S[g][2R + i][j]; P[g][i][j] / P[g][2R+i][j]
+// = bf16 hi / lo of exp2(s_j - max) / sum, zero for j > r.  Grid (2R, 8),
+// 256 threads, up to kGemmAttnMaxRows / 256 keys per thread.
+__global__ void __launch_bounds__(256) softmax_split_kernel(const float *__restrict__ S,
+                                                            __nv_bfloat16 *__restrict__ P, int R) {
+  __shared__ float red[8];
+  constexpr int kPer = kGemmAttnMaxRows / 256;
+  const int i = blockIdx.x, g = blockIdx.y, r = i % R;
+  const float *s_hi = S + ((size_t)g * 4 * R + i) * R;
+  const float *s_lo = S + ((size_t)g * 4 * R + 2 * (size_t)R + i) * R;
+  float v[kPer];
+  float m = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int j = threadIdx.x + 256 * k;
+    v[k] = (j <= r) ? s_hi[j] + s_lo[j] : -INFINITY;
+    m = fmaxf(m, v[k]);
+  }
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+  float l = 0.f;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    v[k] = (v[k] == -INFINITY) ? 0.f : fast_exp2(v[k] - m);
+    l += v[k];
+  }
+  const float inv = 1.f / block_sum256(l, red);  // key 0 is always present: sum >= 1
+  __nv_bfloat16 *p_hi = P + ((size_t)g * 4 * R + i) * R;
+  __nv_bfloat16 *p_lo = P + ((size_t)g * 4 * R + 2 * (size_t)R + i) * R;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int j = threadIdx.x + 256 * k;
+    if (j < R) {
+      const float pv = v[k] * inv;
+      const __nv_bfloat16 hb = __float2bfloat16(pv);
+      p_hi[j] = hb;
+      p_lo[j] = __float2bfloat16(pv - __bfloat162float(hb));
+    }
+  }
+}
+
+// att[r][(2g + hh) 128 + d] = O[g][hh R + r][d] + O[g][2R + hh R + r][d] -> the
+// stacked O-projection input.  Grid: rows, 256 threads, 8 values each.
+__global__ void __launch_bounds__(256) att_combine_kernel(const float *__restrict__ Ob, __nv_bfloat16 *__restrict__ a2) {
+  const int r = blockIdx.x, R = gridDim.x;
+  const int c = 8 * threadIdx.x;
+  const int h = c >> 7, d = c & 127, g = h >> 1, hh = h & 1;
+  const float *hi = Ob + ((size_t)g * 4 * R + (size_t)hh * R + r) * kHeadDim + d;
+  const float *lo = Ob + ((size_t)g * 4 * R + 2 * (size_t)R + (size_t)hh * R + r) * kHeadDim + d;
+#pragma unroll
+  for (int k = 0; k < 8; k += 4) {
+    const float4 x = *reinterpret_cast<const float4 *>(hi + k), y = *reinterpret_cast<const float4 *>(lo + k);
+    const float s4[4] = {x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w};
+    store_att(a2, R, r, h, d + k, s4);
+  }
+}
+
 // m = SiLU(gate) * up from the stacked gate|up GEMM output gu2 [2R, 6144],
 // split into the stacked down-projection input a2 [2R, 3072].  Grid: rows
 // (R = gridDim.x), 256 threads, 12 elements each.
@@ -548,7 +641,7 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 // Workspace regions for R rows and O output rows, in order (GEMM inputs and
 // outputs stacked: 2R or 2O rows, hi halves then lo halves).
 struct Layout {
-  size_t x, a2, qkv2, q, c2, gu2, partial, lm2, logits2, cublas, total;
+  size_t x, a2, qkv2, q, c2, gu2, partial, qs, sc, pr, ob, lm2, logits2, cublas, total;
 };
 
 Layout layout(int R, int O) {
@@ -569,6 +662,13 @@ Layout layout(int R, int O) {
   // split states (used up to kAttSplitRows rows; sized so that the total
   // grows with R: a workspace for R rows serves every smaller call)
   L.partial = take((size_t)(R < kAttSplitRows ? R : kAttSplitRows) * kNumKVHeads * kAttMaxSplits * kAttPartWords * 4);
+  // tensor-core prompt attention (causal runs of kAttSplitRows < R rows;
+  // sized for min(R, kGemmAttnMaxRows) so that the total grows with R)
+  const size_t Rg = (R > kAttSplitRows) ? (size_t)(R < kGemmAttnMaxRows ? R : kGemmAttnMaxRows) : 0;
+  L.qs = take(kNumKVHeads * 4 * Rg * kHeadDim * 2);
+  L.sc = take(kNumKVHeads * 4 * Rg * Rg * 4);
+  L.pr = take(kNumKVHeads * 4 * Rg * Rg * 2);
+  L.ob = take(kNumKVHeads * 4 * Rg * kHeadDim * 4);
   L.lm2 = take((size_t)2 * O * kHidden * 2);
   L.logits2 = take((size_t)2 * O * kVocab * 4);
   L.cublas = take(kCublasWorkspace);
@@ -670,6 +770,12 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
   float *c2 = reinterpret_cast<float *>(ws + Lw.c2);
   float *gu2 = reinterpret_cast<float *>(ws + Lw.gu2);
   float *partial = reinterpret_cast<float *>(ws + Lw.partial);
+  auto *qs = reinterpret_cast<__nv_bfloat16 *>(ws + Lw.qs);
+  float *sc = reinterpret_cast<float *>(ws + Lw.sc);
+  auto *pr = reinterpret_cast<__nv_bfloat16 *>(ws + Lw.pr);
+  float *ob = reinterpret_cast<float *>(ws + Lw.ob);
+  // causal run of a fresh prompt: attention as two tensor-core GEMMs per layer
+  const bool gemm_attn = a->causal_run && R > kAttSplitRows && R <= kGemmAttnMaxRows;
   auto *lm2 = reinterpret_cast<__nv_bfloat16 *>(ws + Lw.lm2);
   float *logits2 = reinterpret_cast<float *>(ws + Lw.logits2);
   auto *kc = static_cast<__nv_bfloat16 *>(a->k_cache);
@@ -696,9 +802,29 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
     qk_rope_kv_kernel<<<R, 256, 0, stream>>>(qkv2, bf(P[4]), bf(P[5]), cos_t, sin_t, a->row_seq, a->row_pos, kc, vc,
                                             a->kv_seq_stride, a->num_seqs, l, a->max_seq_len,
                                             a->attn_scale * kLog2e, q, a->status);
-    attention_kernel<<<dim3(kNumKVHeads, R, splits), 256, 0, stream>>>(
-        q, kc, vc, a->kv_seq_stride, a->num_seqs, l, a->max_seq_len, a->row_seq, a->row_pos, splits, partial, a2);
-    if (splits > 1) merge_kernel<<<dim3(kNumKVHeads, R), 64, 0, stream>>>(partial, splits, a2);
+    if (gemm_attn) {
+      // scores = qs K^T and out = P V per KV head, the cache read in place
+      const long long head = (long long)a->max_seq_len * kHeadDim;  // elements between KV heads
+      const __nv_bfloat16 *kl = kc + (size_t)l * kNumKVHeads * head, *vl = vc + (size_t)l * kNumKVHeads * head;
+      const float one = 1.f, zero = 0.f;
+      qsplit_kernel<<<R, 256, 0, stream>>>(q, qs);
+      s = cublasGemmStridedBatchedEx(h, CUBLAS_OP_T, CUBLAS_OP_N, R, 4 * R, kHeadDim, &one, kl, CUDA_R_16BF, kHeadDim,
+                                     head, qs, CUDA_R_16BF, kHeadDim, (long long)4 * R * kHeadDim, &zero, sc,
+                                     CUDA_R_32F, R, (long long)4 * R * R, kNumKVHeads, CUBLAS_COMPUTE_32F,
+                                     CUBLAS_GEMM_DEFAULT);
+      if (s != CUBLAS_STATUS_SUCCESS) break;
+      softmax_split_kernel<<<dim3(2 * R, kNumKVHeads), 256, 0, stream>>>(sc, pr, R);
+      s = cublasGemmStridedBatchedEx(h, CUBLAS_OP_N, CUBLAS_OP_N, kHeadDim, 4 * R, R, &one, vl, CUDA_R_16BF, kHeadDim,
+                                     head, pr, CUDA_R_16BF, R, (long long)4 * R * R, &zero, ob, CUDA_R_32F, kHeadDim,
+                                     (long long)4 * R * kHeadDim, kNumKVHeads, CUBLAS_COMPUTE_32F,
+                                     CUBLAS_GEMM_DEFAULT);
+      if (s != CUBLAS_STATUS_SUCCESS) break;
+      att_combine_kernel<<<R, 256, 0, stream>>>(ob, a2);
+    } else {
+      attention_kernel<<<dim3(kNumKVHeads, R, splits), 256, 0, stream>>>(
+          q, kc, vc, a->kv_seq_stride, a->num_seqs, l, a->max_seq_len, a->row_seq, a->row_pos, splits, partial, a2);
+      if (splits > 1) merge_kernel<<<dim3(kNumKVHeads, R), 64, 0, stream>>>(partial, splits, a2);
+    }
     s = gemm(h, R2, kHidden, kQSize, P[6], a2, c2, kHidden);
     if (s != CUBLAS_STATUS_SUCCESS) break;
     residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, c2, nullptr, R, bf(P[7]), a2);  // x += O-proj

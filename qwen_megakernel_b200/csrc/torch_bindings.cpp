@@ -318,7 +318,7 @@ void batch_forward(torch::Tensor workspace, torch::Tensor embed_weight, std::vec
                    int64_t num_seqs, int64_t num_layers, int64_t max_seq_len, double attn_scale,
                    torch::Tensor tokens, torch::Tensor row_seq, torch::Tensor row_pos,
                    std::optional<torch::Tensor> out_rows, std::optional<torch::Tensor> out_tokens,
-                   std::optional<torch::Tensor> logits, std::optional<torch::Tensor> status) {
+                   std::optional<torch::Tensor> logits, std::optional<torch::Tensor> status, int64_t causal_run) {
   check_cuda(embed_weight, "embed_weight");
   for (const auto *t : {&workspace, &final_norm_weight, &lm_head_weight, &cos_table, &sin_table, &k_cache, &v_cache,
                         &tokens, &row_seq, &row_pos}) {
@@ -395,6 +395,7 @@ void batch_forward(torch::Tensor workspace, torch::Tensor embed_weight, std::vec
   a.num_out = (int)O;
   a.workspace = workspace.data_ptr();
   a.workspace_bytes = workspace.nbytes();
+  a.causal_run = causal_run ? 1 : 0;
   c10::cuda::CUDAGuard guard(embed_weight.device());
   raise_if_error(qmk_batch_forward(&a, c10::cuda::getCurrentCUDAStream().stream()));
 }
@@ -477,7 +478,7 @@ TORCH_LIBRARY(qwen_megakernel_C, ops) {
       "Tensor lm_head_weight, Tensor cos_table, Tensor sin_table, Tensor k_cache, Tensor v_cache, "
       "int kv_seq_stride, int num_seqs, int num_layers, int max_seq_len, float attn_scale, "
       "Tensor tokens, Tensor row_seq, Tensor row_pos, Tensor? out_rows, Tensor? out_tokens, "
-      "Tensor? logits, Tensor? status) -> ()");
+      "Tensor? logits, Tensor? status, int causal_run=0) -> ()");
   ops.impl("batch_forward", torch::kCUDA, &batch_forward);
   ops.def("batch_workspace_bytes(int num_rows, int num_out) -> int", &batch_workspace_bytes);
 

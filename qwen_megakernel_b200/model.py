@@ -318,7 +318,8 @@ class Decoder:
             row_seq = torch.zeros(c1 - c0, dtype=torch.int32, device=self.device)
             out_rows = torch.full((1,), c1 - c0 - 1, dtype=torch.int32, device=self.device) if last else None
             fw.forward(self._k_cache, self._v_cache, 1, tokens, row_seq, row_pos, out_rows,
-                       self._out_token if last else None, logits if last else None)
+                       self._out_token if last else None, logits if last else None,
+                       causal_run=(start + c0 == 0))
         tok = int(self._out_token.item())
         fw.check_status()
         self._position += n

@@ -40,6 +40,7 @@ class QmkBatchArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
         ("status", ctypes.c_void_p),
+        ("causal_run", ctypes.c_int),
     ]
 
 

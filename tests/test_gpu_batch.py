@@ -24,12 +24,12 @@ def _rows(n, start=0, seq=0):
             torch.arange(start, start + n, dtype=torch.int32, device=dev))
 
 
-@pytest.mark.parametrize("n_rows", [40, 150])
-def test_batched_prefill_matches_oracle_small(n_rows):
+@pytest.mark.parametrize("n_rows,causal_run", [(40, False), (150, False), (150, True)])
+def test_batched_prefill_matches_oracle_small(n_rows, causal_run):
     """2-layer model, random norm weights: every prompt row's logits and the
     K/V cache against the oracle's causal prefill (40 rows: attention with
     position splits and the split merge; 150 rows: one CTA per row and KV
-    head)."""
+    head, or -- declared a causal run -- the tensor-core GEMM attention)."""
     from oracle.qwen3_mirror import MirrorDecoder
     from qwen_megakernel_b200 import BatchForward
 
@@ -44,7 +44,7 @@ def test_batched_prefill_matches_oracle_small(n_rows):
     out_rows = torch.arange(n, dtype=torch.int32, device="cuda")
     out_tok = torch.empty(n, dtype=torch.int32, device="cuda")
     logits = torch.empty(n, V, device="cuda")
-    fw.forward(kc, vc, 1, toks.cuda(), seq, pos, out_rows, out_tok, logits)
+    fw.forward(kc, vc, 1, toks.cuda(), seq, pos, out_rows, out_tok, logits, causal_run=causal_run)
     torch.cuda.synchronize()
     fw.check_status()
     m = MirrorDecoder(w, 256, device="cuda")
@@ -108,7 +108,8 @@ def test_batched_prefill_config1_vs_golden(cuda_weights, fw28, golden1):
     seq, pos = _rows(n)
     out_rows = torch.arange(P - 1, n, dtype=torch.int32, device="cuda")
     logits = torch.empty(n - P + 1, V, device="cuda")
-    fw28.forward(kc, vc, 1, torch.tensor(stream, dtype=torch.int32, device="cuda"), seq, pos, out_rows, None, logits)
+    fw28.forward(kc, vc, 1, torch.tensor(stream, dtype=torch.int32, device="cuda"), seq, pos, out_rows, None, logits,
+                 causal_run=True)
     torch.cuda.synchronize()
     fw28.check_status()
     _check_against_golden(logits, g)
