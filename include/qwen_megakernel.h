@@ -180,7 +180,11 @@ typedef struct QmkRunArgs {
   int eos_token;                         /* first GENERATED token == eos_token    */
                                          /* (forced tokens never stop it)         */
   int *steps_done;                       /* device int32 [1] or NULL: steps run   */
+  int top_k;                             /* 1..QMK_TOP_K_MAX: sample only among   */
+                                         /* the top_k logits (0: all)             */
 } QmkRunArgs;
+
+#define QMK_TOP_K_MAX 64
 
 /* Bytes of device workspace one decoder needs (flags, dataflow buffers). */
 size_t qmk_workspace_bytes(void);
@@ -247,7 +251,7 @@ int qmk_trace_words(void);
  *    the last call) and of the QmkStatus block (device memory: copy it to
  *    the host after the stream completes). */
 #define QMK_STATIC_MAX_STEPS 4096
-#define QMK_STATIC_SCRATCH_BYTES (448 * 1024)
+#define QMK_STATIC_SCRATCH_BYTES (512 * 1024)
 
 int qmk_generate_static(int first_token_id, int num_steps, const void *embed_weight,
                         const LDGLayerWeights *layer_weights, const void *final_norm_weight,

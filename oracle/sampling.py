@@ -8,7 +8,8 @@ an extension (survey row f3).  Its defining semantics are the standard ones:
 the next token is a draw from softmax(logits / T).  The kernel draws it with
 the Gumbel-max trick (Gumbel 1954; e.g. Maddison, Tarlow and Minka 2014):
 argmax_i(logit_i / T + g_i) with i.i.d. standard Gumbel g_i is distributed as
-softmax(logits / T).  The noise is a deterministic function of
+softmax(logits / T); top-k restricts the argmax to the logits >= the k-th
+largest (an exact draw from the renormalized top-k softmax).  The noise is a deterministic function of
 (seed, cache position, vocabulary index):
 
     z  = seed XOR (position << 20 | index)
@@ -45,11 +46,16 @@ def gumbel(seed: int, position: int, index: np.ndarray) -> np.ndarray:
     return -np.log(-np.log(u))
 
 
-def sample(logits: np.ndarray, temperature: float, seed: int, position: int) -> tuple[int, float]:
+def sample(logits: np.ndarray, temperature: float, seed: int, position: int, top_k: int = 0) -> tuple[int, float]:
     """Token the kernel draws from fp32 logits [vocab] at `position`, and the
     gap between the best and second-best perturbed keys (how robust the
-    choice is to the kernel's fp32 rounding of the same keys)."""
+    choice is to the kernel's fp32 rounding of the same keys).  With top_k
+    > 0 only logits >= the top_k-th largest take part (ties at the threshold
+    included, as in the kernel)."""
     v = logits.shape[-1]
     keys = logits.astype(np.float64) / temperature + gumbel(seed, position, np.arange(v))
+    if top_k > 0:
+        tau = np.partition(logits, -top_k)[-top_k]
+        keys = np.where(logits >= tau, keys, -np.inf)
     top2 = np.partition(keys, -2)[-2:]
     return int(np.argmax(keys)), float(top2[1] - top2[0])

@@ -62,6 +62,7 @@ enum Site : unsigned {
   kSiteKVReady = 10,
   kSiteToken = 11,
   kSiteMma = 12,
+  kSiteTopk = 13,
 };
 
 struct Params {
@@ -96,6 +97,7 @@ struct Params {
   unsigned tuning;
   float inv_temp;       // sampling: 1 / temperature, 0 = greedy
   unsigned long long seed;
+  int top_k;            // sampling restricted to the top_k logits (0: all)
   int eos_token;        // stop after a generated token equal to this (-1: never)
   int *steps_done;      // optional: steps executed (< num_steps after an EOS stop)
 };
@@ -157,6 +159,7 @@ struct Ctx {
   int *token_slot;
   Ctrl *ctrl;
   uint64_t *wX, *wQKV, *wPart, *wAtt, *wA, *wM, *wArg;
+  uint64_t *wTopk;  // top-k sampling: [cta][top_k] candidate keys
   int cta, ncta;
   unsigned E0;
   unsigned long long timeout_ns;
@@ -810,6 +813,8 @@ struct Consumer {
   int lm_best_i = 0x7fffffff;
   float *lm_logits = nullptr;
   int lm_pos = 0;             // LM head: cache position of the step (sampling key)
+  float *lm_vals = nullptr;   // top-k sampling: this CTA's logits (smem), row - lm_r0
+  int lm_r0 = 0;
   unsigned mma_issued = 0;   // issuer threads: 1 + the last unit this thread issued
   bool tc_prewaited = false; // issuer threads: the next phase's first unit needs no waits
   NormPairs nw_pref;         // RMSNorm weights of the next normalized GEMV input
@@ -921,6 +926,11 @@ struct Consumer {
         break;
       default: {  // kOutLM
         const float y = v * job.scale;
+        if (lm_vals) {  // top-k sampling: the selection runs on all rows afterwards
+          lm_vals[row - lm_r0] = y;
+          if (lm_logits) lm_logits[row] = y;
+          break;
+        }
         // greedy: the logit; sampling: logit / T + Gumbel noise
         const float key = (p.inv_temp > 0.f) ? fmaf(y, p.inv_temp, gumbel_noise(p.seed, lm_pos, row)) : y;
         if (key > lm_best || (key == lm_best && row < lm_best_i)) {
@@ -1433,6 +1443,113 @@ struct Consumer {
     trace_stamp(c, tid == 0, l * 16 + 11);
   }
 
+  // k-th largest (1 <= k <= n) of the n keys get(0 .. n-1), all consumer
+  // threads: most-significant-digit radix select, 4 passes of 8 bits with a
+  // 256-bin histogram in smem (hist) and the pass result in bc[0..1].
+  template <class GetKey>
+  __device__ unsigned kth_largest_key(int n, int k, GetKey get, unsigned *hist, unsigned *bc) {
+    unsigned prefix = 0u, mask = 0u;
+    unsigned kk = (unsigned)k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = tid; i < 256; i += kConsumerThreads) hist[i] = 0u;
+      consumer_sync();
+      for (int i = tid; i < n; i += kConsumerThreads) {
+        const unsigned key = get(i);
+        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
+      consumer_sync();
+      if (warp == 0) {
+        // lane l sums bins 255 - 8l .. 248 - 8l (descending digits)
+        unsigned cnt[8], sum = 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          cnt[j] = hist[255 - 8 * lane - j];
+          sum += cnt[j];
+        }
+        unsigned incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const unsigned excl = incl - sum;
+        if (excl < kk && kk <= incl) {
+          unsigned run = excl;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (run < kk && kk <= run + cnt[j]) {
+              bc[0] = 255u - 8u * lane - j;
+              bc[1] = kk - run;
+            }
+            run += cnt[j];
+          }
+        }
+      }
+      consumer_sync();
+      prefix |= bc[0] << shift;
+      mask |= 255u << shift;
+      kk = bc[1];
+    }
+    return prefix;
+  }
+
+  // Top-k sampling: every CTA publishes the keys of its top_k logits, every
+  // CTA then finds the global top_k-th key tau from all candidates and draws
+  // its local Gumbel-max among its logits with key >= tau; the usual argmax
+  // exchange picks the grid's winner (an exact draw from softmax(logits / T)
+  // restricted to the logits >= the top_k-th largest).
+  __device__ void topk_select(unsigned E) {
+    const Range R = lm_rows(c.cta, c.ncta);
+    const int n = R.end - R.begin, k = p.top_k;
+    unsigned *hist = reinterpret_cast<unsigned *>(sA);  // free during the LM head
+    unsigned *bc = hist + 256;
+    const float *vals = lm_vals;
+    consumer_sync();  // every row's logit is in smem
+    const unsigned kc = kth_largest_key(n, k, [&](int i) { return float_order_key(vals[i]); }, hist, bc);
+    if (tid == 0) bc[2] = 0u;
+    consumer_sync();
+    uint64_t *mine = c.wTopk + (size_t)c.cta * k;
+    for (int i = tid; i < n; i += kConsumerThreads) {
+      const unsigned key = float_order_key(vals[i]);
+      if (key > kc && live()) put(mine + atomicAdd(&bc[2], 1u), ll_pack_u(key, E));
+    }
+    consumer_sync();
+    for (int i = (int)bc[2] + tid; i < k; i += kConsumerThreads)
+      if (live()) put(mine + i, ll_pack_u(kc, E));
+    flush();
+    // wait for every CTA's candidates (word j * kConsumerThreads + tid of
+    // this thread, at most 64 per thread)
+    const int total = c.ncta * k;
+    unsigned long long pending = 0ull;
+    for (int j = 0; j < 64 && j * kConsumerThreads + tid < total; ++j) pending |= 1ull << j;
+    if (*c.abort_flag) pending = 0ull;
+    Waiter w;
+    while (pending) {
+      for (int j = 0; j < 64; ++j) {
+        if ((pending >> j) & 1ull) {
+          if (ll_flag(ll_load(c.wTopk + j * kConsumerThreads + tid)) == E) pending &= ~(1ull << j);
+        }
+      }
+      if (!pending || !w.keep_going(c, kSiteTopk)) break;
+    }
+    consumer_sync();
+    const unsigned tau = kth_largest_key(
+        total, k, [&](int i) { return (unsigned)(ll_load(c.wTopk + i) & 0xffffffffull); }, hist, bc);
+    lm_best = -INFINITY;
+    lm_best_i = 0x7fffffff;
+    for (int i = tid; i < n; i += kConsumerThreads) {
+      const float v = vals[i];
+      if (float_order_key(v) >= tau) {
+        const int row = R.begin + i;
+        const float key = (p.inv_temp > 0.f) ? fmaf(v, p.inv_temp, gumbel_noise(p.seed, lm_pos, row)) : v;
+        if (key > lm_best || (key == lm_best && row < lm_best_i)) {
+          lm_best = key;
+          lm_best_i = row;
+        }
+      }
+    }
+  }
+
   // Final RMSNorm + LM head rows + CTA argmax -> ARG words.
   __device__ void phase_lm_head(int step, unsigned E_x, unsigned E) {
     const NormPairs nw = nw_pref;  // fetched in the last P5
@@ -1450,8 +1567,12 @@ struct Consumer {
     lm_best_i = 0x7fffffff;
     lm_logits = p.logits ? (p.logits + (size_t)step * kVocab) : nullptr;
     lm_pos = p.start_pos + step;
+    // top-k: the logits stay in smem after the LM-head B operand (sU[0, 1024))
+    lm_vals = (p.top_k > 0) ? sU + kHidden : nullptr;
+    lm_r0 = R.begin;
     const TcJob job{kTcRow, kOutLM, R.begin, R.end, kLMTileRows, rstd, E};
     tc_phase(job, bop);
+    if (lm_vals) topk_select(E);
     float best = lm_best;
     int best_i = lm_best_i;
     // warp argmax (largest value, lowest row on ties)
@@ -1615,6 +1736,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   c.wA = reinterpret_cast<uint64_t *>(p.ws + kOffA);
   c.wM = reinterpret_cast<uint64_t *>(p.ws + kOffM);
   c.wArg = reinterpret_cast<uint64_t *>(p.ws + kOffArg);
+  c.wTopk = reinterpret_cast<uint64_t *>(p.ws + kOffTopk);
   c.cta = blockIdx.x;
   c.ncta = gridDim.x;
   c.timeout_ns = p.timeout_ns;
@@ -1682,7 +1804,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         // every other CTA has finished, nothing reads them concurrently.
         next = 0;
         uint64_t *ll = reinterpret_cast<uint64_t *>(p.ws + kOffX);
-        const long long nwords = (kOffArg + 8LL * kWordsArg - kOffX) / 8;
+        const long long nwords = (kOffLLEnd - kOffX) / 8;
         for (long long i = 0; i < nwords; ++i) ll[i] = 0ull;
         __threadfence();
       }
@@ -1878,6 +2000,8 @@ int qmk_run(const QmkRunArgs *a, cudaStream_t stream) {
     return set_error(QMK_ERR_ARGS, "qmk_run: attn_scale must be positive");
   if (!(a->temperature >= 0.f) || a->temperature > 1e30f)
     return set_error(QMK_ERR_ARGS, "qmk_run: temperature must be finite and >= 0");
+  if (a->top_k < 0 || a->top_k > qmk::kMaxTopK)
+    return set_error(QMK_ERR_ARGS, "qmk_run: top_k=%d outside [0, %d]", a->top_k, qmk::kMaxTopK);
   if (a->stop_at_eos && (a->eos_token < 0 || a->eos_token >= QMK_VOCAB))
     return set_error(QMK_ERR_ARGS, "qmk_run: eos_token %d outside [0, %d)", a->eos_token, QMK_VOCAB);
   const void *ptrs[] = {a->embed_weight, a->final_norm_weight, a->lm_head_weight, a->cos_table,
@@ -1895,6 +2019,9 @@ int qmk_run(const QmkRunArgs *a, cudaStream_t stream) {
     ncta = g_devices[dev].num_sms;
   }
   if (ncta > qmk::kMaxCtas) ncta = qmk::kMaxCtas;
+  // top-k keeps a CTA's LM-head logits in 2048 floats of shared memory
+  if (a->top_k > 0 && (qmk::kVocab + ncta - 1) / ncta > 2 * qmk::kHidden)
+    return set_error(QMK_ERR_ARGS, "qmk_run: top_k needs at least %d SMs", (qmk::kVocab + 2 * qmk::kHidden - 1) / (2 * qmk::kHidden));
   if (ncta < qmk::kMinCtas)
     return set_error(QMK_ERR_LAUNCH, "qmk_run: %d SMs < %d required", ncta, qmk::kMinCtas);
 
@@ -1931,6 +2058,7 @@ int qmk_run(const QmkRunArgs *a, cudaStream_t stream) {
   p.inv_temp = a->temperature > 0.f ? 1.0f / a->temperature : 0.f;
   p.seed = a->seed;
   p.eos_token = a->stop_at_eos ? a->eos_token : -1;
+  p.top_k = a->top_k;
   p.steps_done = a->steps_done;
 
   void *kargs[] = {&p};

@@ -105,6 +105,8 @@ constexpr int kWordsAtt = kQSize;
 constexpr int kWordsA = kHidden;
 constexpr int kWordsM = kInter;
 constexpr int kWordsArg = 2 * kMaxCtas;
+constexpr int kMaxTopK = 64;                       // top-k sampling: candidate keys per CTA
+constexpr int kWordsTopk = kMaxTopK * kMaxCtas;
 constexpr long long kOffX = kCtrlBytes;
 constexpr long long kOffQKV = kOffX + 8LL * kWordsX;
 constexpr long long kOffPart = kOffQKV + 8LL * kWordsQKV;
@@ -112,7 +114,9 @@ constexpr long long kOffAtt = kOffPart + 8LL * kWordsPart;
 constexpr long long kOffA = kOffAtt + 8LL * kWordsAtt;
 constexpr long long kOffM = kOffA + 8LL * kWordsA;
 constexpr long long kOffArg = kOffM + 8LL * kWordsM;
-constexpr long long kWorkspaceBytes = ((kOffArg + 8LL * kWordsArg) + 4095) / 4096 * 4096;
+constexpr long long kOffTopk = kOffArg + 8LL * kWordsArg;
+constexpr long long kOffLLEnd = kOffTopk + 8LL * kWordsTopk;  // end of the dataflow words
+constexpr long long kWorkspaceBytes = (kOffLLEnd + 4095) / 4096 * 4096;
 
 // Control block (first kCtrlBytes of the workspace).
 struct Ctrl {

@@ -210,7 +210,7 @@ void run(torch::Tensor workspace, torch::Tensor embed_weight, torch::Tensor laye
          std::optional<torch::Tensor> status, int64_t timeout_ns, int64_t debug_stall,
          std::optional<torch::Tensor> trace, int64_t trace_step, int64_t poll_backoff_ns,
          int64_t tuning, double temperature, int64_t seed, int64_t stop_at_eos, int64_t eos_token,
-         std::optional<torch::Tensor> steps_done) {
+         std::optional<torch::Tensor> steps_done, int64_t top_k) {
   QMK_CHECK(num_steps >= 1, "num_steps must be >= 1");
   QMK_CHECK(start_position >= 0, "start_position must be >= 0");
   check_model(embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight, cos_table,
@@ -300,6 +300,7 @@ void run(torch::Tensor workspace, torch::Tensor embed_weight, torch::Tensor laye
   a.seed = (unsigned long long)seed;
   a.stop_at_eos = stop_at_eos ? 1 : 0;
   a.eos_token = (int)eos_token;
+  a.top_k = (int)top_k;
   if (steps_done.has_value()) {
     check_dtype(*steps_done, torch::kInt32, "steps_done", "int32");
     check_same_device(*steps_done, embed_weight, "steps_done");
@@ -469,7 +470,7 @@ TORCH_LIBRARY(qwen_megakernel_C, ops) {
       "Tensor? output_log, Tensor? output_token, Tensor? logits, Tensor? final_hidden, "
       "Tensor? status, int timeout_ns=0, int debug_stall=0, Tensor? trace=None, "
       "int trace_step=0, int poll_backoff_ns=0, int tuning=0, float temperature=0.0, int seed=0, "
-      "int stop_at_eos=0, int eos_token=0, Tensor? steps_done=None) -> ()");
+      "int stop_at_eos=0, int eos_token=0, Tensor? steps_done=None, int top_k=0) -> ()");
   ops.impl("run", torch::kCUDA, &run);
 
   ops.def(

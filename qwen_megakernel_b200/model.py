@@ -193,6 +193,7 @@ class Decoder:
         seed: int = 0,
         eos_token: int | None = None,
         steps_done: torch.Tensor | None = None,
+        top_k: int = 0,
     ) -> None:
         """Queue one launch of ``num_steps`` decode steps (no host sync).
 
@@ -201,7 +202,8 @@ class Decoder:
         position ``start_position + t``; it writes its argmax to
         ``output_log[t]`` and its fp32 logits to ``logits[t]`` if given.
         ``temperature`` > 0 samples instead of taking the argmax (Gumbel-max,
-        reproducible per (seed, position)); with ``eos_token`` the launch ends
+        reproducible per (seed, position)), among the ``top_k`` largest logits
+        if ``top_k`` > 0; with ``eos_token`` the launch ends
         after the first generated token equal to it, and ``steps_done``
         (device int32 [1]) receives the number of steps run."""
         start = self._position if start_position is None else int(start_position)
@@ -242,6 +244,7 @@ class Decoder:
             0 if eos_token is None else 1,
             0 if eos_token is None else int(eos_token),
             steps_done,
+            int(top_k),
         )
 
     # ------------------------------------------------------- reference API
@@ -326,7 +329,8 @@ class Decoder:
         return tok
 
     def generate_from(self, token_id: int, max_tokens: int, position: int | None = None,
-                      temperature: float = 0.0, seed: int = 0, eos_token: int | None = None) -> list[int]:
+                      temperature: float = 0.0, seed: int = 0, eos_token: int | None = None,
+                      top_k: int = 0) -> list[int]:
         """Continuation from the current KV cache: consume ``token_id`` at
         ``position`` (default: the decoder's position) and return ``max_tokens``
         generated ids -- the semantics of the reference's ``generate_nosync``
@@ -341,7 +345,7 @@ class Decoder:
         log = torch.empty(n, dtype=torch.int32, device=self.device)
         done = self._steps_done
         self.decode_steps(n, forced_tokens=dev_tok, start_position=pos, output_log=log, temperature=temperature,
-                          seed=seed, eos_token=eos_token, steps_done=done)
+                          seed=seed, eos_token=eos_token, steps_done=done, top_k=top_k)
         host = torch.empty(n + 1, dtype=torch.int32).pin_memory()
         host[:n].copy_(log, non_blocking=True)
         host[n:].copy_(done, non_blocking=True)
@@ -352,7 +356,7 @@ class Decoder:
         return host[:ran].tolist()
 
     def generate_ids(self, prompt_ids, max_tokens: int = 100, reset: bool = True, temperature: float = 0.0,
-                     seed: int = 0, eos_token: int | None = None) -> list[int]:
+                     seed: int = 0, eos_token: int | None = None, top_k: int = 0) -> list[int]:
         """Token-id version of generate(): one launch runs the prompt (forced
         tokens) and ``max_tokens`` greedy (or, with ``temperature`` > 0,
         sampled) steps with on-device feedback, stopping after ``eos_token``
@@ -366,7 +370,7 @@ class Decoder:
         forced = torch.tensor(ids, dtype=torch.int32).pin_memory().to(self.device, non_blocking=True)
         log = torch.empty(n_steps, dtype=torch.int32, device=self.device)
         self.decode_steps(n_steps, forced_tokens=forced, output_log=log, temperature=temperature, seed=seed,
-                          eos_token=eos_token, steps_done=self._steps_done)
+                          eos_token=eos_token, steps_done=self._steps_done, top_k=top_k)
         ran = int(self._steps_done.item())
         out = log[len(ids) - 1 : ran].cpu().tolist()
         self.check_status()

@@ -134,6 +134,7 @@ class QmkRunArgs(ctypes.Structure):
         ("stop_at_eos", ctypes.c_int),
         ("eos_token", ctypes.c_int),
         ("steps_done", ctypes.c_void_p),
+        ("top_k", ctypes.c_int),
     ]
 
 
@@ -172,6 +173,8 @@ def _valid_args(lib) -> QmkRunArgs:
         ("temperature", -1.0, 1),
         ("temperature", float("nan"), 1),
         ("temperature", float("inf"), 1),
+        ("top_k", -1, 1),
+        ("top_k", 65, 1),
     ],
 )
 def test_qmk_run_rejects_bad_arguments(lib, field, value, code):

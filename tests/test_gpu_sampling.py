@@ -25,11 +25,11 @@ def _decoder(seed=7):
     return Decoder(small_model(2, seed=seed), max_seq_len=256)
 
 
-def _sample_run(dec, first, start, n, seed=SEED, temperature=T):
+def _sample_run(dec, first, start, n, seed=SEED, temperature=T, top_k=0):
     log = torch.empty(n, dtype=torch.int32, device="cuda")
     logits = torch.empty(n, V, device="cuda")
     dec.decode_steps(n, forced_tokens=torch.tensor([first], dtype=torch.int32, device="cuda"), start_position=start,
-                     output_log=log, logits=logits, temperature=temperature, seed=seed)
+                     output_log=log, logits=logits, temperature=temperature, seed=seed, top_k=top_k)
     torch.cuda.synchronize()
     dec.check_status()
     return log.cpu().numpy(), logits.cpu().numpy()
@@ -100,3 +100,22 @@ def test_eos_in_forced_tokens_does_not_stop():
     b = _decoder()
     assert b.generate_ids(prompt, 6, eos_token=13) == full[: (full.index(13) + 1 if 13 in full else 6)]
     assert b.position >= len(prompt) - 1
+
+
+@pytest.mark.parametrize("top_k", [1, 5, 40, 64])
+def test_top_k_draws_match_oracle(top_k):
+    """Top-k sampling: every drawn token is the oracle's Gumbel-max over the
+    top_k largest of the kernel's own logits (top_k = 1: the greedy token)."""
+    from oracle.sampling import sample
+
+    dec = _decoder()
+    dec.prefill(list(range(100, 120)))
+    toks, logits = _sample_run(dec, 5, 20, 16, top_k=top_k)
+    for t in range(len(toks)):
+        want, gap = sample(logits[t], T, SEED, 20 + t, top_k=top_k)
+        if top_k == 1:
+            assert toks[t] == int(np.argmax(logits[t]))
+        elif gap > 1e-3:
+            assert toks[t] == want, f"step {t}: kernel {toks[t]}, oracle {want}"
+        top = np.partition(logits[t], -top_k)[-top_k]
+        assert logits[t][toks[t]] >= top, "drawn token outside the top-k set"

@@ -37,3 +37,23 @@ def test_draws_follow_softmax():
     for pos in range(n):
         counts[sample(logits, T, seed=99, position=pos)[0]] += 1
     assert np.abs(counts / n - p).max() < 0.01
+
+
+def test_top_k_draws_follow_renormalized_softmax():
+    logits = np.array([1.0, 0.5, 0.0, -1.0, 2.0, 1.5], dtype=np.float32)
+    T, k = 0.9, 3
+    top = np.argsort(-logits)[:k]
+    p = np.zeros(len(logits))
+    p[top] = np.exp(logits[top] / T) / np.exp(logits[top] / T).sum()
+    n = 30_000
+    counts = np.zeros(len(logits))
+    for pos in range(n):
+        counts[sample(logits, T, seed=7, position=pos, top_k=k)[0]] += 1
+    assert counts[np.setdiff1d(np.arange(len(logits)), top)].sum() == 0
+    assert np.abs(counts / n - p).max() < 0.012
+
+
+def test_top_1_is_greedy():
+    logits = np.random.default_rng(3).standard_normal(5000).astype(np.float32)
+    for pos in range(50):
+        assert sample(logits, 1.3, seed=11, position=pos, top_k=1)[0] == int(np.argmax(logits))
