@@ -801,6 +801,9 @@ struct Producer {
 };
 
 // ------------------------------------------------------------- consumer
+// kTopK: the top-k sampling variant (a separate kernel instance, so that the
+// common paths carry none of its code).
+template <bool kTopK>
 struct Consumer {
   Ctx &c;
   const Params &p;
@@ -813,8 +816,6 @@ struct Consumer {
   int lm_best_i = 0x7fffffff;
   float *lm_logits = nullptr;
   int lm_pos = 0;             // LM head: cache position of the step (sampling key)
-  float *lm_vals = nullptr;   // top-k sampling: this CTA's logits (smem), row - lm_r0
-  int lm_r0 = 0;
   unsigned mma_issued = 0;   // issuer threads: 1 + the last unit this thread issued
   bool tc_prewaited = false; // issuer threads: the next phase's first unit needs no waits
   NormPairs nw_pref;         // RMSNorm weights of the next normalized GEMV input
@@ -926,8 +927,8 @@ struct Consumer {
         break;
       default: {  // kOutLM
         const float y = v * job.scale;
-        if (lm_vals) {  // top-k sampling: the selection runs on all rows afterwards
-          lm_vals[row - lm_r0] = y;
+        if constexpr (kTopK) {  // top-k sampling: the selection runs on all rows afterwards
+          sU[kHidden + (row - job.r0)] = y;  // after the LM-head B operand (sU[0, 1024))
           if (lm_logits) lm_logits[row] = y;
           break;
         }
@@ -1503,7 +1504,7 @@ struct Consumer {
     const int n = R.end - R.begin, k = p.top_k;
     unsigned *hist = reinterpret_cast<unsigned *>(sA);  // free during the LM head
     unsigned *bc = hist + 256;
-    const float *vals = lm_vals;
+    const float *vals = sU + kHidden;  // this CTA's logits, written by the LM-head emit
     consumer_sync();  // every row's logit is in smem
     const unsigned kc = kth_largest_key(n, k, [&](int i) { return float_order_key(vals[i]); }, hist, bc);
     if (tid == 0) bc[2] = 0u;
@@ -1567,12 +1568,9 @@ struct Consumer {
     lm_best_i = 0x7fffffff;
     lm_logits = p.logits ? (p.logits + (size_t)step * kVocab) : nullptr;
     lm_pos = p.start_pos + step;
-    // top-k: the logits stay in smem after the LM-head B operand (sU[0, 1024))
-    lm_vals = (p.top_k > 0) ? sU + kHidden : nullptr;
-    lm_r0 = R.begin;
     const TcJob job{kTcRow, kOutLM, R.begin, R.end, kLMTileRows, rstd, E};
     tc_phase(job, bop);
-    if (lm_vals) topk_select(E);
+    if constexpr (kTopK) topk_select(E);
     float best = lm_best;
     int best_i = lm_best_i;
     // warp argmax (largest value, lowest row on ties)
@@ -1715,6 +1713,7 @@ struct Consumer {
   }
 };
 
+template <bool kTopK>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ int s_abort;
@@ -1780,7 +1779,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       prod.run();
     }
   } else {
-    Consumer cons(c, p, smem);
+    Consumer<kTopK> cons(c, p, smem);
     cons.run();
     cons.drain_mma();
   }
@@ -1888,8 +1887,10 @@ int current_device(int *dev) {
 int prepare_device(int dev) {
   DeviceState &ds = g_devices[dev];
   if (ds.attr_set) return QMK_OK;
-  cudaError_t e = cudaFuncSetAttribute(qmk::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(qmk::decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        qmk::kSmBytes - 0);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(qmk::decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, qmk::kSmBytes);
   if (e != cudaSuccess)
     return set_error(QMK_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem %d): %s", qmk::kSmBytes,
                      cudaGetErrorString(e));
@@ -1897,8 +1898,14 @@ int prepare_device(int dev) {
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return set_error(QMK_ERR_CUDA, "SM count: %s", cudaGetErrorString(e));
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qmk::decode_kernel, qmk::kThreads,
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qmk::decode_kernel<false>, qmk::kThreads,
                                                     qmk::kSmBytes);
+  if (e == cudaSuccess && per_sm >= 1) {
+    int per_sm_topk = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_topk, qmk::decode_kernel<true>, qmk::kThreads,
+                                                      qmk::kSmBytes);
+    if (per_sm_topk < per_sm) per_sm = per_sm_topk;
+  }
   if (e != cudaSuccess) return set_error(QMK_ERR_CUDA, "occupancy query: %s", cudaGetErrorString(e));
   if (per_sm < 1) return set_error(QMK_ERR_LAUNCH, "decode kernel does not fit on one SM");
   ds.num_sms = sms;
@@ -2062,7 +2069,8 @@ int qmk_run(const QmkRunArgs *a, cudaStream_t stream) {
   p.steps_done = a->steps_done;
 
   void *kargs[] = {&p};
-  cudaError_t e = cudaLaunchCooperativeKernel((const void *)qmk::decode_kernel, dim3(ncta),
+  const void *kernel = p.top_k > 0 ? (const void *)qmk::decode_kernel<true> : (const void *)qmk::decode_kernel<false>;
+  cudaError_t e = cudaLaunchCooperativeKernel(kernel, dim3(ncta),
                                               dim3(qmk::kThreads), kargs, qmk::kSmBytes, stream);
   if (e != cudaSuccess) {
     cudaGetLastError();
