@@ -623,6 +623,7 @@ __device__ int read_argmax(Ctx &c, unsigned flag) {
 }
 
 // ------------------------------------------------------------- producer
+template <bool kFeat>
 struct Producer {
   Ctx &c;
   const Params &p;
@@ -765,7 +766,7 @@ struct Producer {
     for (int t = 0; t < p.num_steps && alive && *c.stop_step > t; ++t) {
       cur_step = t;
       const int pos = p.start_pos + t;
-      c.trace = (p.trace && t == p.trace_step) ? p.trace + (size_t)c.cta * kTraceStride : nullptr;
+      c.trace = (kFeat && p.trace && t == p.trace_step) ? p.trace + (size_t)c.cta * kTraceStride : nullptr;
       c.trace_tile0 = tile;
       for (int l = 0; l < p.num_layers && alive; ++l) {
         c.cur_layer = l;
@@ -801,9 +802,12 @@ struct Producer {
 };
 
 // ------------------------------------------------------------- consumer
-// kTopK: the top-k sampling variant (a separate kernel instance, so that the
-// common paths carry none of its code).
-template <bool kTopK>
+// kFeat: the feature instance of the kernel (sampling with temperature and
+// top-k, timeline trace, store/poll tuning knobs).  The greedy instance
+// carries none of that code: the kernel cycles through nearly all of its code
+// every layer, and on B200 every KB less in that loop is measurable (the
+// optional features cost ~17 us/token when compiled into the common path).
+template <bool kFeat>
 struct Consumer {
   Ctx &c;
   const Params &p;
@@ -927,13 +931,15 @@ struct Consumer {
         break;
       default: {  // kOutLM
         const float y = v * job.scale;
-        if constexpr (kTopK) {  // top-k sampling: the selection runs on all rows afterwards
-          sU[kHidden + (row - job.r0)] = y;  // after the LM-head B operand (sU[0, 1024))
-          if (lm_logits) lm_logits[row] = y;
-          break;
+        if constexpr (kFeat) {
+          if (p.top_k > 0) {  // top-k sampling: the selection runs on all rows afterwards
+            sU[kHidden + (row - job.r0)] = y;  // after the LM-head B operand (sU[0, 1024))
+            if (lm_logits) lm_logits[row] = y;
+            break;
+          }
         }
         // greedy: the logit; sampling: logit / T + Gumbel noise
-        const float key = (p.inv_temp > 0.f) ? fmaf(y, p.inv_temp, gumbel_noise(p.seed, lm_pos, row)) : y;
+        const float key = (kFeat && p.inv_temp > 0.f) ? fmaf(y, p.inv_temp, gumbel_noise(p.seed, lm_pos, row)) : y;
         if (key > lm_best || (key == lm_best && row < lm_best_i)) {
           lm_best = key;
           lm_best_i = row;
@@ -1570,7 +1576,9 @@ struct Consumer {
     lm_pos = p.start_pos + step;
     const TcJob job{kTcRow, kOutLM, R.begin, R.end, kLMTileRows, rstd, E};
     tc_phase(job, bop);
-    if constexpr (kTopK) topk_select(E);
+    if constexpr (kFeat) {
+      if (p.top_k > 0) topk_select(E);
+    }
     float best = lm_best;
     int best_i = lm_best_i;
     // warp argmax (largest value, lowest row on ties)
@@ -1647,7 +1655,7 @@ struct Consumer {
     const int L = p.num_layers;
     steps_run = p.num_steps;
     for (int t = 0; t < p.num_steps; ++t) {
-      c.trace = (p.trace && t == p.trace_step) ? p.trace + (size_t)c.cta * kTraceStride : nullptr;
+      c.trace = (kFeat && p.trace && t == p.trace_step) ? p.trace + (size_t)c.cta * kTraceStride : nullptr;
       c.trace_tile0 = tile;
       trace_stamp(c, tid == 0, L * 16 + 5);
       // CTA 0 records the previous step's argmax (needed even when forced).
@@ -1713,7 +1721,7 @@ struct Consumer {
   }
 };
 
-template <bool kTopK>
+template <bool kFeat>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ int s_abort;
@@ -1742,8 +1750,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   c.cur_layer = 0;
   c.trace = nullptr;
   c.trace_tile0 = 0;
-  c.poll_backoff_ns = p.poll_backoff_ns;
-  c.tuning = p.tuning;
+  c.poll_backoff_ns = kFeat ? p.poll_backoff_ns : 0u;
+  c.tuning = kFeat ? p.tuning : 0u;
   c.mma_bar = reinterpret_cast<uint64_t *>(smem + kSmMisc + kMiscMmaBar);
   c.tmem_free = reinterpret_cast<uint64_t *>(smem + kSmMisc + kMiscTmemFree);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kSmMisc + kMiscTmem);
@@ -1775,11 +1783,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 
   if (threadIdx.x >= kConsumerThreads) {
     if ((threadIdx.x & 31) == 0) {
-      Producer prod(c, p);
+      Producer<kFeat> prod(c, p);
       prod.run();
     }
   } else {
-    Consumer<kTopK> cons(c, p, smem);
+    Consumer<kFeat> cons(c, p, smem);
     cons.run();
     cons.drain_mma();
   }
@@ -2069,7 +2077,9 @@ int qmk_run(const QmkRunArgs *a, cudaStream_t stream) {
   p.steps_done = a->steps_done;
 
   void *kargs[] = {&p};
-  const void *kernel = p.top_k > 0 ? (const void *)qmk::decode_kernel<true> : (const void *)qmk::decode_kernel<false>;
+  // the feature instance only when a feature is asked for
+  const bool feat = p.top_k > 0 || p.inv_temp > 0.f || p.trace || p.tuning || p.poll_backoff_ns;
+  const void *kernel = feat ? (const void *)qmk::decode_kernel<true> : (const void *)qmk::decode_kernel<false>;
   cudaError_t e = cudaLaunchCooperativeKernel(kernel, dim3(ncta),
                                               dim3(qmk::kThreads), kargs, qmk::kSmBytes, stream);
   if (e != cudaSuccess) {
