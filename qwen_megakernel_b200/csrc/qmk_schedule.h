@@ -51,11 +51,13 @@ struct Range {
   int end;
 };
 
-// Rows [c*n/N, (c+1)*n/N): balanced to within one row.
+// Rows [c*n/N, (c+1)*n/N): balanced to within one row.  32-bit arithmetic
+// (n * (ncta) <= 151936 * 160 < 2^31): a 64-bit division is a long software
+// sequence on the GPU.
 QMK_HD Range split_rows(int n, int cta, int ncta) {
   Range r;
-  r.begin = (int)(((long long)n * cta) / ncta);
-  r.end = (int)(((long long)n * (cta + 1)) / ncta);
+  r.begin = (int)((unsigned)(n * cta) / (unsigned)ncta);
+  r.end = (int)((unsigned)(n * (cta + 1)) / (unsigned)ncta);
   return r;
 }
 
@@ -79,8 +81,13 @@ QMK_HD int merge_task_of_cta(int cta, int ncta) {
 // Previous positions [0, prev) of a KV head are cut into `splits` chunks.
 QMK_HD Range kv_chunk(int prev, int s, int splits) {
   Range r;
-  r.begin = (int)(((long long)prev * s) / splits);
-  r.end = (int)(((long long)prev * (s + 1)) / splits);
+  if (prev <= (1 << 26)) {  // prev * (s + 1) <= 2^26 * kMaxSplits < 2^31: 32-bit division
+    r.begin = (int)((unsigned)(prev * s) / (unsigned)splits);
+    r.end = (int)((unsigned)(prev * (s + 1)) / (unsigned)splits);
+  } else {
+    r.begin = (int)(((long long)prev * s) / splits);
+    r.end = (int)(((long long)prev * (s + 1)) / splits);
+  }
   return r;
 }
 
