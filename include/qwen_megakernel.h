@@ -282,10 +282,13 @@ int qmk_static_scratch_ptrs(int **output_log, QmkStatus **status);
  * bf16 [num_layers, 8, max_seq_len, 128] as above.  Token ids outside
  * [0, vocab) read token 0, rows whose sequence or position is out of range
  * are skipped; either sets a bit in *status (device uint32, optional):
- * QMK_BATCH_BAD_TOKEN / QMK_BATCH_BAD_ROW.  All launches are stream-ordered
+ * QMK_BATCH_BAD_TOKEN / QMK_BATCH_BAD_ROW.  A K/V tile copy of the
+ * attention that does not complete within 1 s sets QMK_BATCH_TIMEOUT (the
+ * outputs of that call are then invalid).  All launches are stream-ordered
  * and capturable in a CUDA graph (no allocation, no host sync). */
 #define QMK_BATCH_BAD_TOKEN 1u
 #define QMK_BATCH_BAD_ROW 2u
+#define QMK_BATCH_TIMEOUT 4u
 
 typedef struct QmkBatchArgs {
   const void *embed_weight;              /* bf16 [151936, 1024]                 */

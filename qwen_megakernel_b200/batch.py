@@ -26,6 +26,7 @@ from .weights import HEAD_DIM, NUM_KV_HEADS, TENSORS_PER_LAYER, VOCAB_SIZE
 MAX_ROWS = 4096  # QMK_BATCH_MAX_ROWS
 BAD_TOKEN = 1  # QMK_BATCH_BAD_TOKEN
 BAD_ROW = 2  # QMK_BATCH_BAD_ROW
+TIMEOUT = 4  # QMK_BATCH_TIMEOUT
 
 
 class BatchError(RuntimeError):
@@ -100,6 +101,8 @@ class BatchForward:
                 what.append("token id outside the vocabulary (token 0 used)")
             if code & BAD_ROW:
                 what.append("row with a sequence or position out of range (skipped)")
+            if code & TIMEOUT:
+                what.append("attention K/V copy did not complete within 1 s (outputs invalid)")
             raise BatchError("qmk_batch_forward: " + "; ".join(what))
 
 

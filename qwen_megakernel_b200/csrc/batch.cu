@@ -30,6 +30,7 @@
 #include <cstdio>
 #include <mutex>
 
+#include "qmk_device.cuh"
 #include "qwen_megakernel.h"
 
 int qmk_internal_set_error(int code, const char *msg);
@@ -216,6 +217,11 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
 // cache for the q heads 2g, 2g+1 of KV head g (grid (g, r, split), 256
 // threads; split s of `splits` takes the s-th of equal position chunks, so
 // small batches still fill the GPU).
+// The chunk streams through shared memory: 64-position tiles (K rows, then
+// V rows, 16 KB each) in a kAttStages-deep ring of 1-D bulk copies issued by
+// thread 0 and completed on one mbarrier per stage, so several tiles per CTA
+// are in flight while the warps work on an earlier one (direct loads left
+// the kernel waiting on HBM latency with one tile in flight).
 // Group gq = lane / 8 of a warp takes one position per round; lane r8 of
 // the group holds dims [8 r8, 8 r8 + 8) and [64 + 8 r8, 64 + 8 r8 + 8) of
 // both heads (two 16-byte reads cover a 256-byte cache row per group), so a
@@ -226,6 +232,11 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
 // r and R + r, R = gridDim.y); with several, the CTA's unnormalized state
 // (m0, l0, m1, l1, o0[128], o1[128]) goes to `partial` for merge_kernel.
 constexpr int kAttRounds = 2;
+constexpr int kAttTilePos = 32 * kAttRounds;            // positions per tile = one softmax update
+constexpr int kAttTileBytes = kAttTilePos * kHeadDim * 2;  // K (or V) rows of one tile
+constexpr int kAttStages = 3;
+constexpr int kAttSmemBytes = kAttStages * 2 * kAttTileBytes;  // dynamic shared memory: 96 KB
+constexpr unsigned long long kAttWaitNs = 1000000000ull;     // bound on one tile wait (1 s)
 constexpr int kAttPartWords = 4 + 2 * kHeadDim;
 constexpr int kAttMaxSplits = 16;
 constexpr int kAttSplitRows = 64;  // splits > 1 only for up to this many rows
@@ -243,8 +254,10 @@ __global__ void __launch_bounds__(256) attention_kernel(
     const float *__restrict__ q, const __nv_bfloat16 *__restrict__ k_cache,
     const __nv_bfloat16 *__restrict__ v_cache, long long kv_seq_stride, int num_seqs, int layer, int max_seq_len,
     const int *__restrict__ row_seq, const int *__restrict__ row_pos, int splits, float *__restrict__ partial,
-    __nv_bfloat16 *__restrict__ a2) {
+    __nv_bfloat16 *__restrict__ a2, unsigned *status) {
+  extern __shared__ __align__(128) uint8_t att_ring[];  // [stage][K tile | V tile]
   __shared__ __align__(16) float part[8 * kAttPartWords];
+  __shared__ __align__(8) uint64_t full[kAttStages];
   const int g = blockIdx.x, r = blockIdx.y, sp = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 3, r8 = lane & 7;
@@ -267,8 +280,42 @@ __global__ void __launch_bounds__(256) attention_kernel(
   }
   const size_t head_off =
       (size_t)(valid ? seq : 0) * (size_t)kv_seq_stride + ((size_t)layer * kNumKVHeads + g) * (size_t)max_seq_len * kHeadDim;
-  const uint8_t *kbase = reinterpret_cast<const uint8_t *>(k_cache + head_off) + 16 * r8;
-  const uint8_t *vbase = reinterpret_cast<const uint8_t *>(v_cache + head_off) + 16 * r8;
+  const uint8_t *kg = reinterpret_cast<const uint8_t *>(k_cache + head_off);
+  const uint8_t *vg = reinterpret_cast<const uint8_t *>(v_cache + head_off);
+  const int ntiles = (j_hi - j_lo + kAttTilePos - 1) / kAttTilePos;
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int st = 0; st < kAttStages; ++st) qmk::mbar_init(&full[st], 1);
+    qmk::fence_mbar_init();
+  }
+  __syncthreads();
+  // Tile t: positions [j_lo + 64 t, +n) into stage t % kAttStages (thread 0).
+  const uint64_t pol = qmk::l2_policy_evict_first();
+  auto issue = [&](int t) {
+    if (t >= ntiles) return;
+    const int st = t % kAttStages, j0 = j_lo + t * kAttTilePos;
+    const unsigned bytes = (unsigned)(min(kAttTilePos, j_hi - j0) * kHeadDim * 2);
+    uint8_t *dst = att_ring + (size_t)st * 2 * kAttTileBytes;
+    qmk::mbar_arrive_expect_tx(&full[st], 2 * bytes);
+    qmk::bulk_g2s(dst, kg + (size_t)j0 * (kHeadDim * 2), bytes, &full[st], pol);
+    qmk::bulk_g2s(dst + kAttTileBytes, vg + (size_t)j0 * (kHeadDim * 2), bytes, &full[st], pol);
+  };
+  if (threadIdx.x == 0)
+    for (int t = 0; t < kAttStages; ++t) issue(t);
+  // Bounded wait for tile t (every thread); false after kAttWaitNs.
+  auto wait_tile = [&](int t) -> bool {
+    uint64_t *bar = &full[t % kAttStages];
+    const unsigned par = (unsigned)(t / kAttStages) & 1u;
+    uint64_t t0 = 0;
+    for (unsigned it = 0;; ++it) {
+      if (qmk::mbar_try_wait(bar, par)) return true;
+      if ((it & 63u) == 63u) {
+        const uint64_t now = qmk::global_timer_ns();
+        if (t0 == 0) t0 = now;
+        else if (now - t0 > kAttWaitNs) return false;
+      }
+    }
+  };
   float mrun[2] = {-INFINITY, -INFINITY}, lrun[2] = {0.f, 0.f};
   float oacc[2][16];
 #pragma unroll
@@ -276,82 +323,100 @@ __global__ void __launch_bounds__(256) attention_kernel(
 #pragma unroll
     for (int e = 0; e < 16; ++e) oacc[h][e] = 0.f;
 
-  for (int base = j_lo; base < j_hi; base += 32 * kAttRounds) {
-    if (base + 4 * warp >= j_hi) continue;  // warp-uniform: no position of this warp in this update
-    int jr[kAttRounds];
-    bool ok[kAttRounds];
-    uint4 ka[kAttRounds], kb[kAttRounds], va[kAttRounds], vb[kAttRounds];
+  int pending = ntiles;  // first tile not known to have landed
+  for (int tile = 0; tile < ntiles; ++tile) {
+    const int base = j_lo + tile * kAttTilePos;
+    const bool landed = wait_tile(tile);
+    const uint8_t *ks = att_ring + (size_t)(tile % kAttStages) * 2 * kAttTileBytes + 16 * r8;
+    const uint8_t *vs = ks + kAttTileBytes;
+    // warp-uniform: a warp with no position in this tile only joins the barrier
+    if (landed && base + 4 * warp < j_hi) {
+      int jr[kAttRounds];
+      bool ok[kAttRounds];
+      uint4 ka[kAttRounds], kb[kAttRounds], va[kAttRounds], vb[kAttRounds];
 #pragma unroll
-    for (int t = 0; t < kAttRounds; ++t) {
-      const int j = base + 32 * t + 4 * warp + gq;
-      ok[t] = j < j_hi;
-      jr[t] = ok[t] ? j : base + 4 * warp;  // an in-range row, masked below
-      const uint8_t *kr = kbase + (size_t)jr[t] * (kHeadDim * 2);
-      const uint8_t *vr = vbase + (size_t)jr[t] * (kHeadDim * 2);
-      ka[t] = __ldg(reinterpret_cast<const uint4 *>(kr));
-      kb[t] = __ldg(reinterpret_cast<const uint4 *>(kr + kHeadDim));
-      va[t] = __ldg(reinterpret_cast<const uint4 *>(vr));
-      vb[t] = __ldg(reinterpret_cast<const uint4 *>(vr + kHeadDim));
-    }
-    float s[kAttRounds][2];
+      for (int t = 0; t < kAttRounds; ++t) {
+        const int j = 32 * t + 4 * warp + gq;  // row within the tile
+        ok[t] = base + j < j_hi;
+        jr[t] = ok[t] ? j : 4 * warp;  // an in-range row, masked below
+        const uint8_t *kr = ks + jr[t] * (kHeadDim * 2);
+        const uint8_t *vr = vs + jr[t] * (kHeadDim * 2);
+        ka[t] = *reinterpret_cast<const uint4 *>(kr);
+        kb[t] = *reinterpret_cast<const uint4 *>(kr + kHeadDim);
+        va[t] = *reinterpret_cast<const uint4 *>(vr);
+        vb[t] = *reinterpret_cast<const uint4 *>(vr + kHeadDim);
+      }
+      float s[kAttRounds][2];
 #pragma unroll
-    for (int t = 0; t < kAttRounds; ++t)
+      for (int t = 0; t < kAttRounds; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float *qq = qv[h];
+          const unsigned w[8] = {ka[t].x, ka[t].y, ka[t].z, ka[t].w, kb[t].x, kb[t].y, kb[t].z, kb[t].w};
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            s0 = fmaf(qq[2 * k], bf_lo(w[k]), s0);
+            s1 = fmaf(qq[2 * k + 1], bf_hi(w[k]), s1);
+          }
+          s[t][h] = s0 + s1;
+        }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int t = 0; t < kAttRounds; ++t) {
+          s[t][0] += __shfl_xor_sync(0xffffffffu, s[t][0], o);
+          s[t][1] += __shfl_xor_sync(0xffffffffu, s[t][1], o);
+        }
+      float mn[2] = {mrun[0], mrun[1]};
+#pragma unroll
+      for (int t = 0; t < kAttRounds; ++t) {
+        if (!ok[t]) s[t][0] = s[t][1] = -INFINITY;
+        mn[0] = fmaxf(mn[0], s[t][0]);
+        mn[1] = fmaxf(mn[1], s[t][1]);
+      }
+#pragma unroll
+      for (int o = 8; o < 32; o <<= 1) {
+        mn[0] = fmaxf(mn[0], __shfl_xor_sync(0xffffffffu, mn[0], o));
+        mn[1] = fmaxf(mn[1], __shfl_xor_sync(0xffffffffu, mn[1], o));
+      }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const float *qq = qv[h];
-        const unsigned w[8] = {ka[t].x, ka[t].y, ka[t].z, ka[t].w, kb[t].x, kb[t].y, kb[t].z, kb[t].w};
-        float s0 = 0.f, s1 = 0.f;
+        const float corr = fast_exp2(mrun[h] - mn[h]);  // 0 while mrun is -inf
+        float pt[kAttRounds];
+        float l = lrun[h] * corr;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          s0 = fmaf(qq[2 * k], bf_lo(w[k]), s0);
-          s1 = fmaf(qq[2 * k + 1], bf_hi(w[k]), s1);
+        for (int t = 0; t < kAttRounds; ++t) {
+          pt[t] = fast_exp2(s[t][h] - mn[h]);  // 0 for masked positions
+          l += pt[t];
         }
-        s[t][h] = s0 + s1;
-      }
+        lrun[h] = l;
+        mrun[h] = mn[h];
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1)
+        for (int e = 0; e < 16; ++e) oacc[h][e] *= corr;
 #pragma unroll
-      for (int t = 0; t < kAttRounds; ++t) {
-        s[t][0] += __shfl_xor_sync(0xffffffffu, s[t][0], o);
-        s[t][1] += __shfl_xor_sync(0xffffffffu, s[t][1], o);
-      }
-    float mn[2] = {mrun[0], mrun[1]};
+        for (int t = 0; t < kAttRounds; ++t) {
+          const unsigned w[8] = {va[t].x, va[t].y, va[t].z, va[t].w, vb[t].x, vb[t].y, vb[t].z, vb[t].w};
 #pragma unroll
-    for (int t = 0; t < kAttRounds; ++t) {
-      if (!ok[t]) s[t][0] = s[t][1] = -INFINITY;
-      mn[0] = fmaxf(mn[0], s[t][0]);
-      mn[1] = fmaxf(mn[1], s[t][1]);
-    }
-#pragma unroll
-    for (int o = 8; o < 32; o <<= 1) {
-      mn[0] = fmaxf(mn[0], __shfl_xor_sync(0xffffffffu, mn[0], o));
-      mn[1] = fmaxf(mn[1], __shfl_xor_sync(0xffffffffu, mn[1], o));
-    }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float corr = fast_exp2(mrun[h] - mn[h]);  // 0 while mrun is -inf
-      float pt[kAttRounds];
-      float l = lrun[h] * corr;
-#pragma unroll
-      for (int t = 0; t < kAttRounds; ++t) {
-        pt[t] = fast_exp2(s[t][h] - mn[h]);  // 0 for masked positions
-        l += pt[t];
-      }
-      lrun[h] = l;
-      mrun[h] = mn[h];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) oacc[h][e] *= corr;
-#pragma unroll
-      for (int t = 0; t < kAttRounds; ++t) {
-        const unsigned w[8] = {va[t].x, va[t].y, va[t].z, va[t].w, vb[t].x, vb[t].y, vb[t].z, vb[t].w};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          oacc[h][2 * k] = fmaf(pt[t], bf_lo(w[k]), oacc[h][2 * k]);
-          oacc[h][2 * k + 1] = fmaf(pt[t], bf_hi(w[k]), oacc[h][2 * k + 1]);
+          for (int k = 0; k < 8; ++k) {
+            oacc[h][2 * k] = fmaf(pt[t], bf_lo(w[k]), oacc[h][2 * k]);
+            oacc[h][2 * k + 1] = fmaf(pt[t], bf_hi(w[k]), oacc[h][2 * k + 1]);
+          }
         }
       }
     }
+    // Stage tile % kAttStages fully read: refill it with tile + kAttStages.
+    if (__syncthreads_or(!landed)) {
+      if (threadIdx.x == 0 && status) atomicOr(status, QMK_BATCH_TIMEOUT);
+      pending = tile;
+      break;
+    }
+    if (threadIdx.x == 0) issue(tile + kAttStages);
   }
+  // After a timeout: bounded wait for the copies still in flight before the
+  // CTA (and its shared memory) goes away.
+  if (threadIdx.x == 0)
+    for (int t = pending; t < ntiles && t < pending + kAttStages; ++t) (void)wait_tile(t);
   // Groups -> warp (same running max in every group): reduce-scatter, then
   // lane (gq, r8) holds head gq & 1, dims [base, base + 8), base = 8 r8 + 64 (gq >> 1).
 #pragma unroll
@@ -688,6 +753,7 @@ int attention_splits(int R) {
 
 constexpr int kMaxDevices = 64;
 cublasHandle_t g_handles[kMaxDevices] = {};
+bool g_att_smem_set[kMaxDevices] = {};  // attention_kernel's dynamic shared memory limit raised
 std::mutex g_batch_mutex;
 
 const char *cublas_name(cublasStatus_t s) {
@@ -739,6 +805,13 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
   if (a->num_seqs > 1 && a->kv_seq_stride < per_seq)
     return fail(QMK_ERR_ARGS, "qmk_batch_forward: kv_seq_stride=%lld < one cache (%lld elements)", a->kv_seq_stride,
                 per_seq);
+  // The attention copies cache rows with 1-D bulk copies: 16-byte aligned
+  // sources (cache bases and the per-sequence stride).
+  if ((reinterpret_cast<uintptr_t>(a->k_cache) | reinterpret_cast<uintptr_t>(a->v_cache)) % 16)
+    return fail(QMK_ERR_ARGS, "qmk_batch_forward: k_cache / v_cache not 16-byte aligned");
+  if (a->num_seqs > 1 && a->kv_seq_stride % 8)
+    return fail(QMK_ERR_ARGS, "qmk_batch_forward: kv_seq_stride=%lld not a multiple of 8 elements (16 bytes)",
+                a->kv_seq_stride);
   for (int i = 0; i < a->num_layers * 11; ++i)
     if (!a->layer_ptrs[i]) return fail(QMK_ERR_ARGS, "qmk_batch_forward: layer pointer %d is null", i);
   const Layout Lw = layout(a->num_rows, a->num_out);
@@ -756,6 +829,11 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
     const cublasStatus_t s = cublasCreate(&h);
     if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublasCreate: %s", cublas_name(s));
     g_handles[dev] = h;
+  }
+  if (!g_att_smem_set[dev]) {
+    e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttSmemBytes);
+    if (e != cudaSuccess) return fail(QMK_ERR_CUDA, "attention_kernel shared memory: %s", cudaGetErrorString(e));
+    g_att_smem_set[dev] = true;
   }
   uint8_t *ws = static_cast<uint8_t *>(a->workspace);
   cublasStatus_t s = cublasSetStream(h, stream);
@@ -821,8 +899,9 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
       if (s != CUBLAS_STATUS_SUCCESS) break;
       att_combine_kernel<<<R, 256, 0, stream>>>(ob, a2);
     } else {
-      attention_kernel<<<dim3(kNumKVHeads, R, splits), 256, 0, stream>>>(
-          q, kc, vc, a->kv_seq_stride, a->num_seqs, l, a->max_seq_len, a->row_seq, a->row_pos, splits, partial, a2);
+      attention_kernel<<<dim3(kNumKVHeads, R, splits), 256, kAttSmemBytes, stream>>>(
+          q, kc, vc, a->kv_seq_stride, a->num_seqs, l, a->max_seq_len, a->row_seq, a->row_pos, splits, partial, a2,
+          a->status);
       if (splits > 1) merge_kernel<<<dim3(kNumKVHeads, R), 64, 0, stream>>>(partial, splits, a2);
     }
     s = gemm(h, R2, kHidden, kQSize, P[6], a2, c2, kHidden);

@@ -113,6 +113,19 @@ def test_forward_rejects_bad_arguments(lib, field, value):
     assert len(lib.qmk_get_last_error_message()) > 0
 
 
+def test_forward_rejects_unaligned_cache(lib):
+    """Cache rows are copied with 16-byte-aligned bulk copies."""
+    a, table = _valid(lib)
+    a.k_cache = 0x10008
+    assert lib.qmk_batch_forward(ctypes.byref(a), None) == QMK_ERR_ARGS
+    assert b"aligned" in lib.qmk_get_last_error_message()
+    a, table = _valid(lib)
+    a.num_seqs = 2
+    a.kv_seq_stride = 28 * 8 * 2048 * 128 + 4
+    assert lib.qmk_batch_forward(ctypes.byref(a), None) == QMK_ERR_ARGS
+    assert b"multiple of 8" in lib.qmk_get_last_error_message()
+
+
 def test_forward_rejects_null_layer_pointer(lib):
     a, table = _valid(lib)
     table[5 * 11 + 6] = None  # o_proj of layer 5
