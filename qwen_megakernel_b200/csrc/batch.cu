@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 #include <cublas_v2.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -114,27 +115,38 @@ __global__ void __launch_bounds__(256) embed_kernel(const __nv_bfloat16 *__restr
 // GEMM inputs and outputs are "stacked": for n rows the hi halves fill rows
 // [0, n) and the lo halves rows [n, 2n), so ONE GEMM over 2n rows reads each
 // weight once for both halves; the consumer of its fp32 output adds row r
-// and row n + r.  Here: v = x[r] + c2[r] + c2[num_in + r] (c2 = the stacked
-// output of the previous projection, or null), with r = rows ? rows[i] : i;
+// and row n + r.  Here: v = x[r] + sum over the nsplit K-split partials c of
+// (c[r] + c[num_in + r]) (c = c2 + s split_stride: the stacked output of the
+// previous projection, or c2 null), with r = rows ? rows[i] : i;
 // without `rows` v is written back to x (the residual stream).  Output row i
 // of n_out = gridDim.x: hi at a2 row i, lo at a2 row n_out + i (stride 1024).
 __global__ void __launch_bounds__(256) residual_norm_split_kernel(float *__restrict__ x,
                                                                   const float *__restrict__ c2,
                                                                   const int *__restrict__ rows, int num_in,
                                                                   const __nv_bfloat16 *__restrict__ w,
-                                                                  __nv_bfloat16 *__restrict__ a2) {
+                                                                  __nv_bfloat16 *__restrict__ a2, int nsplit,
+                                                                  long long split_stride) {
   __shared__ float red[8];
   const int i = blockIdx.x, n_out = gridDim.x;
   int r = rows ? rows[i] : i;
   if (r < 0 || r >= num_in) r = 0;  // validated on the host; never read out of bounds
   float4 v = reinterpret_cast<const float4 *>(x + (size_t)r * kHidden)[threadIdx.x];
   if (c2) {
-    const float4 h = reinterpret_cast<const float4 *>(c2 + (size_t)r * kHidden)[threadIdx.x];
-    const float4 l = reinterpret_cast<const float4 *>(c2 + (size_t)(num_in + r) * kHidden)[threadIdx.x];
-    v.x += h.x + l.x;
-    v.y += h.y + l.y;
-    v.z += h.z + l.z;
-    v.w += h.w + l.w;
+    // nsplit K-split partial products of the GEMM, each stacked hi/lo
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float *c = c2 + (size_t)sp * (size_t)split_stride;
+      const float4 h = reinterpret_cast<const float4 *>(c + (size_t)r * kHidden)[threadIdx.x];
+      const float4 l = reinterpret_cast<const float4 *>(c + (size_t)(num_in + r) * kHidden)[threadIdx.x];
+      sum.x += h.x + l.x;
+      sum.y += h.y + l.y;
+      sum.z += h.z + l.z;
+      sum.w += h.w + l.w;
+    }
+    v.x += sum.x;
+    v.y += sum.y;
+    v.z += sum.z;
+    v.w += sum.w;
     if (!rows) reinterpret_cast<float4 *>(x + (size_t)r * kHidden)[threadIdx.x] = v;
   }
   const float ss = block_sum256(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w, red);
@@ -709,6 +721,14 @@ struct Layout {
   size_t x, a2, qkv2, q, c2, gu2, partial, qs, sc, pr, ob, lm2, logits2, cublas, total;
 };
 
+// K splits of the N = 1024 projections (O, down) for R rows.  With few rows
+// cuBLAS tiles N = 1024 into ~16 CTAs that cannot stream the weight at HBM
+// speed; the K chunks as a batch multiply the CTAs, the partial sums are
+// added by residual_norm_split_kernel.
+constexpr int kMaxSplitK = 4;
+constexpr int kSplitKRows = 64;
+int split_k(int R) { return R <= kSplitKRows ? kMaxSplitK : 1; }
+
 Layout layout(int R, int O) {
   using namespace qmb;
   Layout L{};
@@ -722,7 +742,9 @@ Layout layout(int R, int O) {
   L.a2 = take((size_t)2 * R * kInter * 2);  // largest GEMM input: K = 3072
   L.qkv2 = take((size_t)2 * R * kQKV * 4);
   L.q = take((size_t)R * kQSize * 4);
-  L.c2 = take((size_t)2 * R * kHidden * 4);  // O and down outputs
+  // O and down outputs: split_k(R) K-split partials of 2R rows each, sized
+  // 2 max(R, kMaxSplitK min(R, kSplitKRows)) rows so the total grows with R
+  L.c2 = take((size_t)2 * std::max<size_t>(R, (size_t)kMaxSplitK * std::min(R, kSplitKRows)) * kHidden * 4);
   L.gu2 = take((size_t)2 * R * 2 * kInter * 4);
   // split states (used up to kAttSplitRows rows; sized so that the total
   // grows with R: a workspace for R rows serves every smaller call)
@@ -776,6 +798,18 @@ cublasStatus_t gemm(cublasHandle_t h, int rows, int n, int k, const void *W, con
   const float one = 1.f, zero = 0.f;
   return cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, n, rows, k, &one, W, CUDA_R_16BF, k, A, CUDA_R_16BF, k, &zero, C,
                       CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+}
+
+// Split-K form of gemm: nsplit partial products C_s = A[:, K_s] W[:, K_s]^T
+// over equal K chunks, C_s at C + s rows ldc, as one strided-batched call.
+cublasStatus_t gemm_splitk(cublasHandle_t h, int rows, int n, int k, const void *W, const void *A, float *C, int ldc,
+                           int nsplit) {
+  if (nsplit <= 1) return gemm(h, rows, n, k, W, A, C, ldc);
+  const float one = 1.f, zero = 0.f;
+  const int kc = k / nsplit;  // callers pass k % (8 nsplit) == 0: 16-byte aligned chunks
+  return cublasGemmStridedBatchedEx(h, CUBLAS_OP_T, CUBLAS_OP_N, n, rows, kc, &one, W, CUDA_R_16BF, k, kc, A,
+                                    CUDA_R_16BF, k, kc, &zero, C, CUDA_R_32F, ldc, (long long)rows * ldc, nsplit,
+                                    CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
 }
 
 }  // namespace
@@ -863,12 +897,15 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
   auto bf = [](const void *p) { return static_cast<const __nv_bfloat16 *>(p); };
   const int splits = attention_splits(R);
   const float *resid = nullptr;  // stacked output of the last down projection
+  const int ks = split_k(R);
+  const long long ks_stride = (long long)R2 * kHidden;  // floats between K-split partials
+  static_assert(kQSize % (8 * kMaxSplitK) == 0 && kInter % (8 * kMaxSplitK) == 0, "K chunks must stay aligned");
 
   embed_kernel<<<R, 256, 0, stream>>>(bf(a->embed_weight), a->tokens, x, a->status);
   for (int l = 0; l < a->num_layers && s == CUBLAS_STATUS_SUCCESS; ++l) {
     const void *const *P = a->layer_ptrs + 11 * l;
     const void *const *F = a->fused_ptrs ? a->fused_ptrs + 2 * l : nullptr;
-    residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, resid, nullptr, R, bf(P[0]), a2);
+    residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, resid, nullptr, R, bf(P[0]), a2, ks, ks_stride);
     if (F) {
       s = gemm(h, R2, kQKV, kHidden, F[0], a2, qkv2, kQKV);
     } else {
@@ -904,9 +941,9 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
           a->status);
       if (splits > 1) merge_kernel<<<dim3(kNumKVHeads, R), 64, 0, stream>>>(partial, splits, a2);
     }
-    s = gemm(h, R2, kHidden, kQSize, P[6], a2, c2, kHidden);
+    s = gemm_splitk(h, R2, kHidden, kQSize, P[6], a2, c2, kHidden, ks);
     if (s != CUBLAS_STATUS_SUCCESS) break;
-    residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, c2, nullptr, R, bf(P[7]), a2);  // x += O-proj
+    residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, c2, nullptr, R, bf(P[7]), a2, ks, ks_stride);  // x += O-proj
     if (F) {
       s = gemm(h, R2, 2 * kInter, kHidden, F[1], a2, gu2, 2 * kInter);
     } else {
@@ -915,12 +952,13 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
     }
     if (s != CUBLAS_STATUS_SUCCESS) break;
     silu_split_kernel<<<R, 256, 0, stream>>>(gu2, a2);
-    s = gemm(h, R2, kHidden, kInter, P[10], a2, c2, kHidden);
+    s = gemm_splitk(h, R2, kHidden, kInter, P[10], a2, c2, kHidden, ks);
     resid = c2;  // added to x by the next norm
   }
   if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublasGemmEx: %s", cublas_name(s));
   if (O > 0) {
-    residual_norm_split_kernel<<<O, 256, 0, stream>>>(x, resid, a->out_rows, R, bf(a->final_norm_weight), lm2);
+    residual_norm_split_kernel<<<O, 256, 0, stream>>>(x, resid, a->out_rows, R, bf(a->final_norm_weight), lm2, ks,
+                                                      ks_stride);
     s = gemm(h, 2 * O, kVocab, kHidden, a->lm_head_weight, lm2, logits2, kVocab);
     if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublasGemmEx (LM head): %s", cublas_name(s));
     argmax_kernel<<<O, 1024, 0, stream>>>(logits2, a->logits, a->out_tokens);
