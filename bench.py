@@ -77,6 +77,14 @@ def profiled_traffic_per_token():
         return None
 
 
+def smi_gpu_id(local: int) -> str:
+    """nvidia-smi's id of CUDA device `local`: with CUDA_VISIBLE_DEVICES set,
+    its local-th entry (a physical index or a UUID, both accepted by
+    `nvidia-smi -i`), else the index itself."""
+    ids = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    return ids[local] if local < len(ids) else str(local)
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
 
@@ -87,7 +95,7 @@ class ClockSampler:
     )
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+        self.gpu = smi_gpu_id(gpu_index)
         self.proc = None
         self.lines: list[str] = []
         self._t = None

@@ -102,3 +102,19 @@ def test_prompt_seeds_differ_per_rank(n):
     a, b = bench.prompt_for_rank(0), bench.prompt_for_rank(n)
     assert len(a) == bench.PROMPT_LEN and a != b
     assert all(0 <= t < 151936 for t in a)
+
+
+def test_clock_sampler_follows_visible_devices(monkeypatch):
+    """Each rank samples the clocks of its own GPU: CUDA device i is entry i
+    of CUDA_VISIBLE_DEVICES when that is set."""
+    import sys
+
+    sys.path.insert(0, ROOT)
+    import bench
+
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES", raising=False)
+    assert bench.smi_gpu_id(1) == "1"
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "3,5")
+    assert bench.smi_gpu_id(0) == "3" and bench.smi_gpu_id(1) == "5"
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "GPU-aaaa, GPU-bbbb")
+    assert bench.smi_gpu_id(1) == "GPU-bbbb"
