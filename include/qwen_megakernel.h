@@ -305,9 +305,10 @@ typedef struct QmkBatchArgs {
   const void *lm_head_weight;            /* bf16 [151936, 1024]                 */
   const void *cos_table;                 /* bf16 [max_seq_len, 128]             */
   const void *sin_table;
-  void *k_cache;                         /* bf16, see above                     */
-  void *v_cache;
-  long long kv_seq_stride;               /* elements between sequences' caches  */
+  void *k_cache;                         /* bf16, see above; 16-byte aligned    */
+  void *v_cache;                         /* 16-byte aligned                     */
+  long long kv_seq_stride;               /* elements between sequences' caches, */
+                                         /* a multiple of 8 (16 bytes)          */
   int num_seqs;
   int num_layers;
   int max_seq_len;
