@@ -174,6 +174,36 @@ def test_batch_decoder_matches_oracle_per_sequence():
         assert first[s] == int(pl[s].argmax())
 
 
+def test_batch_attention_ring_wraps_vs_oracle():
+    """K/V tiles past the shared-memory ring's depth (3 tiles of 64
+    positions), in both attention modes: 16 prompts of 400 tokens prefilled
+    as 6400 rows in two chunks (one position split per row, up to 7 tiles),
+    then 2 batched steps (2 position splits of ~200 positions: 4 tiles each).
+    Every sequence's logits vs the oracle run on that sequence alone."""
+    from oracle.qwen3_mirror import MirrorDecoder
+    from qwen_megakernel_b200 import BatchDecoder
+
+    w = small_model(2, seed=23, max_seq_len=512)
+    B, n, steps = 16, 400, 2
+    g = torch.Generator().manual_seed(29)
+    prompts = [[int(t) for t in torch.randint(0, V, (n,), generator=g)] for _ in range(B)]
+    forced = [[int(t) for t in torch.randint(0, V, (steps,), generator=g)] for _ in range(B)]
+    bd = BatchDecoder(w, B, max_seq_len=512, use_graphs=False)
+    pl = torch.empty(B, V, device="cuda")
+    bd.prefill(prompts, logits=pl)
+    outs = []
+    for t in range(steps):
+        lg = torch.empty(B, V, device="cuda")
+        bd.step([forced[s][t] for s in range(B)], logits=lg)
+        outs.append(lg)
+    torch.cuda.synchronize()
+    bd.fw.check_status()
+    for s in range(B):
+        ref = MirrorDecoder(w, 512, device="cuda").prefill(prompts[s] + forced[s], 0)
+        got = torch.stack([pl[s]] + [outs[t][s] for t in range(steps)])
+        _check_vs_oracle(got, ref[n - 1:])
+
+
 def test_batch_decoder_graph_equals_eager():
     """The CUDA-graph step loop (device-side token feedback) gives the same
     tokens as the eager loop, and each sequence the same tokens as the
