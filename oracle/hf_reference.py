@@ -3,7 +3,7 @@
 The reference compares its kernel against Hugging Face
 ``Qwen3ForCausalLM`` (qwen_megakernel/bench.py:19-55 times it, :83-133 uses it
 as the correctness comparator).  That model is a third-party dependency, not
-part of /root/reference: transformers (pinned only as ``>=4.40.0`` by the
+part of the reference project: transformers (pinned only as ``>=4.40.0`` by the
 reference's requirements.txt:2; this image has 5.5.0).  Here it is built from
 an explicit Qwen3-0.6B config with the same bf16 weights the kernel uses and
 evaluated either in fp32 (bf16 weights upcast exactly: the "after fp32

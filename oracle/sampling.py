@@ -4,7 +4,7 @@ This module is a CHECKER: only tests/ import it; the product never does.
 
 The reference decodes greedily only (csrc/kernel.cu:1020-1183, argmax) and
 truncates at EOS on the host (qwen_megakernel/model.py:242-244); sampling is
-an extension (survey row f3).  Its defining semantics are the standard ones:
+an extension (on-device sampling).  Its defining semantics are the standard ones:
 the next token is a draw from softmax(logits / T).  The kernel draws it with
 the Gumbel-max trick (Gumbel 1954; e.g. Maddison, Tarlow and Minka 2014):
 argmax_i(logit_i / T + g_i) with i.i.d. standard Gumbel g_i is distributed as
