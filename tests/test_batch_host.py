@@ -69,6 +69,19 @@ def test_workspace_bytes(lib):
         assert lib.qmk_batch_workspace_bytes(rows, out) == 0
 
 
+def test_workspace_bytes_monotone_in_rows(lib):
+    """A workspace sized for R rows serves every smaller call (BatchForward
+    grows its buffer only): the size never decreases with rows or outputs,
+    across the split-K and split-attention thresholds (64 rows) and the
+    tensor-core attention limit (2048 rows)."""
+    prev = 0
+    for rows in list(range(1, 300)) + [1000, 2047, 2048, 2049, 3000, MAX_ROWS]:
+        n = lib.qmk_batch_workspace_bytes(rows, 1)
+        assert n >= prev, f"workspace shrinks at {rows} rows"
+        prev = n
+        assert lib.qmk_batch_workspace_bytes(rows, rows) >= n
+
+
 def _valid(lib, layers=28):
     fake = 0x10000  # never dereferenced: validation fails before any launch
     table = (ctypes.c_void_p * (layers * 11))(*([fake] * (layers * 11)))
