@@ -226,7 +226,8 @@ int qmk_trace_words(void);
 
 /* ---- allocation-free variant (no counterpart in the reference) ----------
  * qmk_generate_static runs the same decode as launch_ldg_generate_nosync
- * (csrc/torch_bindings.cpp:83-91 of the reference) but allocates nothing:
+ * above (first token, num_steps greedy steps from start_position, the token
+ * of step t into entry t of a token log) but allocates nothing:
  * no cudaMalloc / cudaFree / cudaHostAlloc, no allocator of any library.
  * Its scratch -- the kernel workspace, the token log and a status block --
  * is one file-scope __device__ array of QMK_STATIC_SCRATCH_BYTES per device

@@ -1,7 +1,7 @@
 // Persistent decode megakernel for Qwen3-0.6B on B200 (sm_100a), plus the C ABI.
 //
 // Structure (one cooperative launch runs `num_steps` greedy decode steps):
-//   * one CTA per SM (148 on B200), 288 threads: 8 consumer warps + 1 producer warp;
+//   * one CTA per SM (148 on B200), 256 threads: 7 consumer warps + 1 producer warp;
 //   * the producer warp streams every byte the CTA will read (its slice of each
 //     weight matrix, its KV-cache chunk, its LM-head rows) through a 6 x 32 KB
 //     shared-memory ring with 1-D TMA bulk copies (cp.async.bulk) and mbarriers.
@@ -39,7 +39,7 @@
 
 namespace qmk {
 
-constexpr int kConsumerWarps = 7;  // + 1 producer warp = 8 warps: 255 registers per thread
+constexpr int kConsumerWarps = 7;  // + 1 producer warp = 8 warps (256 threads; ptxas: 228 registers)
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 

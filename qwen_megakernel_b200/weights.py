@@ -126,16 +126,22 @@ def weights_checksum(weights: dict) -> dict:
     return out
 
 
-def load_hf_weights(model_name_or_path: str, device="cuda", max_seq_len: int = 2048, verbose: bool = True):
+def load_hf_weights(model_name_or_path: str, device="cuda", max_seq_len: int = 2048, verbose: bool = True,
+                    tokenizer: bool = True):
     """Load a local Qwen3-0.6B Hugging Face checkpoint into the reference's
     weight dict (mirrors qwen_megakernel/model.py:21-94, minus the network:
-    the path must already be on disk).  Returns (weights, tokenizer)."""
+    the path must already be on disk).  Returns (weights, tokenizer).
+
+    The RoPE base is read from the checkpoint's config (Qwen3: 1e6).  An
+    untied ``lm_head.weight`` is used when the config does not tie it to the
+    embedding (Qwen3-0.6B ties them).  With ``tokenizer=False`` the returned
+    tokenizer is None: the token-id APIs need none."""
     from transformers import AutoModelForCausalLM, AutoTokenizer
 
     if verbose:
         print(f"Loading {model_name_or_path}...")
     model = AutoModelForCausalLM.from_pretrained(model_name_or_path, dtype=torch.bfloat16)
-    tokenizer = AutoTokenizer.from_pretrained(model_name_or_path)
+    tok = AutoTokenizer.from_pretrained(model_name_or_path) if tokenizer else None
     cfg = model.config
     rope = getattr(cfg, "rope_parameters", None) or {}
     theta = float(rope.get("rope_theta", getattr(cfg, "rope_theta", ROPE_THETA)))
@@ -146,14 +152,18 @@ def load_hf_weights(model_name_or_path: str, device="cuda", max_seq_len: int = 2
         for name, _shape, _kind in LAYER_TENSORS:
             layers.append(state[p + name].to(device).contiguous())
     embed = state["model.embed_tokens.weight"].to(device).contiguous()
+    lm_head = embed
+    head = state.get("lm_head.weight")
+    if head is not None and not getattr(cfg, "tie_word_embeddings", True):
+        lm_head = head.to(device).contiguous()
     cos, sin = rope_tables(max_seq_len, theta, device=device)
     weights = dict(
         embed_weight=embed,
         layer_weights=layers,
         final_norm_weight=state["model.norm.weight"].to(device).contiguous(),
-        lm_head_weight=embed,
+        lm_head_weight=lm_head,
         cos_table=cos,
         sin_table=sin,
     )
     del model
-    return weights, tokenizer
+    return weights, tok
