@@ -446,6 +446,53 @@ def run_profile_case(steps: int) -> int:
     return 0
 
 
+def run_trace(steps: int) -> int:
+    """Per-phase critical path of the decode kernel: the bench model and
+    prompt, then launches of `steps` greedy tokens at ctx ~1k whose middle
+    step is traced (the feature instance of the kernel carries the trace
+    stamps).  Three global-timer traces (the fastest step is tabulated) and
+    one clock64 trace (inside the phases).  Prints markdown tables and one
+    JSON line."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from qwen_megakernel_b200 import Decoder, cdll
+    from qwen_megakernel_b200.trace import TUNE_TRACE_CLOCK, format_detail, format_table, phase_detail, phase_table
+    from qwen_megakernel_b200.weights import random_weights
+
+    weights = random_weights(seed=0, device="cuda", max_seq_len=2048)
+    dec = Decoder(weights, max_seq_len=2048)
+    prompt = prompt_for_rank(0)
+    dec.prefill(prompt[:-1])
+    lib = cdll()
+    ncta = lib.qmk_num_ctas(0)
+    words = lib.qmk_trace_words()
+    first = torch.tensor([prompt[-1]], dtype=torch.int32, device=dev)
+    log = torch.empty(steps, dtype=torch.int32, device=dev)
+
+    def traced(tuning: int):
+        trace = torch.zeros(ncta * words, dtype=torch.int64, device=dev)
+        dec.decode_steps(steps, forced_tokens=first, start_position=PROMPT_LEN - 1, output_log=log,
+                         trace=trace, trace_step=steps // 2, tuning=tuning)
+        torch.cuda.synchronize(dev)
+        dec.check_status()
+        return trace.view(ncta, words).cpu().numpy()
+
+    tabs = [phase_table(traced(0), dec.num_layers) for _ in range(3)]
+    best = min(tabs, key=lambda t: t["step_us"])
+    pos = PROMPT_LEN - 1 + steps // 2
+    splits = lib.qmk_attention_splits(ncta, PROMPT_LEN - 1 + steps - 1)
+    detail = phase_detail(traced(TUNE_TRACE_CLOCK), dec.num_layers, splits, pos)
+    print(format_table(best))
+    print()
+    print("inside the phases (SM cycles, clock64):")
+    print(format_detail(detail))
+    print(json.dumps({"trace": {"steps": steps, "traced_step": steps // 2, "position": pos, "ctas": ncta,
+                                "step_us": [round(t["step_us"], 2) for t in tabs], "phases": best["phases"],
+                                "lm_head": best["lm_head"], "layer_us": best["layer_us"],
+                                "detail_cycles": detail}}), flush=True)
+    return 0
+
+
 def run_batch(args) -> int:
     """BASELINE config 4 (not the headline line): B independent sequences,
     1024-token random prompts (token-parallel prefill, untimed), then
@@ -653,7 +700,11 @@ def main(argv=None) -> int:
                     help="config 3 instead of the headline: batch-1 decode after L cached positions of random K/V")
     ap.add_argument("--profile-batch", type=int, default=0, metavar="B",
                     help="run only the small ncu case of the token-parallel path: one batched step of B rows")
+    ap.add_argument("--trace", type=int, default=0, metavar="STEPS",
+                    help="print the per-phase critical path of one traced step of a STEPS-token launch")
     args = ap.parse_args(argv)
+    if args.trace:
+        return run_trace(args.trace)
     if args.profile_batch:
         return run_profile_batch(args.profile_batch)
     if args.batch:

@@ -215,8 +215,23 @@ __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned *p) {
   return v;
 }
 
+// QmkRunArgs.tuning bit 4: trace stamps in SM clock cycles (%clock64) instead
+// of %globaltimer ns.  The global timer ticks in 256 ns steps on B200, too
+// coarse for the sub-microsecond intervals inside a phase; clock64 resolves
+// them but is per SM, so only differences within one CTA are meaningful.
+constexpr unsigned kTuneTraceClock = 16u;
+
+__device__ __forceinline__ uint64_t trace_now(const Ctx &c) {
+  if (c.tuning & kTuneTraceClock) {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+    return t;
+  }
+  return global_timer_ns();
+}
+
 __device__ __forceinline__ void trace_stamp(const Ctx &c, bool active, int slot) {
-  if (active && c.trace) c.trace[slot] = global_timer_ns();
+  if (active && c.trace) c.trace[slot] = trace_now(c);
 }
 
 // Slow paths stay out of line: the kernel cycles through all of its phases
@@ -273,7 +288,7 @@ __device__ __forceinline__ bool wait_full(Ctx &c, uint32_t tile) {
   bool ok = (*c.abort_flag == 0);
   const uint32_t k = tile - c.trace_tile0;
   const bool stamp = c.trace && threadIdx.x == 0 && k < (uint32_t)kTraceTiles;
-  if (stamp) c.trace[kTraceTileBase + 2 * k] = global_timer_ns();
+  if (stamp) c.trace[kTraceTileBase + 2 * k] = trace_now(c);
   if (ok) {
     const int slot = tile % kNumSlots;
     const unsigned par = (tile / kNumSlots) & 1u;
@@ -285,14 +300,14 @@ __device__ __forceinline__ bool wait_full(Ctx &c, uint32_t tile) {
       }
     }
   }
-  if (stamp) c.trace[kTraceTileBase + 2 * k + 1] = global_timer_ns();
+  if (stamp) c.trace[kTraceTileBase + 2 * k + 1] = trace_now(c);
   return __all_sync(0xffffffffu, ok);
 }
 
 __device__ __forceinline__ void release_tile(Ctx &c, uint32_t tile, bool ok) {
   const uint32_t k = tile - c.trace_tile0;
   if (c.trace && threadIdx.x == 0 && k < (uint32_t)kTraceTiles)
-    c.trace[kTraceTileBase + 3 * kTraceTiles + k] = global_timer_ns();
+    c.trace[kTraceTileBase + 3 * kTraceTiles + k] = trace_now(c);
   __syncwarp();
   if (ok && (threadIdx.x & 31) == 0) mbar_arrive(&c.empty[tile % kNumSlots]);
 }
@@ -302,14 +317,14 @@ __device__ __forceinline__ bool wait_full_one(Ctx &c, uint32_t tile) {
   if (*c.abort_flag) return false;
   const uint32_t k = tile - c.trace_tile0;
   const bool stamp = c.trace && k < (uint32_t)kTraceTiles;
-  if (stamp) c.trace[kTraceTileBase + 2 * k] = global_timer_ns();
+  if (stamp) c.trace[kTraceTileBase + 2 * k] = trace_now(c);
   const int slot = tile % kNumSlots;
   const unsigned par = (tile / kNumSlots) & 1u;
   Waiter w;
   while (!mbar_try_wait(&c.full[slot], par)) {
     if (!w.keep_going(c, kSiteFull)) return false;
   }
-  if (stamp) c.trace[kTraceTileBase + 2 * k + 1] = global_timer_ns();
+  if (stamp) c.trace[kTraceTileBase + 2 * k + 1] = trace_now(c);
   return true;
 }
 
@@ -656,7 +671,7 @@ struct Producer {
     mbar_arrive_expect_tx(&c.full[slot], bytes);
     if (c.trace) {
       const uint32_t k = tile - c.trace_tile0;
-      if (k < (uint32_t)kTraceTiles) c.trace[kTraceTileBase + 2 * kTraceTiles + k] = global_timer_ns();
+      if (k < (uint32_t)kTraceTiles) c.trace[kTraceTileBase + 2 * kTraceTiles + k] = trace_now(c);
     }
     return c.ring + slot * kSlotBytes;
   }
@@ -987,7 +1002,7 @@ struct Consumer {
         const bool tstamp = c.trace && tid == 0 && tk < (uint32_t)kTraceTiles;
         if (got && tid == 0) {
           // both units' MMAs have read the tile: hand the ring slot back
-          if (tstamp) c.trace[kTraceTileBase + 3 * kTraceTiles + tk] = global_timer_ns();
+          if (tstamp) c.trace[kTraceTileBase + 3 * kTraceTiles + tk] = trace_now(c);
           mbar_arrive_cnt(&c.empty[(tile + (uint32_t)t) % kNumSlots], kConsumerWarps);
         }
         __syncwarp();
@@ -1003,7 +1018,7 @@ struct Consumer {
           if (!valid) v = 0.f;
         }
         tc_fence_before_sync();
-        if (tstamp) c.trace[kTraceTileBase + 4 * kTraceTiles + tk] = global_timer_ns();
+        if (tstamp) c.trace[kTraceTileBase + 4 * kTraceTiles + tk] = trace_now(c);
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         v += __shfl_xor_sync(0xffffffffu, v, 4);
@@ -1025,7 +1040,7 @@ struct Consumer {
           mbar_arrive(&c.tmem_free[seq % kTmemBufs]);
           mbar_arrive(&c.tmem_free[(seq + 1u) % kTmemBufs]);
         }
-        if (tstamp) c.trace[kTraceTileBase + 5 * kTraceTiles + tk] = global_timer_ns();
+        if (tstamp) c.trace[kTraceTileBase + 5 * kTraceTiles + tk] = trace_now(c);
       }
     }
     tile += (uint32_t)ntiles;
