@@ -16,6 +16,10 @@
 //     attention items -> P2.5 merge of the split partials -> P3 O-proj rows +
 //     residual -> P4 RMSNorm + gate/up rows + SiLU -> P5 down rows + residual;
 //     after the last layer the final RMSNorm + tied LM head + grid-wide argmax.
+//   * the layer GEMVs run on the CUDA cores straight from the ring tiles (fp32
+//     FMA over bf16 weights, input vector fp32 in shared memory); the LM head,
+//     which streams 311 MB and is bound by HBM, runs on the tensor cores
+//     (tcgen05.mma with TMEM accumulators).
 //
 // Numerics follow the reference kernel (fp32 activations and accumulation,
 // bf16 weights, bf16 K/V cache, bf16 cos/sin tables), except that the residual
@@ -108,17 +112,27 @@ constexpr int kSmX = kNumSlots * kSlotBytes;   // layer input residual, fp32 [10
 constexpr int kSmA = kSmX + 4 * kHidden;       // post-attention residual, fp32 [1024]
 constexpr int kSmAtt = kSmA + 4 * kHidden;     // attention output, fp32 [2048]
 constexpr int kSmU = kSmAtt + 4 * kQSize;      // MLP intermediate / attention scratch, fp32 [3072]
-constexpr int kSmMisc = kSmU + 4 * kInter;
+constexpr int kSmXW = kSmU + 4 * kInter;       // RMSNorm input times the norm weights, fp32 [1024]
+constexpr int kSmMisc = kSmXW + 4 * kHidden;
 // misc: full/empty mbarriers (96 B), per-warp argmax (64 B), reductions (128 B),
 // tensor-core completion mbarrier (8 B), TMEM base address (4 B)
 constexpr int kMiscRed = 160;
 constexpr int kMiscMmaBar = 288;   // [kTmemBufs] tensor-core completion (count 1)
 constexpr int kMiscTmemFree = 352; // [kTmemBufs] accumulator read by warps 0-3 (count 4)
 constexpr int kMiscTmem = 416;
+constexpr int kMiscPart = 512;     // [2][kConsumerWarps][kKsplitRows] fp32: per-warp partial row sums (K split)
+constexpr int kKsplitRows = 4;     // rows of a K-split GEMV batch
+static_assert(kMiscPart + 2 * kConsumerWarps * kKsplitRows * 4 <= 1024, "K-split partials exceed the misc area");
+// A CUDA-core GEMV phase holds all of its ring tiles at once: they must fit
+// in the ring for the smallest grid.
+static_assert((kQKVRows / kMinCtas + 1 + kQKVTileRows - 1) / kQKVTileRows <= kNumSlots, "q|k|v tiles exceed the ring");
+static_assert((kHidden / kMinCtas + 1 + kOTileRows - 1) / kOTileRows <= kNumSlots, "O tiles exceed the ring");
+static_assert((kInter / kMinCtas + kGUTileRows - 1) / kGUTileRows <= kNumSlots, "gate/up tiles exceed the ring");
+static_assert((kHidden / kMinCtas + 1 + kDTileRows - 1) / kDTileRows <= kNumSlots, "down tiles exceed the ring");
 constexpr int kTmemBufs = 8;       // GEMV units (M blocks) in flight
 constexpr int kTmemBufCols = 64;   // D of one unit: 128 lanes x N (<= 48) fp32 columns
 constexpr int kTmemCols = kTmemBufs * kTmemBufCols;
-constexpr int kSmBytes = kSmMisc + 512;
+constexpr int kSmBytes = kSmMisc + 1024;
 static_assert(kSmBytes <= 232448, "shared memory plan exceeds the sm_100 per-block limit");
 
 // Attention scratch inside the U region (floats).
@@ -333,7 +347,7 @@ __device__ __forceinline__ const uint8_t *slot_ptr(const Ctx &c, uint32_t tile) 
 }
 
 // ------------------------------------------------------------- GEMV (tcgen05)
-// y = W x for the rows of one 32 KB ring tile runs on the 5th-generation
+// LM head: y = W x for the rows of one 32 KB ring tile runs on the 5th-generation
 // tensor cores: tcgen05.mma (M = 128, N = 16S, K = 16, bf16 in, fp32
 // accumulate in TMEM) with the tile's weights as the A operand exactly as
 // the 1-D bulk copies deliver them and the activation vector as the B
@@ -431,6 +445,9 @@ enum StageMode : int {
   kStageFrag = 2,      // tensor-core B operand of the vector into bop
   kStageNormFrag = 3,  // fp32 copy into dst, B operand of x * w (norm weights
                        // prefetched in nw), returns sum of squares
+  kStageNorm = 4,      // fp32 copy into dst, fp32 x * w into dst2 (passed as
+                       // bop), returns sum of squares
+  kStageCopy = 5,      // fp32 copy into dst
 };
 
 // All consumer threads: poll the N words of `src` until their flag equals
@@ -450,9 +467,9 @@ __device__ __forceinline__ float stage_vec(Ctx &c, float *dst, uint8_t *bop, con
                                         unsigned site, float *red, NormPairs nw) {
   constexpr int kPairs = N / 2;
   constexpr int P = (kPairs + kConsumerThreads - 1) / kConsumerThreads;
-  constexpr bool kSum = (MODE == kStageSumSq || MODE == kStageNormFrag);
+  constexpr bool kSum = (MODE == kStageSumSq || MODE == kStageNormFrag || MODE == kStageNorm);
   static_assert(N % 2 == 0 && P <= 32, "stage_vec size");
-  static_assert(MODE != kStageNormFrag || P <= 4, "norm-weight pairs per thread");
+  static_assert((MODE != kStageNormFrag && MODE != kStageNorm) || P <= 4, "norm-weight pairs per thread");
   const int tid = threadIdx.x;
   unsigned pending = 0;
 #pragma unroll
@@ -482,6 +499,10 @@ __device__ __forceinline__ float stage_vec(Ctx &c, float *dst, uint8_t *bop, con
         if (MODE == kStageNormFrag) {
           const uint32_t wk = nw.w[k < 4 ? k : 3];
           store_bop_pair<N / 1024>(bop, 2 * q, v0 * bf_lo(wk), v1 * bf_hi(wk));
+        }
+        if (MODE == kStageNorm) {
+          const uint32_t wk = nw.w[k < 4 ? k : 3];
+          reinterpret_cast<float2 *>(bop)[q] = make_float2(v0 * bf_lo(wk), v1 * bf_hi(wk));
         }
         if (kSum) {
           keep[kSum ? k : 0][0] = v0;
@@ -541,6 +562,28 @@ __device__ __forceinline__ void build_norm_bop(uint8_t *bop, const float *x, con
     }
   }
   fence_proxy_async_smem();
+}
+
+// xw <- x * w (the RMSNorm weight; 1/rms is applied to the GEMV results),
+// fp32; the caller's next consumer_sync publishes it.  K = 1024.
+__device__ __forceinline__ void build_norm_xw(float *xw, const float *x, const NormPairs &nw, int tid) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int q = tid + j * kConsumerThreads;
+    if (q < kHidden / 2) {
+      const float2 v = reinterpret_cast<const float2 *>(x)[q];
+      reinterpret_cast<float2 *>(xw)[q] = make_float2(v.x * bf_lo(nw.w[j]), v.y * bf_hi(nw.w[j]));
+    }
+  }
+}
+
+// s0/s1 += 4 bf16 weights (w, two pairs) times 4 fp32 inputs (x), even and
+// odd elements in separate chains.
+__device__ __forceinline__ void dot4(float &s0, float &s1, const uint2 w, const float4 x) {
+  s0 = fmaf(x.x, bf_lo(w.x), s0);
+  s1 = fmaf(x.y, bf_hi(w.x), s1);
+  s0 = fmaf(x.z, bf_lo(w.y), s0);
+  s1 = fmaf(x.w, bf_hi(w.y), s1);
 }
 
 // Poll up to K words per thread at arbitrary addresses: word i (i < n) of the
@@ -827,7 +870,9 @@ struct Consumer {
   Ctx &c;
   const Params &p;
   uint8_t *smem;
-  float *sX, *sA, *sAtt, *sU;
+  float *sX, *sA, *sAtt, *sU, *sXW;
+  float *sPart;  // [2][kConsumerWarps][8] K-split partial sums
+  unsigned kpart_seq = 0;  // K-split phases run so far (selects the partials buffer)
   float *red_x, *red_a, *red_lm, *red_e;  // block-reduction slots, one per call site
   uint32_t tile = 0;
   unsigned mma_seq = 0;      // tensor-core units consumed (buffer = seq % kTmemBufs)
@@ -846,6 +891,8 @@ struct Consumer {
     sA = reinterpret_cast<float *>(smem + kSmA);
     sAtt = reinterpret_cast<float *>(smem + kSmAtt);
     sU = reinterpret_cast<float *>(smem + kSmU);
+    sXW = reinterpret_cast<float *>(smem + kSmXW);
+    sPart = reinterpret_cast<float *>(smem + kSmMisc + kMiscPart);
     float *red = reinterpret_cast<float *>(smem + kSmMisc + kMiscRed);
     red_x = red;
     red_a = red + 8;
@@ -1047,6 +1094,182 @@ struct Consumer {
     mma_seq += (unsigned)nunits;
   }
 
+  // GEMV phases on the CUDA cores.  The weights of a phase stream through
+  // the ring in tiles of tile_rows rows at `pitch` bytes (the layouts of the
+  // producer's bulk copies), the input vector x is fp32 in shared memory.
+  // Shared-memory bandwidth (128 B per clock) bounds these loops, so every
+  // weight byte and, as far as possible, every x byte is read once, with
+  // conflict-free accesses: lane l takes elements 4l + 128j + (0..3) of a
+  // 1024-element chunk (x as one float4 per j, weights as one 8-byte pair
+  // of bf16 pairs per j, a warp reading 256 contiguous bytes per j).
+
+  // The weight tiles of a phase are normally resident before its input
+  // arrives (the stream runs a layer ahead), so a phase waits for all of
+  // its tiles first and then gives every warp all of its work at once: the
+  // loads of several rows are in flight together, which a single warp needs
+  // to hide shared-memory latency.  The tiles are released at the end.
+  __device__ __forceinline__ bool wait_tiles(int ntiles) {
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) ok = wait_full(c, tile + (uint32_t)t) && ok;
+    return ok;
+  }
+  __device__ __forceinline__ void release_tiles(int ntiles, bool ok) {
+    for (int t = 0; t < ntiles; ++t) release_tile(c, tile + (uint32_t)t, ok);
+    tile += (uint32_t)ntiles;
+  }
+  // Address of byte `off` of row i of the phase (tiles of tile_rows rows at
+  // `pitch` bytes, consecutive ring slots).
+  __device__ __forceinline__ const uint8_t *row_ptr(int i, int tile_rows, int pitch, int off) const {
+    return slot_ptr(c, tile + (uint32_t)(i / tile_rows)) + (size_t)(i % tile_rows) * pitch + off;
+  }
+
+  // Row split (q|k|v, gate/up: K = 1024, many rows): phase row i is computed
+  // by warp i % kConsumerWarps, MR rows of a warp at a time; the warp adds
+  // the lanes' partial sums with a butterfly and lane 0 emits.  kOutGU: a
+  // gate row and, 2048 bytes further, an up row per output row.  No barrier
+  // between the warps.
+  template <int OUT, int MR>
+  __device__ void fma_rows_phase(const float *x, int r0, int r1, int tile_rows, int pitch, float scale,
+                                 unsigned E) {
+    constexpr bool kGU = (OUT == kOutGU);
+    const TcJob job{kTcRow, OUT, r0, r1, tile_rows, scale, E};
+    const int n = r1 - r0;
+    const int ntiles = (n + tile_rows - 1) / tile_rows;
+    float4 xv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xv[j] = reinterpret_cast<const float4 *>(x)[lane + 32 * j];
+    const bool ok = wait_tiles(ntiles);
+    for (int i0 = warp; ok && i0 < n; i0 += kConsumerWarps * MR) {
+      // rows i0 + 7r of this batch; rows past the end repeat row i0 (no
+      // branch inside the loop, so the rows' FMA chains interleave)
+      const uint8_t *rp[MR];
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        const int i = i0 + kConsumerWarps * r;
+        rp[r] = row_ptr(i < n ? i : i0, tile_rows, pitch, 8 * lane);
+      }
+      float s[MR][kGU ? 8 : 4];
+#pragma unroll
+      for (int r = 0; r < MR; ++r)
+#pragma unroll
+        for (int a = 0; a < (kGU ? 8 : 4); ++a) s[r][a] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint2 w[MR], u[kGU ? MR : 1];
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+          w[r] = *reinterpret_cast<const uint2 *>(rp[r] + 256 * j);
+          if (kGU) u[kGU ? r : 0] = *reinterpret_cast<const uint2 *>(rp[r] + 2048 + 256 * j);
+        }
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+          s[r][0] = fmaf(xv[j].x, bf_lo(w[r].x), s[r][0]);
+          s[r][1] = fmaf(xv[j].y, bf_hi(w[r].x), s[r][1]);
+          s[r][2] = fmaf(xv[j].z, bf_lo(w[r].y), s[r][2]);
+          s[r][3] = fmaf(xv[j].w, bf_hi(w[r].y), s[r][3]);
+          if (kGU) {
+            const uint2 q = u[kGU ? r : 0];
+            s[r][kGU ? 4 : 0] = fmaf(xv[j].x, bf_lo(q.x), s[r][kGU ? 4 : 0]);
+            s[r][kGU ? 5 : 1] = fmaf(xv[j].y, bf_hi(q.x), s[r][kGU ? 5 : 1]);
+            s[r][kGU ? 6 : 2] = fmaf(xv[j].z, bf_lo(q.y), s[r][kGU ? 6 : 2]);
+            s[r][kGU ? 7 : 3] = fmaf(xv[j].w, bf_hi(q.y), s[r][kGU ? 7 : 3]);
+          }
+        }
+      }
+      float v[MR], v2[MR];
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        v[r] = (s[r][0] + s[r][1]) + (s[r][2] + s[r][3]);
+        v2[r] = kGU ? (s[r][kGU ? 4 : 0] + s[r][kGU ? 5 : 1]) + (s[r][kGU ? 6 : 2] + s[r][kGU ? 7 : 3]) : 0.f;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+          v[r] += __shfl_xor_sync(0xffffffffu, v[r], o);
+          if (kGU) v2[r] += __shfl_xor_sync(0xffffffffu, v2[r], o);
+        }
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+          const int i = i0 + kConsumerWarps * r;
+          if (i < n) tc_emit(job, r0 + i, v[r], v2[r]);
+        }
+      }
+    }
+    release_tiles(ntiles, ok);
+  }
+
+  // K split (O: K = 2048, down: K = 3072; about as many rows per CTA as
+  // warps): the 128-element blocks of K are dealt to the warps round-robin
+  // and every warp multiplies its blocks of all rows, so x and the weights
+  // are read once per CTA.  The warps' partial row sums meet in shared
+  // memory (double-buffered) behind one consumer barrier per batch of
+  // kKsplitRows rows; thread r then adds row r's partials in warp order
+  // (deterministic) and emits it.
+  template <int KC, int OUT>
+  __device__ void fma_ksplit_phase(const float *x, int r0, int r1, int tile_rows, int pitch, unsigned E) {
+    constexpr int kBlocks = 8 * KC;  // 128-element blocks per row
+    constexpr int kMine = (kBlocks + kConsumerWarps - 1) / kConsumerWarps;
+    constexpr int RB = kKsplitRows;
+    const TcJob job{kTcRow, OUT, r0, r1, tile_rows, 1.f, E};
+    const int n = r1 - r0;
+    const int ntiles = (n + tile_rows - 1) / tile_rows;
+    float4 xv[kMine];
+#pragma unroll
+    for (int q = 0; q < kMine; ++q) {
+      const int b = warp + kConsumerWarps * q;
+      xv[q] = (b < kBlocks) ? reinterpret_cast<const float4 *>(x)[lane + 32 * b] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const bool ok = wait_tiles(ntiles);
+    for (int i0 = 0; i0 < n; i0 += RB) {  // every warp runs every batch (barrier inside)
+      float v[RB];
+#pragma unroll
+      for (int r = 0; r < RB; ++r) v[r] = 0.f;
+      if (ok) {
+        uint2 w[RB][kMine];
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (i0 + r < n) {
+            const uint8_t *rp = row_ptr(i0 + r, tile_rows, pitch, 8 * lane);
+#pragma unroll
+            for (int q = 0; q < kMine; ++q) {
+              const int b = warp + kConsumerWarps * q;
+              if (b < kBlocks) w[r][q] = *reinterpret_cast<const uint2 *>(rp + 256 * b);
+            }
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (i0 + r < n) {
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int q = 0; q < kMine; ++q)
+              if (warp + kConsumerWarps * q < kBlocks) dot4(s0, s1, w[r][q], xv[q]);
+            v[r] = s0 + s1;
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r < RB; ++r) v[r] += __shfl_xor_sync(0xffffffffu, v[r], o);
+      float *part = sPart + (kpart_seq++ & 1) * (kConsumerWarps * RB);
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < RB; ++r) part[warp * RB + r] = v[r];
+      }
+      consumer_sync();
+      if (tid < min(RB, n - i0) && ok && live()) {
+        float sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < kConsumerWarps; ++q) sum += part[q * RB + tid];
+        tc_emit(job, r0 + i0 + tid, sum, 0.f);
+      }
+    }
+    release_tiles(ntiles, ok);
+  }
+
   // Issuer threads: wait (bounded) for the last MMAs they issued, so that
   // TMEM can be freed (normally they were consumed already).
   __device__ void drain_mma() {
@@ -1082,20 +1305,16 @@ struct Consumer {
   // layer input (the embedding row of layer 0) and x_ss its sum of squares.
   __device__ void phase_qkv(const LDGLayerWeights &w, unsigned E, int l, unsigned x_flag, float x_ss) {
     const NormPairs nw = nw_pref;  // fetched one phase ahead
-    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
     const Range R = qkv_rows(c.cta, c.ncta);
-    tc_prewait(R.begin, R.end, kQKVTileRows);
     if (x_flag) {
-      x_ss = stage_vec<kHidden, kStageNormFrag>(c, sX, bop, c.wX, x_flag, kSiteX, red_x, nw);
+      x_ss = stage_vec<kHidden, kStageNorm>(c, sX, reinterpret_cast<uint8_t *>(sXW), c.wX, x_flag, kSiteX, red_x, nw);
     } else {
-      build_norm_bop(bop, sX, nw, tid);
+      build_norm_xw(sXW, sX, nw, tid);
       consumer_sync();
     }
     trace_stamp(c, tid == 0, l * 16 + 0);
-    const TcJob job{kTcRow, kOutQKV, R.begin, R.end, kQKVTileRows, rsqrtf(x_ss / (float)kHidden + kRmsEps), E};
-    tc_phase(job, bop);
+    fma_rows_phase<kOutQKV, 4>(sXW, R.begin, R.end, kQKVTileRows, 2048, rsqrtf(x_ss / (float)kHidden + kRmsEps), E);
     flush();
-    consumer_sync();  // the B operand in sU is overwritten by the next phase
     trace_stamp(c, tid == 0, l * 16 + 1);
   }
 
@@ -1421,14 +1640,11 @@ struct Consumer {
   __device__ void phase_o(const LDGLayerWeights &w, unsigned E, bool stall, int l) {
     // RMSNorm weights of P4, fetched now so that their latency is hidden.
     nw_pref = load_norm_pairs((const __nv_bfloat16 *)w.post_attn_layernorm_weight, tid);
-    uint8_t *bop = reinterpret_cast<uint8_t *>(sAtt);
     const Range R = o_rows(c.cta, c.ncta);
-    tc_prewait(R.begin, R.end, kOTileRows);
     // Test hook: 0xFFFFFFFF is never an epoch, so this wait can only expire.
-    stage_vec<kQSize, kStageFrag>(c, nullptr, bop, c.wAtt, stall ? 0xFFFFFFFFu : E, kSiteAtt, nullptr, NormPairs{});
+    stage_vec<kQSize, kStageCopy>(c, sAtt, nullptr, c.wAtt, stall ? 0xFFFFFFFFu : E, kSiteAtt, nullptr, NormPairs{});
     trace_stamp(c, tid == 0, l * 16 + 6);
-    const TcJob job{kTcHalf, kOutO, R.begin, R.end, kOTileRows, 1.f, E};
-    tc_phase(job, bop);
+    fma_ksplit_phase<2, kOutO>(sAtt, R.begin, R.end, kOTileRows, kQSize * 2, E);
     flush();
     trace_stamp(c, tid == 0, l * 16 + 7);
   }
@@ -1436,15 +1652,11 @@ struct Consumer {
   // P4: RMSNorm(a) then gate/up rows, SiLU(gate) * up -> M words.
   __device__ void phase_gate_up(const LDGLayerWeights &w, unsigned E, int l) {
     const NormPairs nw = nw_pref;  // fetched in P3
-    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
     const Range R = gu_rows(c.cta, c.ncta);
-    tc_prewait(R.begin, R.end, kGUTileRows);
-    const float ss = stage_vec<kHidden, kStageNormFrag>(c, sA, bop, c.wA, E, kSiteA, red_a, nw);
+    const float ss = stage_vec<kHidden, kStageNorm>(c, sA, reinterpret_cast<uint8_t *>(sXW), c.wA, E, kSiteA, red_a, nw);
     trace_stamp(c, tid == 0, l * 16 + 8);
-    const TcJob job{kTcGU, kOutGU, R.begin, R.end, kGUTileRows, rsqrtf(ss / (float)kHidden + kRmsEps), E};
-    tc_phase(job, bop);
+    fma_rows_phase<kOutGU, 3>(sXW, R.begin, R.end, kGUTileRows, 4096, rsqrtf(ss / (float)kHidden + kRmsEps), E);
     flush();
-    consumer_sync();  // the B operand in sU is overwritten by the next phase
     trace_stamp(c, tid == 0, l * 16 + 9);
   }
 
@@ -1453,15 +1665,11 @@ struct Consumer {
     // RMSNorm weights of the next P1 (or of the final norm), fetched now.
     nw_pref = load_norm_pairs(
         (l + 1 < p.num_layers) ? (const __nv_bfloat16 *)p.layers[l + 1].input_layernorm_weight : p.final_norm, tid);
-    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
     const Range R = d_rows(c.cta, c.ncta);
-    tc_prewait(R.begin, R.end, kDTileRows);
-    stage_vec<kInter, kStageFrag>(c, nullptr, bop, c.wM, E, kSiteM, nullptr, NormPairs{});
+    stage_vec<kInter, kStageCopy>(c, sU, nullptr, c.wM, E, kSiteM, nullptr, NormPairs{});
     trace_stamp(c, tid == 0, l * 16 + 10);
-    const TcJob job{kTcQuarter, kOutDown, R.begin, R.end, kDTileRows, 1.f, E};
-    tc_phase(job, bop);
+    fma_ksplit_phase<3, kOutDown>(sU, R.begin, R.end, kDTileRows, kDRowPitch, E);
     flush();
-    consumer_sync();  // sU (B operand) is reused by the next phase
     trace_stamp(c, tid == 0, l * 16 + 11);
   }
 

@@ -250,3 +250,45 @@ def test_batch_status_reports_bad_token():
     with pytest.raises(BatchError, match="vocabulary"):
         fw.check_status()
     fw.check_status()  # cleared
+
+
+@pytest.mark.parametrize("B", [4, 16, 64])
+def test_config4_full_depth_batches_vs_oracle(cuda_weights, B):
+    """BASELINE config 4 at full depth: the 28-layer model, B sequences with
+    random 1024-token prompts (batched prefill), then 16 batched decode steps
+    teacher forced on seeded random tokens.  Every sequence's full logit
+    vectors (the prompt's last position and the 16 steps) against the oracle
+    run on that sequence alone; greedy tokens identical wherever the
+    oracle's top-2 gap exceeds the tolerance."""
+    from oracle.qwen3_mirror import MirrorDecoder
+    from qwen_megakernel_b200 import BatchDecoder
+
+    P, steps = 1024, 16
+    msl = P + steps + 8
+    w = cuda_weights
+    g = torch.Generator().manual_seed(400 + B)
+    prompts = [[int(t) for t in torch.randint(0, V, (P,), generator=g)] for _ in range(B)]
+    forced = [[int(t) for t in torch.randint(0, V, (steps,), generator=g)] for _ in range(B)]
+    bd = BatchDecoder(w, B, max_seq_len=msl, use_graphs=False)
+    pl = torch.empty(B, V, device="cuda")
+    bd.prefill(prompts, logits=pl)
+    outs = []
+    for t in range(steps):
+        lg = torch.empty(B, V, device="cuda")
+        bd.step([forced[s][t] for s in range(B)], logits=lg)
+        outs.append(lg)
+    torch.cuda.synchronize()
+    bd.fw.check_status()
+    got_all = torch.stack([pl] + outs, dim=1)  # [B, steps + 1, V]
+    del outs, pl
+    m = MirrorDecoder(w, msl, device="cuda")
+    # the oracle on every sequence alone (a spread of them at B = 64 to bound the run time)
+    check = range(B) if B <= 16 else range(0, B, 4)
+    for s in check:
+        m.reset()
+        ref = m.prefill(prompts[s] + forced[s], 0)[P - 1:]
+        got = got_all[s]
+        _check_vs_oracle(got, ref)
+        top2 = ref.topk(2, dim=-1).values
+        conf = (top2[:, 0] - top2[:, 1]) > TOL_MAX_ABS
+        assert torch.equal(got.argmax(-1)[conf], ref.argmax(-1)[conf]), f"sequence {s}"

@@ -20,8 +20,8 @@ from conftest import TOL_MAX_ABS, TOL_REL_L2
 pytestmark = pytest.mark.gpu
 
 # Kernel vs oracle (same storage formats; they differ in fp32 summation order,
-# the kernel's hardware exp2/rcp and its activations split into two bf16
-# halves for the tensor-core GEMVs, ~2^-17 relative).  Over many layers and
+# the kernel's hardware exp2/rcp and, in the tensor-core LM head, its input
+# split into two bf16 halves, ~2^-17 relative).  Over many layers and
 # steps those tiny differences occasionally flip a bf16 rounding of a cached
 # K/V element, and the flip propagates, so the bound on the maximum is loose;
 # the mean error and the relative L2 bounds catch systematic mistakes (a
@@ -243,9 +243,17 @@ def test_reference_operator_surface(cuda_weights, decoder28, golden1):
     assert got == want_prompt
     want = decoder28.generate_ids(prompt, 24)
     assert gen == want
-    # the reference's `normalized` output holds the final RMSNorm (fp32)
-    assert torch.isfinite(s["norm_out"]).all() and s["norm_out"].abs().max().item() > 0
     assert o.default_status()[0] == 0
+    # the reference's `normalized` output holds the final RMSNorm (fp32) of
+    # the launch's last step: the oracle's normalized hidden state of the
+    # last consumed token (teacher forced on the kernel's tokens)
+    from oracle.qwen3_mirror import MirrorDecoder
+
+    stream = prompt + gen[:-1]
+    _, hidden = MirrorDecoder(w, 2048, device="cuda").prefill(stream, 0, return_hidden=True)
+    d = (s["norm_out"] - hidden[-1]).abs().max().item()
+    assert d < TOL_MAX_ABS, f"normalized output vs oracle: max |d| = {d}"
+    assert _rel_l2(s["norm_out"][None], hidden[-1][None]).item() < TOL_VS_ORACLE_REL
 
 
 def test_config2_prompt_1024_then_512_steps(decoder28, oracle28, golden2):
@@ -271,13 +279,15 @@ def test_config2_prompt_1024_then_512_steps(decoder28, oracle28, golden2):
 @pytest.mark.parametrize("ctx", [8192, 32768])
 def test_long_context_random_kv(cuda_weights, ctx):
     """KV cache filled with bf16 N(0,1) for positions
-    [0, ctx), then decode steps at positions ctx, ctx+1, ... ."""
+    [0, ctx), then all 64 decode steps of the config at positions ctx ..
+    ctx + 63 (teacher forced on seeded random tokens), every step's full
+    logit vector against the oracle."""
     from oracle.qwen3_mirror import MirrorDecoder
     from qwen_megakernel_b200 import Decoder
     from qwen_megakernel_b200.weights import rope_tables
 
-    steps = 4
-    msl = ctx + 16
+    steps = 64
+    msl = ctx + 72
     w = dict(cuda_weights)
     w["cos_table"], w["sin_table"] = rope_tables(msl, device="cuda")
     dec = Decoder(w, max_seq_len=msl)
@@ -287,12 +297,14 @@ def test_long_context_random_kv(cuda_weights, ctx):
     m = MirrorDecoder(w, msl, device="cuda")
     m.k_cache.copy_(dec.k_cache)
     m.v_cache.copy_(dec.v_cache)
-    toks = [17, 4242, 151000, 9]
+    toks = [int(t) for t in torch.randint(0, V, (steps,), generator=torch.Generator().manual_seed(ctx))]
     dec.position = ctx
     logits = torch.empty(steps, V, device="cuda")
     dec.prefill(toks, logits=logits)
     ref = m.prefill(toks, ctx)
     _check_vs_oracle(logits, ref)
-    assert torch.equal(logits.argmax(-1), ref.argmax(-1))
+    top2 = ref.topk(2, dim=-1).values
+    conf = (top2[:, 0] - top2[:, 1]) > TOL_MAX_ABS
+    assert torch.equal(logits.argmax(-1)[conf], ref.argmax(-1)[conf])
     new_k = dec.k_cache[:, :, ctx : ctx + steps].float()
     assert (new_k - m.k_cache[:, :, ctx : ctx + steps].float()).abs().max().item() < 0.05
