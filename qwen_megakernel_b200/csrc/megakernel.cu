@@ -43,7 +43,11 @@
 
 namespace qmk {
 
-constexpr int kConsumerWarps = 7;  // + 1 producer warp = 8 warps (256 threads; ptxas: 228 registers)
+#ifndef QMK_CONSUMER_WARPS
+#define QMK_CONSUMER_WARPS 7
+#endif
+constexpr int kConsumerWarps = QMK_CONSUMER_WARPS;  // + 1 producer warp
+static_assert(kConsumerWarps >= 7 && kConsumerWarps <= 15, "the LM head needs 4 TMEM reader + 3 issuer warps");
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
 
@@ -114,15 +118,19 @@ constexpr int kSmAtt = kSmA + 4 * kHidden;     // attention output, fp32 [2048]
 constexpr int kSmU = kSmAtt + 4 * kQSize;      // MLP intermediate / attention scratch, fp32 [3072]
 constexpr int kSmXW = kSmU + 4 * kInter;       // RMSNorm input times the norm weights, fp32 [1024]
 constexpr int kSmMisc = kSmXW + 4 * kHidden;
-// misc: full/empty mbarriers (96 B), per-warp argmax (64 B), reductions (128 B),
-// tensor-core completion mbarrier (8 B), TMEM base address (4 B)
-constexpr int kMiscRed = 160;
-constexpr int kMiscMmaBar = 288;   // [kTmemBufs] tensor-core completion (count 1)
-constexpr int kMiscTmemFree = 352; // [kTmemBufs] accumulator read by warps 0-3 (count 4)
-constexpr int kMiscTmem = 416;
-constexpr int kMiscPart = 512;     // [2][kConsumerWarps][kKsplitRows] fp32: per-warp partial row sums (K split)
+// misc (bytes): full/empty mbarriers, per-warp argmax (value, index), block
+// reductions (4 call sites), tensor-core completion / TMEM-free mbarriers,
+// TMEM base address, K-split partial row sums.
+constexpr int kMiscBestV = 16 * kNumSlots;
+constexpr int kMiscBestI = kMiscBestV + 64;
+constexpr int kMiscRed = kMiscBestI + 64;  // [4][16] fp32
+constexpr int kMiscMmaBar = kMiscRed + 256;  // [kTmemBufs] tensor-core completion (count 1)
+constexpr int kMiscTmemFree = kMiscMmaBar + 64; // [kTmemBufs] accumulator read by warps 0-3 (count 4)
+constexpr int kMiscTmem = kMiscTmemFree + 64;
+static_assert(kConsumerWarps <= 16, "per-warp misc slots hold 16 warps");
+constexpr int kMiscPart = kMiscTmem + 64;  // [2][kConsumerWarps][kKsplitRows] fp32: per-warp partial row sums (K split)
 constexpr int kKsplitRows = 4;     // rows of a K-split GEMV batch
-static_assert(kMiscPart + 2 * kConsumerWarps * kKsplitRows * 4 <= 1024, "K-split partials exceed the misc area");
+constexpr int kMiscBytes = kMiscPart + 2 * 16 * kKsplitRows * 4;
 // A CUDA-core GEMV phase holds all of its ring tiles at once: they must fit
 // in the ring for the smallest grid.
 static_assert((kQKVRows / kMinCtas + 1 + kQKVTileRows - 1) / kQKVTileRows <= kNumSlots, "q|k|v tiles exceed the ring");
@@ -132,7 +140,7 @@ static_assert((kHidden / kMinCtas + 1 + kDTileRows - 1) / kDTileRows <= kNumSlot
 constexpr int kTmemBufs = 8;       // GEMV units (M blocks) in flight
 constexpr int kTmemBufCols = 64;   // D of one unit: 128 lanes x N (<= 48) fp32 columns
 constexpr int kTmemCols = kTmemBufs * kTmemBufCols;
-constexpr int kSmBytes = kSmMisc + 1024;
+constexpr int kSmBytes = kSmMisc + kMiscBytes;
 static_assert(kSmBytes <= 232448, "shared memory plan exceeds the sm_100 per-block limit");
 
 // Attention scratch inside the U region (floats).
@@ -142,7 +150,8 @@ constexpr int kUV = 384;    // v [128]
 constexpr int kUKn = 512;   // new k after norm/RoPE, one bf16 cache row (256 B)
 constexpr int kUVn = 640;   // new v, one bf16 cache row (256 B)
 constexpr int kUPW = 768;   // per-warp partials [8][260]
-static_assert(kUPW + kConsumerWarps * kPartWords <= kInter, "attention scratch too large");
+// (the per-warp partials may run on into the x*w buffer, free during attention)
+static_assert(kUPW + kConsumerWarps * kPartWords <= kInter + kHidden, "attention scratch too large");
 static_assert(kMaxSplits * kMergeWordsPerSplit <= kInter, "merge scratch too large");
 
 // Optional timeline trace (one step): per CTA, per layer 16 slots
@@ -895,9 +904,9 @@ struct Consumer {
     sPart = reinterpret_cast<float *>(smem + kSmMisc + kMiscPart);
     float *red = reinterpret_cast<float *>(smem + kSmMisc + kMiscRed);
     red_x = red;
-    red_a = red + 8;
-    red_lm = red + 16;
-    red_e = red + 24;
+    red_a = red + 16;
+    red_lm = red + 32;
+    red_e = red + 48;
     tid = threadIdx.x;
     warp = tid >> 5;
     lane = tid & 31;
@@ -1954,8 +1963,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   c.ring = smem + kSmRing;
   c.full = reinterpret_cast<uint64_t *>(smem + kSmMisc);
   c.empty = c.full + kNumSlots;
-  c.warp_best_v = reinterpret_cast<float *>(smem + kSmMisc + 16 * kNumSlots);
-  c.warp_best_i = reinterpret_cast<int *>(smem + kSmMisc + 16 * kNumSlots + 4 * kConsumerWarps);
+  c.warp_best_v = reinterpret_cast<float *>(smem + kSmMisc + kMiscBestV);
+  c.warp_best_i = reinterpret_cast<int *>(smem + kSmMisc + kMiscBestI);
   c.abort_flag = &s_abort;
   c.stop_step = &s_stop;
   c.ctrl = reinterpret_cast<Ctrl *>(p.ws);
