@@ -362,6 +362,13 @@ def run_ours(args):
             cpu_baseline = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
                             "sample": f"failed: {type(e).__name__}: {e}"}
 
+    extras = {}
+    if not args.no_extras:
+        try:
+            extras = measure_extras(args, rank, ws, distributed)
+        except Exception as e:  # secondary configs are informative; never lose the headline line
+            extras = {"error": f"{type(e).__name__}: {e}"}
+
     if rank == 0:
         peak, peak_kind = measured_peak()
         lb = launch_bytes()
@@ -414,6 +421,8 @@ def run_ours(args):
         }
         if cpu_baseline is not None:
             line["cpu_baseline"] = cpu_baseline
+        if extras:
+            line["extra"] = extras
         print(json.dumps(line), flush=True)
 
     if distributed:
@@ -493,71 +502,74 @@ def run_trace(steps: int) -> int:
     return 0
 
 
-def run_batch(args) -> int:
-    """BASELINE config 4 (not the headline line): B independent sequences,
-    1024-token random prompts (token-parallel prefill, untimed), then
-    args.steps batched greedy decode steps (CUDA-graph replays, B tokens each)
-    through BatchDecoder.generate.  One JSON line."""
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
+def measure_batch(B: int, steps: int, warmup: int, seed_base: int = 100, distributed: bool = False,
+                  clock_gpu: int = 0) -> dict:
+    """BASELINE config 4 (and config 5's batch-16 replicas): B independent
+    sequences, 1024-token random prompts (token-parallel prefill, untimed),
+    then `steps` batched greedy decode steps (CUDA-graph replays, B tokens
+    each) through BatchDecoder.generate.  Device time with CUDA events,
+    max over ranks when distributed."""
+    dev = torch.device("cuda", torch.cuda.current_device())
     from qwen_megakernel_b200 import BatchDecoder
-    from qwen_megakernel_b200._native import loaded_library_paths
     from qwen_megakernel_b200.weights import random_weights
 
-    B, K, W = args.batch, args.steps, args.warmup
-    weights = random_weights(seed=0, device="cuda", max_seq_len=2048)
+    weights = random_weights(seed=0, device=dev, max_seq_len=2048)
     bd = BatchDecoder(weights, B, max_seq_len=2048)
-    prompts = [prompt_for_rank(100 + s) for s in range(B)]
+    prompts = [prompt_for_rank(seed_base + s) for s in range(B)]
     first = bd.prefill(prompts)
     pos0 = bd.positions[0]
-    bd.generate(first, W)  # capture + warm-up (advances positions by W)
+    bd.generate(first, max(1, warmup))  # capture + warm-up (advances positions)
     torch.cuda.synchronize(dev)
     p_start = bd.positions[0]
     stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(0)
+    sampler = ClockSampler(clock_gpu)
+    barrier(distributed)
+    torch.cuda.synchronize(dev)
     sampler.start()
     e0.record(stream)
-    log = bd.generate(first, K)
+    log = bd.generate(first, steps)
     e1.record(stream)
     torch.cuda.synchronize(dev)
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1)
+    barrier(distributed)
+    ms = reduce_max(e0.elapsed_time(e1), distributed)
     # end to end: host tokens in, host token log out
-    bd2_first = first
     t0 = time.perf_counter()
-    out = bd.generate(bd2_first, K).cpu()
-    e2e_ms = (time.perf_counter() - t0) * 1000.0
+    out = bd.generate(first, steps).cpu()
+    e2e_ms = reduce_max((time.perf_counter() - t0) * 1000.0, distributed)
     bd.fw.check_status()
-    step_bytes = [WEIGHT_BYTES + B * KV_BYTES_PER_POS * (p + 1) for p in range(p_start, p_start + K)]
+    step_bytes = [WEIGHT_BYTES + B * KV_BYTES_PER_POS * (p + 1) for p in range(p_start, p_start + steps)]
     achieved = sum(step_bytes) / (ms / 1000.0) / 1e9
     peak, peak_kind = measured_peak()
-    line = {
+    del log
+    return {
         "metric": f"batched decode tok/s (Qwen3-0.6B bf16, ctx 1k, B={B})",
-        "value": round(B * K / (ms / 1000.0), 1),
-        "unit": "tok/s",
-        "n_gpus": 1,
-        "steps": K,
-        "warmup": W,
-        "ms_per_step": round(ms / K, 4),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
-        "config": {"workload": f"configs[4]-style: {B} sequences, 1024-token prompts, {K} greedy steps "
-                               f"(cache positions {p_start}..{p_start + K - 1})", "batch": B,
-                   "path": "token-parallel (qmk_batch_forward), CUDA-graph step"},
+        "value": round(B * steps / (ms / 1000.0), 1), "unit": "tok/s", "steps": steps, "warmup": warmup,
+        "ms_per_step": round(ms / steps, 4), "batch": B,
+        "workload": f"configs[3]-style: {B} sequences, 1024-token prompts, {steps} greedy steps "
+                    f"(cache positions {p_start}..{p_start + steps - 1}), CUDA-graph step",
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "algorithmic_bytes_per_step": int(sum(step_bytes) / K)},
-        "e2e": {"value": round(B * K / (e2e_ms / 1000.0), 1), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                     "algorithmic_bytes_per_step": int(sum(step_bytes) / steps)},
+        "e2e": {"value": round(B * steps / (e2e_ms / 1000.0), 1), "unit": "tok/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 4 * B},
-        "prefill_positions": pos0,
-        "clocks": clocks,
-        "tokens_sample": out[:2, :4].tolist(),
-        "native_libraries": [os.path.basename(p) for p in loaded_library_paths()],
+        "prefill_positions": pos0, "clocks": clocks, "tokens_sample": out[:2, :4].tolist(),
     }
+
+
+def run_batch(args) -> int:
+    """BASELINE config 4 as its own JSON line: `bench.py --batch B`."""
+    torch.cuda.set_device(0)
+    from qwen_megakernel_b200._native import loaded_library_paths
+
+    r = measure_batch(args.batch, args.steps, args.warmup)
+    line = {k: v for k, v in r.items() if k not in ("workload", "batch")}
+    line.update({"n_gpus": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                 "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
+                 "config": {"workload": r["workload"], "batch": r["batch"],
+                            "path": "token-parallel (qmk_batch_forward), CUDA-graph step"},
+                 "native_libraries": [os.path.basename(p) for p in loaded_library_paths()]})
     print(json.dumps(line), flush=True)
     return 0
 
@@ -585,36 +597,33 @@ def run_profile_batch(B: int) -> int:
     return 0
 
 
-def run_long_context(args) -> int:
-    """BASELINE config 3 (not the headline line): the K/V cache holds bf16
-    N(0, 1) at positions [0, L) (seed 2), then one launch of args.steps
-    greedy decode steps at positions L, L+1, ... through the megakernel."""
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
+def measure_long_context(L: int, steps: int, warmup: int, reps: int = 3) -> dict:
+    """the K/V cache holds bf16 N(0, 1) at positions
+    [0, L) (seed 2), then launches of `steps` greedy decode steps at
+    positions L, L+1, ... through the megakernel (mean of `reps` launches)."""
+    dev = torch.device("cuda", torch.cuda.current_device())
     from qwen_megakernel_b200 import Decoder
     from qwen_megakernel_b200.weights import random_weights, rope_tables
 
-    L, K, W = args.ctx, args.steps, args.warmup
-    msl = L + K + 8
-    weights = random_weights(seed=0, device="cuda", max_seq_len=2048)
-    weights["cos_table"], weights["sin_table"] = rope_tables(msl, device="cuda")
+    msl = L + steps + 8
+    weights = random_weights(seed=0, device=dev, max_seq_len=2048)
+    weights["cos_table"], weights["sin_table"] = rope_tables(msl, device=dev)
     dec = Decoder(weights, max_seq_len=msl)
-    gen = torch.Generator(device="cuda").manual_seed(2)
+    gen = torch.Generator(device=dev).manual_seed(2)
     dec.k_cache[:, :, :L].normal_(generator=gen)
     dec.v_cache[:, :, :L].normal_(generator=gen)
     first = torch.tensor([17], dtype=torch.int32, device=dev)
-    log = torch.empty(K, dtype=torch.int32, device=dev)
+    log = torch.empty(steps, dtype=torch.int32, device=dev)
 
     def launch():
-        dec.decode_steps(K, forced_tokens=first, start_position=L, output_log=log)
+        dec.decode_steps(steps, forced_tokens=first, start_position=L, output_log=log)
 
-    for _ in range(W):
+    for _ in range(max(1, warmup)):
         launch()
     torch.cuda.synchronize(dev)
-    sampler = ClockSampler(0)
+    sampler = ClockSampler(torch.cuda.current_device())
     sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 3
     e0.record()
     for _ in range(reps):
         launch()
@@ -623,40 +632,52 @@ def run_long_context(args) -> int:
     clocks = sampler.stop()
     dec.check_status()
     ms = e0.elapsed_time(e1) / reps
-    launch_b = K * WEIGHT_BYTES + kv_bytes(L, K)
+    launch_b = steps * WEIGHT_BYTES + kv_bytes(L, steps)
     achieved = launch_b / (ms / 1000.0) / 1e9
     peak, peak_kind = measured_peak()
-    print(json.dumps({
-        "metric": f"batch-1 decode tok/s (Qwen3-0.6B bf16, ctx {L})", "value": round(K / (ms / 1000.0), 2),
-        "unit": "tok/s", "n_gpus": 1, "steps": reps, "warmup": W, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "dtype": "bf16",
-        "data": "synthetic (seeded random-init weights, K/V cache N(0,1) at positions [0, L))",
-        "config": {"workload": f"configs[3]-style: {K} greedy steps at positions {L}..{L + K - 1}, one launch",
-                   "ctx": L, "attention_splits_per_kv_head": 18},
+    return {
+        "metric": f"batch-1 decode tok/s (Qwen3-0.6B bf16, ctx {L})", "value": round(steps / (ms / 1000.0), 2),
+        "unit": "tok/s", "steps": steps, "reps": reps, "ms_per_launch": round(ms, 4),
+        "per_token_us": round(ms / steps * 1000.0, 2),
+        "workload": f"configs[2]: {steps} greedy steps at positions {L}..{L + steps - 1}, one launch; "
+                    f"K/V cache N(0,1) at positions [0, {L})",
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": launch_b},
-        "per_token_us": round(ms / K * 1000.0, 2), "clocks": clocks}), flush=True)
+        "clocks": clocks,
+    }
+
+
+def run_long_context(args) -> int:
+    """BASELINE config 3 as its own JSON line: `bench.py --ctx L`."""
+    torch.cuda.set_device(0)
+    r = measure_long_context(args.ctx, args.steps, args.warmup)
+    line = {k: v for k, v in r.items() if k != "workload"}
+    line.update({"n_gpus": 1, "higher_is_better": True, "dtype": "bf16",
+                 "data": "synthetic (seeded random-init weights, K/V cache N(0,1) at positions [0, L))",
+                 "config": {"workload": r["workload"], "ctx": args.ctx}})
+    print(json.dumps(line), flush=True)
     return 0
 
 
-def run_prefill(args) -> int:
-    """Token-parallel prompt prefill (not the headline line): a 1024-token
-    prompt through Decoder.prefill_batched, args.steps timed repetitions."""
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
+def measure_prefill(steps: int, warmup: int) -> dict:
+    """Token-parallel prompt prefill: a 1024-token prompt through
+    Decoder.prefill_batched, median of `steps` timed repetitions."""
+    dev = torch.device("cuda", torch.cuda.current_device())
     from qwen_megakernel_b200 import Decoder
     from qwen_megakernel_b200.weights import random_weights
 
-    weights = random_weights(seed=0, device="cuda", max_seq_len=2048)
+    weights = random_weights(seed=0, device=dev, max_seq_len=2048)
     dec = Decoder(weights, max_seq_len=2048)
     prompt = prompt_for_rank(0)
-    for _ in range(max(1, args.warmup)):
+    for _ in range(max(1, warmup)):
         dec.reset()
         dec.prefill_batched(prompt)
     torch.cuda.synchronize(dev)
+    sampler = ClockSampler(torch.cuda.current_device())
+    sampler.start()
     times = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         dec.reset()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -665,23 +686,59 @@ def run_prefill(args) -> int:
         e1.record()
         torch.cuda.synchronize(dev)
         times.append(e0.elapsed_time(e1))
+    clocks = sampler.stop()
     ms = statistics.median(times)
     flops = 2 * 2 * 595_984_384 * PROMPT_LEN  # stacked hi/lo GEMMs: twice the model's 2 N flops per token
-    peak_tf = 1590.0
+    peak_tf, kind = 1590.0, "fallback"
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peak_tf = float(json.load(f).get("bf16_tflops", peak_tf))
-    except (OSError, ValueError):
+            peak_tf, kind = float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, ValueError, KeyError):
         pass
-    print(json.dumps({
+    return {
         "metric": "prefill tok/s (Qwen3-0.6B bf16, 1024-token prompt, token-parallel)",
         "value": round(PROMPT_LEN / (ms / 1000.0), 1), "unit": "tok/s", "ms_per_prompt": round(ms, 3),
-        "steps": args.steps, "warmup": args.warmup, "dtype": "bf16",
+        "steps": steps, "warmup": warmup,
         "roofline": {"bound": "tensor", "achieved": round(flops / (ms / 1000.0) / 1e12, 1), "peak": peak_tf,
                      "unit": "TFLOP/s", "frac": round(flops / (ms / 1000.0) / 1e12 / peak_tf, 4),
-                     "flops_per_prompt": flops},
-        "next_token": tok}), flush=True)
+                     "flops_per_prompt": flops, "peak_kind": kind},
+        "next_token": tok, "clocks": clocks,
+    }
+
+
+def run_prefill(args) -> int:
+    torch.cuda.set_device(0)
+    r = measure_prefill(args.steps, args.warmup)
+    r["dtype"] = "bf16"
+    print(json.dumps(r), flush=True)
     return 0
+
+
+def measure_extras(args, rank: int, ws: int, distributed: bool) -> dict:
+    """The secondary BASELINE configs as extra keys of the headline line.
+    One GPU: configs[2] (ctx 8192 and 32768, 64 steps), configs[3] (B = 4,
+    16, 64; 64 batched steps) and the 1024-token prefill.  N GPUs (config
+    5): every rank also decodes a batch of 16 of its own sequences; the
+    whole-job rate is all ranks' tokens over the slowest rank's time."""
+    extras = {}
+    torch.cuda.empty_cache()
+    if ws == 1:
+        for L in (8192, 32768):
+            extras[f"ctx{L}"] = measure_long_context(L, 64, 1, reps=2)
+            torch.cuda.empty_cache()
+        for B in (4, 16, 64):
+            extras[f"batch{B}"] = measure_batch(B, 64, 3)
+            torch.cuda.empty_cache()
+        extras["prefill1024"] = measure_prefill(5, 2)
+    else:
+        r = measure_batch(16, 64, 3, seed_base=1000 * (rank + 1), distributed=distributed,
+                          clock_gpu=torch.cuda.current_device())
+        total = 16 * 64 * ws
+        r["value"] = round(total / (r["ms_per_step"] * 64 / 1000.0), 1)
+        r["metric"] = "batched decode tok/s, batch-16 replicas (whole job)"
+        r["n_gpus"] = ws
+        extras["batch16_replicas"] = r
+    return extras
 
 
 def main(argv=None) -> int:
@@ -691,6 +748,8 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the secondary configs (ctx 8k/32k, batches 4/16/64, prefill; N>1: batch-16 replicas)")
     ap.add_argument("--profile-case", type=int, default=0, metavar="STEPS",
                     help="run only the small ncu case: one decode launch of STEPS tokens")
     ap.add_argument("--batch", type=int, default=0, metavar="B",
