@@ -345,6 +345,22 @@ size_t qmk_batch_workspace_bytes(int num_rows, int num_out);
  * (QMK_ERR_ARGS, QMK_ERR_WORKSPACE, QMK_ERR_CUDA). */
 int qmk_batch_forward(const QmkBatchArgs *args, cudaStream_t stream);
 
+/* ---- tensor-core GEMM of the token-parallel path -------------------------
+ * No reference counterpart (the reference has no token-parallel path).  The
+ * GEMM qmk_batch_forward runs every projection and the prompt attention with
+ * (tcgen05, TMEM accumulators, TMA operand ring), exported for tests and for
+ * callers that want it directly:
+ *   C[z][s] = A[z][:, K_s] * W[z][:, K_s]^T, z < batch, s < splits
+ * with W bf16 [n, k] (row stride ldw elements, batch stride w_batch_stride),
+ * A bf16 [rows, k] (lda, a_batch_stride), C fp32 [rows, n] (ldc,
+ * c_batch_stride), split s of the K blocks into C + s * c_split_stride.
+ * Operands 16-byte aligned, ldw / lda / batch strides multiples of 8,
+ * splits > 1 only with k a multiple of 64.  A wait that exceeds 1 s sets
+ * QMK_BATCH_TIMEOUT in *status (optional) and leaves C unwritten. */
+int qmk_gemm_bf16_nt(const void *W, long long ldw, long long w_batch_stride, int n, const void *A, long long lda,
+                     long long a_batch_stride, int rows, int k, int batch, int splits, float *C, long long ldc,
+                     long long c_batch_stride, long long c_split_stride, unsigned int *status, cudaStream_t stream);
+
 /* Library version string. */
 const char *qmk_version(void);
 

@@ -2,7 +2,7 @@
 
 Outputs, next to this file:
   libqwen_megakernel.so   the C-ABI library (kernels + launchers), nvcc, static
-                          cudart, cuBLAS for the token-parallel path's GEMMs
+                          cudart; no vendor GEMM library
   qwen_megakernel_C.so    the torch operator library (TORCH_LIBRARY qwen_megakernel_C)
 
 Mirrors the role of the reference's qwen_megakernel/build.py (JIT
@@ -46,6 +46,7 @@ NVCC_FLAGS = ARCH_FLAGS + [
 KERNEL_SOURCES = [
     os.path.join(CSRC, "megakernel.cu"),
     os.path.join(CSRC, "batch.cu"),
+    os.path.join(CSRC, "gemm_tc.cu"),
 ]
 KERNEL_DEPS = KERNEL_SOURCES + [
     os.path.join(CSRC, "qmk_device.cuh"),
@@ -106,11 +107,10 @@ def _run(cmd: list[str], verbose: bool) -> None:
 
 
 def _link_flags() -> list[str]:
-    """cuBLAS (the token-parallel path's GEMMs).  torch loads its own
-    libcublas.so.12 first when it is imported; the rpath covers ctypes-only
-    use of the library."""
-    lib64 = os.path.join(_cuda_home(), "lib64")
-    return [f"-L{lib64}", "-lcublas", "-Xlinker", f"-rpath={lib64}"]
+    """Static cudart only: every kernel is this library's own (the GEMMs of
+    the token-parallel path included); the driver's tensor-map encoder is
+    reached through cudaGetDriverEntryPoint, so no libcuda link either."""
+    return []
 
 
 def build_kernel_library(force: bool = False, verbose: bool = False) -> str:

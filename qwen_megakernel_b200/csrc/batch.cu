@@ -23,7 +23,6 @@
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
-#include <cublas_v2.h>
 
 #include <algorithm>
 #include <cstdarg>
@@ -161,7 +160,7 @@ __global__ void __launch_bounds__(256) residual_norm_split_kernel(float *__restr
 }
 
 // Per-head RMSNorm of q and k (weights [128]) of the stacked QKV GEMM output
-// [2 rows, 4096], RoPE (rotate-half, bf16 tables) at the row's position, K/V rounded to bf16 into the sequence's
+// [2 rows, 4096] (nsplit K-split partials split_stride floats apart), RoPE (rotate-half, bf16 tables) at the row's position, K/V rounded to bf16 into the sequence's
 // cache, q scaled by attn_scale * log2(e) (scores in log2 units).  Grid:
 // rows, 256 threads: warp w takes q heads w and w + 8, K/V head w; lane l
 // holds dims 4l .. 4l + 3, the rotation partner (d +- 64) sits in lane l ^ 16.
@@ -170,7 +169,8 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
     const __nv_bfloat16 *__restrict__ k_norm, const __nv_bfloat16 *__restrict__ cos_t,
     const __nv_bfloat16 *__restrict__ sin_t, const int *__restrict__ row_seq, const int *__restrict__ row_pos,
     __nv_bfloat16 *__restrict__ k_cache, __nv_bfloat16 *__restrict__ v_cache, long long kv_seq_stride,
-    int num_seqs, int layer, int max_seq_len, float q_scale, float *__restrict__ q_out, unsigned *status) {
+    int num_seqs, int layer, int max_seq_len, float q_scale, float *__restrict__ q_out, unsigned *status,
+    int nsplit, long long split_stride) {
   const int r = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq = row_seq[r], pos = row_pos[r];
@@ -185,10 +185,18 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
   const float sf[4] = {bf_lo(sv.x), bf_hi(sv.x), bf_lo(sv.y), bf_hi(sv.y)};
   const float *row = qkv + (size_t)r * kQKV;
   const float *row_lo = qkv + (size_t)(gridDim.x + r) * kQKV;  // stacked GEMM output: hi + lo rows
-  auto load4 = [&](int col) {
-    const float4 h = *reinterpret_cast<const float4 *>(row + col);
-    const float4 l = *reinterpret_cast<const float4 *>(row_lo + col);
-    return make_float4(h.x + l.x, h.y + l.y, h.z + l.z, h.w + l.w);
+  auto load4 = [&](int col) {  // hi + lo rows of every K-split partial, in split order
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const size_t o = (size_t)sp * (size_t)split_stride;
+      const float4 h = *reinterpret_cast<const float4 *>(row + o + col);
+      const float4 l = *reinterpret_cast<const float4 *>(row_lo + o + col);
+      acc.x += h.x + l.x;
+      acc.y += h.y + l.y;
+      acc.z += h.z + l.z;
+      acc.w += h.w + l.w;
+    }
+    return acc;
   };
   auto norm_rope = [&](int col, const __nv_bfloat16 *nw, float (&y)[4]) {
     const float4 x4 = load4(col + d0);
@@ -555,10 +563,11 @@ __global__ void __launch_bounds__(256) qsplit_kernel(const float *__restrict__ q
 
 // Softmax of score row i (< 2R: q head 2g + i / R, position r = i % R) over
 // keys j <= r: s_j = S[g][i][j] + S[g][2R + i][j]; P[g][i][j] / P[g][2R+i][j]
-// = bf16 hi / lo of exp2(s_j - max) / sum, zero for j > r.  Grid (2R, 8),
+// = bf16 hi / lo of exp2(s_j - max) / sum, zero for j > r (P rows at a
+// stride of Rp >= R elements, a multiple of 8 for the GEMM's TMA).  Grid (2R, 8),
 // 256 threads, up to kGemmAttnMaxRows / 256 keys per thread.
 __global__ void __launch_bounds__(256) softmax_split_kernel(const float *__restrict__ S,
-                                                            __nv_bfloat16 *__restrict__ P, int R) {
+                                                            __nv_bfloat16 *__restrict__ P, int R, int Rp) {
   __shared__ float red[8];
   constexpr int kPer = kGemmAttnMaxRows / 256;
   const int i = blockIdx.x, g = blockIdx.y, r = i % R;
@@ -589,8 +598,8 @@ __global__ void __launch_bounds__(256) softmax_split_kernel(const float *__restr
     l += v[k];
   }
   const float inv = 1.f / block_sum256(l, red);  // key 0 is always present: sum >= 1
-  __nv_bfloat16 *p_hi = P + ((size_t)g * 4 * R + i) * R;
-  __nv_bfloat16 *p_lo = P + ((size_t)g * 4 * R + 2 * (size_t)R + i) * R;
+  __nv_bfloat16 *p_hi = P + ((size_t)g * 4 * R + i) * Rp;
+  __nv_bfloat16 *p_lo = P + ((size_t)g * 4 * R + 2 * (size_t)R + i) * Rp;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
     const int j = threadIdx.x + 256 * k;
@@ -619,20 +628,45 @@ __global__ void __launch_bounds__(256) att_combine_kernel(const float *__restric
   }
 }
 
-// m = SiLU(gate) * up from the stacked gate|up GEMM output gu2 [2R, 6144],
-// split into the stacked down-projection input a2 [2R, 3072].  Grid: rows
+// Vt[g][d][p] = V[g][p][d] for positions p < R of one layer's V cache (the
+// P V GEMM wants both operands K-major: K = positions).  Grid (ceil(R / 64),
+// 8 KV heads), 256 threads; a 64-position x 128-dim tile through shared
+// memory.  Vt rows at a stride of Rp elements.
+__global__ void __launch_bounds__(256) vtrans_kernel(const __nv_bfloat16 *__restrict__ v_layer, long long head_stride,
+                                                     int R, int Rp, __nv_bfloat16 *__restrict__ vt) {
+  __shared__ __nv_bfloat16 t[64][kHeadDim + 2];
+  const int p0 = blockIdx.x * 64, g = blockIdx.y;
+  const __nv_bfloat16 *src = v_layer + (size_t)g * (size_t)head_stride;
+  for (int i = threadIdx.x; i < 64 * kHeadDim; i += 256) {
+    const int p = i / kHeadDim, d = i % kHeadDim;
+    t[p][d] = (p0 + p < R) ? src[(size_t)(p0 + p) * kHeadDim + d] : __float2bfloat16(0.f);
+  }
+  __syncthreads();
+  __nv_bfloat16 *dst = vt + (size_t)g * kHeadDim * (size_t)Rp;
+  for (int i = threadIdx.x; i < 64 * kHeadDim; i += 256) {
+    const int d = i / 64, p = i % 64;
+    if (p0 + p < R) dst[(size_t)d * Rp + p0 + p] = t[p][d];
+  }
+}
+
+// m = SiLU(gate) * up from the stacked gate|up GEMM output gu2 [2R, 6144]
+// (nsplit K-split partials split_stride floats apart), split into the stacked down-projection input a2 [2R, 3072].  Grid: rows
 // (R = gridDim.x), 256 threads, 12 elements each.
 __global__ void __launch_bounds__(256) silu_split_kernel(const float *__restrict__ gu2,
-                                                         __nv_bfloat16 *__restrict__ a2) {
+                                                         __nv_bfloat16 *__restrict__ a2, int nsplit,
+                                                         long long split_stride) {
   const int r = blockIdx.x, R = gridDim.x;
-  const float *hi_row = gu2 + (size_t)r * (2 * kInter);
-  const float *lo_row = gu2 + (size_t)(R + r) * (2 * kInter);
   for (int c = threadIdx.x; c < kInter / 4; c += 256) {
-    const float4 gh = reinterpret_cast<const float4 *>(hi_row)[c], gl = reinterpret_cast<const float4 *>(lo_row)[c];
-    const float4 uh = reinterpret_cast<const float4 *>(hi_row + kInter)[c];
-    const float4 ul = reinterpret_cast<const float4 *>(lo_row + kInter)[c];
-    const float gg[4] = {gh.x + gl.x, gh.y + gl.y, gh.z + gl.z, gh.w + gl.w};
-    const float uu[4] = {uh.x + ul.x, uh.y + ul.y, uh.z + ul.z, uh.w + ul.w};
+    float gg[4] = {0.f, 0.f, 0.f, 0.f}, uu[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int sp = 0; sp < nsplit; ++sp) {  // K-split partials in split order
+      const float *hi_row = gu2 + (size_t)sp * (size_t)split_stride + (size_t)r * (2 * kInter);
+      const float *lo_row = gu2 + (size_t)sp * (size_t)split_stride + (size_t)(R + r) * (2 * kInter);
+      const float4 gh = reinterpret_cast<const float4 *>(hi_row)[c], gl = reinterpret_cast<const float4 *>(lo_row)[c];
+      const float4 uh = reinterpret_cast<const float4 *>(hi_row + kInter)[c];
+      const float4 ul = reinterpret_cast<const float4 *>(lo_row + kInter)[c];
+      gg[0] += gh.x + gl.x; gg[1] += gh.y + gl.y; gg[2] += gh.z + gl.z; gg[3] += gh.w + gl.w;
+      uu[0] += uh.x + ul.x; uu[1] += uh.y + ul.y; uu[2] += uh.z + ul.z; uu[3] += uh.w + ul.w;
+    }
     float y[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) y[e] = gg[e] * fast_rcp(1.0f + fast_exp2(-gg[e] * kLog2e)) * uu[e];
@@ -711,23 +745,39 @@ int fail(int code, const char *fmt, ...) {
 }
 
 constexpr size_t kAlign = 256;
-constexpr size_t kCublasWorkspace = 32u << 20;
 
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 // Workspace regions for R rows and O output rows, in order (GEMM inputs and
 // outputs stacked: 2R or 2O rows, hi halves then lo halves).
 struct Layout {
-  size_t x, a2, qkv2, q, c2, gu2, partial, qs, sc, pr, ob, lm2, logits2, cublas, total;
+  size_t x, a2, qkv2, q, c2, gu2, partial, qs, sc, pr, vt, ob, lm2, logits2, total;
 };
 
-// K splits of the N = 1024 projections (O, down) for R rows.  With few rows
-// cuBLAS tiles N = 1024 into ~16 CTAs that cannot stream the weight at HBM
-// speed; the K chunks as a batch multiply the CTAs, the partial sums are
-// added by residual_norm_split_kernel.
-constexpr int kMaxSplitK = 4;
-constexpr int kSplitKRows = 64;
-int split_k(int R) { return R <= kSplitKRows ? kMaxSplitK : 1; }
+// K splits of a projection GEMM with n outputs over rows2 stacked rows: with
+// few rows the GEMM has few 128 x TN tiles (n / 128 weight-row tiles, one
+// activation tile), too few CTAs to stream the weights at HBM speed; K
+// chunks multiply the CTAs (up to ~one wave of 148 SMs) and the consumer of
+// the output adds the partial products in split order.
+constexpr int kMaxSplitK = 8;
+int gemm_tile_n(int rows2) { return rows2 <= 32 ? 32 : rows2 <= 64 ? 64 : rows2 <= 128 ? 128 : 256; }
+int split_k(int n, int rows2, int k) {
+  const int tiles = ((n + 127) / 128) * ((rows2 + gemm_tile_n(rows2) - 1) / gemm_tile_n(rows2));
+  int s = 1;
+  while (2 * s <= kMaxSplitK && 2 * s * tiles <= 148 && k / (2 * s) >= 256) s *= 2;
+  return s;
+}
+// Rows of a split-K output region for up to R rows: max over r <= R of
+// splits(r) 2r (so that a workspace for R rows serves every smaller call).
+size_t split_rows(int R, int n, int k) {
+  size_t best = 0;
+  for (int r = 1; r <= R; ++r) {
+    const size_t v = (size_t)split_k(n, 2 * r, k) * 2 * (size_t)r;
+    if (v > best) best = v;
+  }
+  return best;
+}
+int round8(int v) { return (v + 7) / 8 * 8; }
 
 Layout layout(int R, int O) {
   using namespace qmb;
@@ -740,25 +790,24 @@ Layout layout(int R, int O) {
   };
   L.x = take((size_t)R * kHidden * 4);
   L.a2 = take((size_t)2 * R * kInter * 2);  // largest GEMM input: K = 3072
-  L.qkv2 = take((size_t)2 * R * kQKV * 4);
+  L.qkv2 = take(split_rows(R, kQKV, kHidden) * kQKV * 4);
   L.q = take((size_t)R * kQSize * 4);
-  // O and down outputs: split_k(R) K-split partials of 2R rows each, sized
-  // 2 max(R, kMaxSplitK min(R, kSplitKRows)) rows so the total grows with R
-  L.c2 = take((size_t)2 * std::max<size_t>(R, (size_t)kMaxSplitK * std::min(R, kSplitKRows)) * kHidden * 4);
-  L.gu2 = take((size_t)2 * R * 2 * kInter * 4);
+  L.c2 = take(std::max(split_rows(R, kHidden, kQSize), split_rows(R, kHidden, kInter)) * kHidden * 4);
+  L.gu2 = take(split_rows(R, 2 * kInter, kHidden) * 2 * kInter * 4);
   // split states (used up to kAttSplitRows rows; sized so that the total
   // grows with R: a workspace for R rows serves every smaller call)
   L.partial = take((size_t)(R < kAttSplitRows ? R : kAttSplitRows) * kNumKVHeads * kAttMaxSplits * kAttPartWords * 4);
   // tensor-core prompt attention (causal runs of kAttSplitRows < R rows;
   // sized for min(R, kGemmAttnMaxRows) so that the total grows with R)
   const size_t Rg = (R > kAttSplitRows) ? (size_t)(R < kGemmAttnMaxRows ? R : kGemmAttnMaxRows) : 0;
+  const size_t Rgp = (size_t)round8((int)Rg);
   L.qs = take(kNumKVHeads * 4 * Rg * kHeadDim * 2);
   L.sc = take(kNumKVHeads * 4 * Rg * Rg * 4);
-  L.pr = take(kNumKVHeads * 4 * Rg * Rg * 2);
+  L.pr = take(kNumKVHeads * 4 * Rg * Rgp * 2);
+  L.vt = take(kNumKVHeads * kHeadDim * Rgp * 2);
   L.ob = take(kNumKVHeads * 4 * Rg * kHeadDim * 4);
   L.lm2 = take((size_t)2 * O * kHidden * 2);
   L.logits2 = take((size_t)2 * O * kVocab * 4);
-  L.cublas = take(kCublasWorkspace);
   L.total = off;
   return L;
 }
@@ -774,45 +823,15 @@ int attention_splits(int R) {
 }
 
 constexpr int kMaxDevices = 64;
-cublasHandle_t g_handles[kMaxDevices] = {};
 bool g_att_smem_set[kMaxDevices] = {};  // attention_kernel's dynamic shared memory limit raised
 std::mutex g_batch_mutex;
 
-const char *cublas_name(cublasStatus_t s) {
-  switch (s) {
-    case CUBLAS_STATUS_SUCCESS: return "success";
-    case CUBLAS_STATUS_NOT_INITIALIZED: return "not initialized";
-    case CUBLAS_STATUS_ALLOC_FAILED: return "alloc failed";
-    case CUBLAS_STATUS_INVALID_VALUE: return "invalid value";
-    case CUBLAS_STATUS_ARCH_MISMATCH: return "arch mismatch";
-    case CUBLAS_STATUS_EXECUTION_FAILED: return "execution failed";
-    case CUBLAS_STATUS_NOT_SUPPORTED: return "not supported";
-    default: return "error";
-  }
-}
-
-// C[rows, n] (fp32, row stride ldc) = A[rows, k] W[n, k]^T with bf16 A (row
-// stride k) and W (row-major [n, k]): one cuBLAS call, fp32 accumulation.
-// cuBLAS is column-major: this is C^T = W * A^T, i.e. op(W) = T, op(A) = N.
-cublasStatus_t gemm(cublasHandle_t h, int rows, int n, int k, const void *W, const void *A, float *C, int ldc) {
-  const float one = 1.f, zero = 0.f;
-  return cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, n, rows, k, &one, W, CUDA_R_16BF, k, A, CUDA_R_16BF, k, &zero, C,
-                      CUDA_R_32F, ldc, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-}
-
-// Split-K form of gemm: nsplit partial products C_s = A[:, K_s] W[:, K_s]^T
-// over equal K chunks, C_s at C + s rows ldc, as one strided-batched call.
-cublasStatus_t gemm_splitk(cublasHandle_t h, int rows, int n, int k, const void *W, const void *A, float *C, int ldc,
-                           int nsplit) {
-  if (nsplit <= 1) return gemm(h, rows, n, k, W, A, C, ldc);
-  const float one = 1.f, zero = 0.f;
-  const int kc = k / nsplit;  // callers pass k % (8 nsplit) == 0: 16-byte aligned chunks
-  return cublasGemmStridedBatchedEx(h, CUBLAS_OP_T, CUBLAS_OP_N, n, rows, kc, &one, W, CUDA_R_16BF, k, kc, A,
-                                    CUDA_R_16BF, k, kc, &zero, C, CUDA_R_32F, ldc, (long long)rows * ldc, nsplit,
-                                    CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-}
-
 }  // namespace
+
+__attribute__((visibility("hidden"))) int qmk_internal_gemm(
+    const void *W, long long ldw, long long w_batch_stride, int n, const void *A, long long lda,
+    long long a_batch_stride, int rows, int k, int batch, int splits, float *C, long long ldc, long long c_batch_stride,
+    long long c_split_stride, unsigned *status, cudaStream_t stream);
 
 extern "C" size_t qmk_batch_workspace_bytes(int num_rows, int num_out) {
   if (num_rows < 1 || num_rows > QMK_BATCH_MAX_ROWS || num_out < 0 || num_out > num_rows) return 0;
@@ -858,21 +877,12 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
     return fail(QMK_ERR_CUDA, "qmk_batch_forward: cudaGetDevice: %s", cudaGetErrorString(e));
 
   std::lock_guard<std::mutex> lock(g_batch_mutex);
-  cublasHandle_t h = g_handles[dev];
-  if (!h) {
-    const cublasStatus_t s = cublasCreate(&h);
-    if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublasCreate: %s", cublas_name(s));
-    g_handles[dev] = h;
-  }
   if (!g_att_smem_set[dev]) {
     e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttSmemBytes);
     if (e != cudaSuccess) return fail(QMK_ERR_CUDA, "attention_kernel shared memory: %s", cudaGetErrorString(e));
     g_att_smem_set[dev] = true;
   }
   uint8_t *ws = static_cast<uint8_t *>(a->workspace);
-  cublasStatus_t s = cublasSetStream(h, stream);
-  if (s == CUBLAS_STATUS_SUCCESS) s = cublasSetWorkspace(h, ws + Lw.cublas, kCublasWorkspace);
-  if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublas setup: %s", cublas_name(s));
 
   const int R = a->num_rows, O = a->num_out, R2 = 2 * R;
   float *x = reinterpret_cast<float *>(ws + Lw.x);
@@ -885,9 +895,11 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
   auto *qs = reinterpret_cast<__nv_bfloat16 *>(ws + Lw.qs);
   float *sc = reinterpret_cast<float *>(ws + Lw.sc);
   auto *pr = reinterpret_cast<__nv_bfloat16 *>(ws + Lw.pr);
+  auto *vt = reinterpret_cast<__nv_bfloat16 *>(ws + Lw.vt);
   float *ob = reinterpret_cast<float *>(ws + Lw.ob);
   // causal run of a fresh prompt: attention as two tensor-core GEMMs per layer
   const bool gemm_attn = a->causal_run && R > kAttSplitRows && R <= kGemmAttnMaxRows;
+  const int Rp = round8(R);  // row stride of P and Vt (16-byte aligned rows for the TMA)
   auto *lm2 = reinterpret_cast<__nv_bfloat16 *>(ws + Lw.lm2);
   float *logits2 = reinterpret_cast<float *>(ws + Lw.logits2);
   auto *kc = static_cast<__nv_bfloat16 *>(a->k_cache);
@@ -897,43 +909,51 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
   auto bf = [](const void *p) { return static_cast<const __nv_bfloat16 *>(p); };
   const int splits = attention_splits(R);
   const float *resid = nullptr;  // stacked output of the last down projection
-  const int ks = split_k(R);
+  // K splits per projection (the same for O and down: n = 1024 both)
+  const int s_qkv = split_k(kQKV, R2, kHidden), s_gu = split_k(2 * kInter, R2, kHidden);
+  const int ks = split_k(kHidden, R2, kQSize);
+  const long long qkv_stride = (long long)R2 * kQKV, gu_stride = (long long)R2 * 2 * kInter;
   const long long ks_stride = (long long)R2 * kHidden;  // floats between K-split partials
-  static_assert(kQSize % (8 * kMaxSplitK) == 0 && kInter % (8 * kMaxSplitK) == 0, "K chunks must stay aligned");
+  static_assert(kQSize % (64 * kMaxSplitK) == 0 && kInter % (64 * kMaxSplitK) == 0 &&
+                    kHidden % (64 * kMaxSplitK) == 0,
+                "K chunks must stay whole 64-element blocks");
+  unsigned *st = a->status;
+  // C[rows, n] (+ nsplit partials) = A[rows, k] W[n, k]^T, row-major operands
+  auto gemm = [&](int rows, int n, int k, const void *W, const void *A, float *C, int ldc, int nsplit,
+                  long long split_stride) {
+    return qmk_internal_gemm(W, k, 0, n, A, k, 0, rows, k, 1, nsplit, C, ldc, 0, split_stride, st, stream);
+  };
+  int rc = QMK_OK;
 
   embed_kernel<<<R, 256, 0, stream>>>(bf(a->embed_weight), a->tokens, x, a->status);
-  for (int l = 0; l < a->num_layers && s == CUBLAS_STATUS_SUCCESS; ++l) {
+  for (int l = 0; l < a->num_layers && rc == QMK_OK; ++l) {
     const void *const *P = a->layer_ptrs + 11 * l;
     const void *const *F = a->fused_ptrs ? a->fused_ptrs + 2 * l : nullptr;
     residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, resid, nullptr, R, bf(P[0]), a2, ks, ks_stride);
     if (F) {
-      s = gemm(h, R2, kQKV, kHidden, F[0], a2, qkv2, kQKV);
+      rc = gemm(R2, kQKV, kHidden, F[0], a2, qkv2, kQKV, s_qkv, qkv_stride);
     } else {
-      s = gemm(h, R2, kQSize, kHidden, P[1], a2, qkv2, kQKV);
-      if (s == CUBLAS_STATUS_SUCCESS) s = gemm(h, R2, kKVSize, kHidden, P[2], a2, qkv2 + kQSize, kQKV);
-      if (s == CUBLAS_STATUS_SUCCESS) s = gemm(h, R2, kKVSize, kHidden, P[3], a2, qkv2 + kQSize + kKVSize, kQKV);
+      rc = gemm(R2, kQSize, kHidden, P[1], a2, qkv2, kQKV, s_qkv, qkv_stride);
+      if (rc == QMK_OK) rc = gemm(R2, kKVSize, kHidden, P[2], a2, qkv2 + kQSize, kQKV, s_qkv, qkv_stride);
+      if (rc == QMK_OK) rc = gemm(R2, kKVSize, kHidden, P[3], a2, qkv2 + kQSize + kKVSize, kQKV, s_qkv, qkv_stride);
     }
-    if (s != CUBLAS_STATUS_SUCCESS) break;
+    if (rc != QMK_OK) break;
     qk_rope_kv_kernel<<<R, 256, 0, stream>>>(qkv2, bf(P[4]), bf(P[5]), cos_t, sin_t, a->row_seq, a->row_pos, kc, vc,
                                             a->kv_seq_stride, a->num_seqs, l, a->max_seq_len,
-                                            a->attn_scale * kLog2e, q, a->status);
+                                            a->attn_scale * kLog2e, q, a->status, s_qkv, qkv_stride);
     if (gemm_attn) {
       // scores = qs K^T and out = P V per KV head, the cache read in place
       const long long head = (long long)a->max_seq_len * kHeadDim;  // elements between KV heads
       const __nv_bfloat16 *kl = kc + (size_t)l * kNumKVHeads * head, *vl = vc + (size_t)l * kNumKVHeads * head;
-      const float one = 1.f, zero = 0.f;
       qsplit_kernel<<<R, 256, 0, stream>>>(q, qs);
-      s = cublasGemmStridedBatchedEx(h, CUBLAS_OP_T, CUBLAS_OP_N, R, 4 * R, kHeadDim, &one, kl, CUDA_R_16BF, kHeadDim,
-                                     head, qs, CUDA_R_16BF, kHeadDim, (long long)4 * R * kHeadDim, &zero, sc,
-                                     CUDA_R_32F, R, (long long)4 * R * R, kNumKVHeads, CUBLAS_COMPUTE_32F,
-                                     CUBLAS_GEMM_DEFAULT);
-      if (s != CUBLAS_STATUS_SUCCESS) break;
-      softmax_split_kernel<<<dim3(2 * R, kNumKVHeads), 256, 0, stream>>>(sc, pr, R);
-      s = cublasGemmStridedBatchedEx(h, CUBLAS_OP_N, CUBLAS_OP_N, kHeadDim, 4 * R, R, &one, vl, CUDA_R_16BF, kHeadDim,
-                                     head, pr, CUDA_R_16BF, R, (long long)4 * R * R, &zero, ob, CUDA_R_32F, kHeadDim,
-                                     (long long)4 * R * kHeadDim, kNumKVHeads, CUBLAS_COMPUTE_32F,
-                                     CUBLAS_GEMM_DEFAULT);
-      if (s != CUBLAS_STATUS_SUCCESS) break;
+      rc = qmk_internal_gemm(kl, kHeadDim, head, R, qs, kHeadDim, (long long)4 * R * kHeadDim, 4 * R, kHeadDim,
+                             kNumKVHeads, 1, sc, R, (long long)4 * R * R, 0, st, stream);
+      if (rc != QMK_OK) break;
+      softmax_split_kernel<<<dim3(2 * R, kNumKVHeads), 256, 0, stream>>>(sc, pr, R, Rp);
+      vtrans_kernel<<<dim3((R + 63) / 64, kNumKVHeads), 256, 0, stream>>>(vl, head, R, Rp, vt);
+      rc = qmk_internal_gemm(vt, Rp, (long long)kHeadDim * Rp, kHeadDim, pr, Rp, (long long)4 * R * Rp, 4 * R, R,
+                             kNumKVHeads, 1, ob, kHeadDim, (long long)4 * R * kHeadDim, 0, st, stream);
+      if (rc != QMK_OK) break;
       att_combine_kernel<<<R, 256, 0, stream>>>(ob, a2);
     } else {
       attention_kernel<<<dim3(kNumKVHeads, R, splits), 256, kAttSmemBytes, stream>>>(
@@ -941,26 +961,26 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
           a->status);
       if (splits > 1) merge_kernel<<<dim3(kNumKVHeads, R), 64, 0, stream>>>(partial, splits, a2);
     }
-    s = gemm_splitk(h, R2, kHidden, kQSize, P[6], a2, c2, kHidden, ks);
-    if (s != CUBLAS_STATUS_SUCCESS) break;
+    rc = gemm(R2, kHidden, kQSize, P[6], a2, c2, kHidden, ks, ks_stride);
+    if (rc != QMK_OK) break;
     residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, c2, nullptr, R, bf(P[7]), a2, ks, ks_stride);  // x += O-proj
     if (F) {
-      s = gemm(h, R2, 2 * kInter, kHidden, F[1], a2, gu2, 2 * kInter);
+      rc = gemm(R2, 2 * kInter, kHidden, F[1], a2, gu2, 2 * kInter, s_gu, gu_stride);
     } else {
-      s = gemm(h, R2, kInter, kHidden, P[8], a2, gu2, 2 * kInter);
-      if (s == CUBLAS_STATUS_SUCCESS) s = gemm(h, R2, kInter, kHidden, P[9], a2, gu2 + kInter, 2 * kInter);
+      rc = gemm(R2, kInter, kHidden, P[8], a2, gu2, 2 * kInter, s_gu, gu_stride);
+      if (rc == QMK_OK) rc = gemm(R2, kInter, kHidden, P[9], a2, gu2 + kInter, 2 * kInter, s_gu, gu_stride);
     }
-    if (s != CUBLAS_STATUS_SUCCESS) break;
-    silu_split_kernel<<<R, 256, 0, stream>>>(gu2, a2);
-    s = gemm_splitk(h, R2, kHidden, kInter, P[10], a2, c2, kHidden, ks);
+    if (rc != QMK_OK) break;
+    silu_split_kernel<<<R, 256, 0, stream>>>(gu2, a2, s_gu, gu_stride);
+    rc = gemm(R2, kHidden, kInter, P[10], a2, c2, kHidden, ks, ks_stride);
     resid = c2;  // added to x by the next norm
   }
-  if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublasGemmEx: %s", cublas_name(s));
+  if (rc != QMK_OK) return rc;
   if (O > 0) {
     residual_norm_split_kernel<<<O, 256, 0, stream>>>(x, resid, a->out_rows, R, bf(a->final_norm_weight), lm2, ks,
                                                       ks_stride);
-    s = gemm(h, 2 * O, kVocab, kHidden, a->lm_head_weight, lm2, logits2, kVocab);
-    if (s != CUBLAS_STATUS_SUCCESS) return fail(QMK_ERR_CUDA, "cublasGemmEx (LM head): %s", cublas_name(s));
+    rc = gemm(2 * O, kVocab, kHidden, a->lm_head_weight, lm2, logits2, kVocab, 1, 0);
+    if (rc != QMK_OK) return rc;
     argmax_kernel<<<O, 1024, 0, stream>>>(logits2, a->logits, a->out_tokens);
   }
   e = cudaGetLastError();

@@ -208,7 +208,7 @@ __device__ __forceinline__ void ll_store_redmax(uint64_t *p, uint64_t w) {
 __device__ __forceinline__ void ll_store_exch(uint64_t *p, uint64_t w) {
   uint64_t old;
   asm volatile("atom.relaxed.gpu.global.exch.b64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(w) : "memory");
-  (void)old;
+  asm volatile("" ::"l"(old));
 }
 __device__ __forceinline__ uint64_t ll_load(const uint64_t *p) {
   uint64_t w;
