@@ -50,6 +50,9 @@ constexpr int kVocab = QMK_VOCAB;
 constexpr float kRmsEps = 1e-6f;
 constexpr float kLog2e = 1.4426950408889634f;
 
+using qmk::pdl_trigger;
+using qmk::pdl_wait;
+
 __device__ __forceinline__ float bf_lo(unsigned u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf_hi(unsigned u) { return __uint_as_float(u & 0xffff0000u); }
 
@@ -99,6 +102,8 @@ __device__ __forceinline__ float block_sum256(float v, float *red) {
 __global__ void __launch_bounds__(256) embed_kernel(const __nv_bfloat16 *__restrict__ embed,
                                                    const int *__restrict__ tokens, float *__restrict__ x,
                                                    unsigned *status) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   const int r = blockIdx.x;
   int tok = tokens[r];
   if (tok < 0 || tok >= kVocab) {
@@ -125,6 +130,8 @@ __global__ void __launch_bounds__(256) residual_norm_split_kernel(float *__restr
                                                                   const __nv_bfloat16 *__restrict__ w,
                                                                   __nv_bfloat16 *__restrict__ a2, int nsplit,
                                                                   long long split_stride) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   __shared__ float red[8];
   const int i = blockIdx.x, n_out = gridDim.x;
   int r = rows ? rows[i] : i;
@@ -171,6 +178,8 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
     __nv_bfloat16 *__restrict__ k_cache, __nv_bfloat16 *__restrict__ v_cache, long long kv_seq_stride,
     int num_seqs, int layer, int max_seq_len, float q_scale, float *__restrict__ q_out, unsigned *status,
     int nsplit, long long split_stride) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   const int r = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq = row_seq[r], pos = row_pos[r];
@@ -275,6 +284,8 @@ __global__ void __launch_bounds__(256) attention_kernel(
     const __nv_bfloat16 *__restrict__ v_cache, long long kv_seq_stride, int num_seqs, int layer, int max_seq_len,
     const int *__restrict__ row_seq, const int *__restrict__ row_pos, int splits, float *__restrict__ partial,
     __nv_bfloat16 *__restrict__ a2, unsigned *status) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t att_ring[];  // [stage][K tile | V tile]
   __shared__ __align__(16) float part[8 * kAttPartWords];
   __shared__ __align__(8) uint64_t full[kAttStages];
@@ -509,6 +520,8 @@ __global__ void __launch_bounds__(256) attention_kernel(
 // thread i: q head 2g + i / 32, dims 4 (i % 32) .. + 3.
 __global__ void __launch_bounds__(64) merge_kernel(const float *__restrict__ partial, int splits,
                                                    __nv_bfloat16 *__restrict__ a2) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   const int g = blockIdx.x, r = blockIdx.y;
   const int hh = threadIdx.x >> 5, d = 4 * (threadIdx.x & 31);
   const float *pp = partial + ((size_t)r * kNumKVHeads + g) * splits * kAttPartWords;
@@ -546,6 +559,8 @@ constexpr int kGemmAttnMaxRows = 2048;
 
 // qs[g][hh R + r] (hi) and qs[g][2R + hh R + r] (lo) <- q[r][(2g + hh) 128 + :]
 __global__ void __launch_bounds__(256) qsplit_kernel(const float *__restrict__ q, __nv_bfloat16 *__restrict__ qs) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   const int r = blockIdx.x, R = gridDim.x;
   const int c = 8 * threadIdx.x;  // 8 of the row's 2048 values
   const int h = c >> 7, d = c & 127, g = h >> 1, hh = h & 1;
@@ -568,6 +583,8 @@ __global__ void __launch_bounds__(256) qsplit_kernel(const float *__restrict__ q
 // 256 threads, up to kGemmAttnMaxRows / 256 keys per thread.
 __global__ void __launch_bounds__(256) softmax_split_kernel(const float *__restrict__ S,
                                                             __nv_bfloat16 *__restrict__ P, int R, int Rp) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   __shared__ float red[8];
   constexpr int kPer = kGemmAttnMaxRows / 256;
   const int i = blockIdx.x, g = blockIdx.y, r = i % R;
@@ -615,6 +632,8 @@ __global__ void __launch_bounds__(256) softmax_split_kernel(const float *__restr
 // att[r][(2g + hh) 128 + d] = O[g][hh R + r][d] + O[g][2R + hh R + r][d] -> the
 // stacked O-projection input.  Grid: rows, 256 threads, 8 values each.
 __global__ void __launch_bounds__(256) att_combine_kernel(const float *__restrict__ Ob, __nv_bfloat16 *__restrict__ a2) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   const int r = blockIdx.x, R = gridDim.x;
   const int c = 8 * threadIdx.x;
   const int h = c >> 7, d = c & 127, g = h >> 1, hh = h & 1;
@@ -634,6 +653,8 @@ __global__ void __launch_bounds__(256) att_combine_kernel(const float *__restric
 // memory.  Vt rows at a stride of Rp elements.
 __global__ void __launch_bounds__(256) vtrans_kernel(const __nv_bfloat16 *__restrict__ v_layer, long long head_stride,
                                                      int R, int Rp, __nv_bfloat16 *__restrict__ vt) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   __shared__ __nv_bfloat16 t[64][kHeadDim + 2];
   const int p0 = blockIdx.x * 64, g = blockIdx.y;
   const __nv_bfloat16 *src = v_layer + (size_t)g * (size_t)head_stride;
@@ -655,6 +676,8 @@ __global__ void __launch_bounds__(256) vtrans_kernel(const __nv_bfloat16 *__rest
 __global__ void __launch_bounds__(256) silu_split_kernel(const float *__restrict__ gu2,
                                                          __nv_bfloat16 *__restrict__ a2, int nsplit,
                                                          long long split_stride) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   const int r = blockIdx.x, R = gridDim.x;
   for (int c = threadIdx.x; c < kInter / 4; c += 256) {
     float gg[4] = {0.f, 0.f, 0.f, 0.f}, uu[4] = {0.f, 0.f, 0.f, 0.f};
@@ -682,6 +705,8 @@ __global__ void __launch_bounds__(256) silu_split_kernel(const float *__restrict
 // largest value, lowest index on ties.  1024 threads.
 __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ logits2, float *__restrict__ logits,
                                                       int *__restrict__ out) {
+  pdl_wait();  // inputs are written by the previous kernel
+  pdl_trigger();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int i = blockIdx.x, O = gridDim.x;
@@ -822,6 +847,27 @@ int attention_splits(int R) {
   return s < 1 ? 1 : (s > kAttMaxSplits ? kAttMaxSplits : s);
 }
 
+// Every kernel of the forward pass is launched with programmatic stream
+// serialization: it may be scheduled while its predecessor still runs and
+// waits (pdl_wait) before touching the predecessor's data, so launch latency
+// and prologues overlap the previous kernel; the GEMM prefetches its weight
+// tiles before that wait.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 constexpr int kMaxDevices = 64;
 bool g_att_smem_set[kMaxDevices] = {};  // attention_kernel's dynamic shared memory limit raised
 std::mutex g_batch_mutex;
@@ -831,7 +877,7 @@ std::mutex g_batch_mutex;
 __attribute__((visibility("hidden"))) int qmk_internal_gemm(
     const void *W, long long ldw, long long w_batch_stride, int n, const void *A, long long lda,
     long long a_batch_stride, int rows, int k, int batch, int splits, float *C, long long ldc, long long c_batch_stride,
-    long long c_split_stride, unsigned *status, cudaStream_t stream);
+    long long c_split_stride, unsigned *status, cudaStream_t stream, int causal, int causal_R, int w_static);
 
 extern "C" size_t qmk_batch_workspace_bytes(int num_rows, int num_out) {
   if (num_rows < 1 || num_rows > QMK_BATCH_MAX_ROWS || num_out < 0 || num_out > num_rows) return 0;
@@ -921,15 +967,16 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
   // C[rows, n] (+ nsplit partials) = A[rows, k] W[n, k]^T, row-major operands
   auto gemm = [&](int rows, int n, int k, const void *W, const void *A, float *C, int ldc, int nsplit,
                   long long split_stride) {
-    return qmk_internal_gemm(W, k, 0, n, A, k, 0, rows, k, 1, nsplit, C, ldc, 0, split_stride, st, stream);
+    // model weights: independent of the previous kernel (prefetched early)
+    return qmk_internal_gemm(W, k, 0, n, A, k, 0, rows, k, 1, nsplit, C, ldc, 0, split_stride, st, stream, 0, 0, 1);
   };
   int rc = QMK_OK;
 
-  embed_kernel<<<R, 256, 0, stream>>>(bf(a->embed_weight), a->tokens, x, a->status);
+  launch_pdl(embed_kernel, dim3(R), dim3(256), 0, stream, bf(a->embed_weight), a->tokens, x, a->status);
   for (int l = 0; l < a->num_layers && rc == QMK_OK; ++l) {
     const void *const *P = a->layer_ptrs + 11 * l;
     const void *const *F = a->fused_ptrs ? a->fused_ptrs + 2 * l : nullptr;
-    residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, resid, nullptr, R, bf(P[0]), a2, ks, ks_stride);
+    launch_pdl(residual_norm_split_kernel, dim3(R), dim3(256), 0, stream, x, resid, nullptr, R, bf(P[0]), a2, ks, ks_stride);
     if (F) {
       rc = gemm(R2, kQKV, kHidden, F[0], a2, qkv2, kQKV, s_qkv, qkv_stride);
     } else {
@@ -938,32 +985,35 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
       if (rc == QMK_OK) rc = gemm(R2, kKVSize, kHidden, P[3], a2, qkv2 + kQSize + kKVSize, kQKV, s_qkv, qkv_stride);
     }
     if (rc != QMK_OK) break;
-    qk_rope_kv_kernel<<<R, 256, 0, stream>>>(qkv2, bf(P[4]), bf(P[5]), cos_t, sin_t, a->row_seq, a->row_pos, kc, vc,
+    launch_pdl(qk_rope_kv_kernel, dim3(R), dim3(256), 0, stream, qkv2, bf(P[4]), bf(P[5]), cos_t, sin_t, a->row_seq, a->row_pos, kc, vc,
                                             a->kv_seq_stride, a->num_seqs, l, a->max_seq_len,
                                             a->attn_scale * kLog2e, q, a->status, s_qkv, qkv_stride);
     if (gemm_attn) {
       // scores = qs K^T and out = P V per KV head, the cache read in place
       const long long head = (long long)a->max_seq_len * kHeadDim;  // elements between KV heads
       const __nv_bfloat16 *kl = kc + (size_t)l * kNumKVHeads * head, *vl = vc + (size_t)l * kNumKVHeads * head;
-      qsplit_kernel<<<R, 256, 0, stream>>>(q, qs);
+      launch_pdl(qsplit_kernel, dim3(R), dim3(256), 0, stream, q, qs);
+      // (causal: key tiles after every query of a tile are skipped; the
+      // softmax reads only keys j <= r)
       rc = qmk_internal_gemm(kl, kHeadDim, head, R, qs, kHeadDim, (long long)4 * R * kHeadDim, 4 * R, kHeadDim,
-                             kNumKVHeads, 1, sc, R, (long long)4 * R * R, 0, st, stream);
+                             kNumKVHeads, 1, sc, R, (long long)4 * R * R, 0, st, stream, 1, R, 0);
       if (rc != QMK_OK) break;
-      softmax_split_kernel<<<dim3(2 * R, kNumKVHeads), 256, 0, stream>>>(sc, pr, R, Rp);
-      vtrans_kernel<<<dim3((R + 63) / 64, kNumKVHeads), 256, 0, stream>>>(vl, head, R, Rp, vt);
+      launch_pdl(softmax_split_kernel, dim3(dim3(2 * R, kNumKVHeads)), dim3(256), 0, stream, sc, pr, R, Rp);
+      launch_pdl(vtrans_kernel, dim3(dim3((R + 63) / 64, kNumKVHeads)), dim3(256), 0, stream, vl, head, R, Rp, vt);
+      // (causal: a query tile's K range ends at its last position; P is 0 beyond)
       rc = qmk_internal_gemm(vt, Rp, (long long)kHeadDim * Rp, kHeadDim, pr, Rp, (long long)4 * R * Rp, 4 * R, R,
-                             kNumKVHeads, 1, ob, kHeadDim, (long long)4 * R * kHeadDim, 0, st, stream);
+                             kNumKVHeads, 1, ob, kHeadDim, (long long)4 * R * kHeadDim, 0, st, stream, 2, R, 0);
       if (rc != QMK_OK) break;
-      att_combine_kernel<<<R, 256, 0, stream>>>(ob, a2);
+      launch_pdl(att_combine_kernel, dim3(R), dim3(256), 0, stream, ob, a2);
     } else {
-      attention_kernel<<<dim3(kNumKVHeads, R, splits), 256, kAttSmemBytes, stream>>>(
+      launch_pdl(attention_kernel, dim3(dim3(kNumKVHeads, R, splits)), dim3(256), kAttSmemBytes, stream, 
           q, kc, vc, a->kv_seq_stride, a->num_seqs, l, a->max_seq_len, a->row_seq, a->row_pos, splits, partial, a2,
           a->status);
-      if (splits > 1) merge_kernel<<<dim3(kNumKVHeads, R), 64, 0, stream>>>(partial, splits, a2);
+      if (splits > 1) launch_pdl(merge_kernel, dim3(dim3(kNumKVHeads, R)), dim3(64), 0, stream, partial, splits, a2);
     }
     rc = gemm(R2, kHidden, kQSize, P[6], a2, c2, kHidden, ks, ks_stride);
     if (rc != QMK_OK) break;
-    residual_norm_split_kernel<<<R, 256, 0, stream>>>(x, c2, nullptr, R, bf(P[7]), a2, ks, ks_stride);  // x += O-proj
+    launch_pdl(residual_norm_split_kernel, dim3(R), dim3(256), 0, stream, x, c2, nullptr, R, bf(P[7]), a2, ks, ks_stride);  // x += O-proj
     if (F) {
       rc = gemm(R2, 2 * kInter, kHidden, F[1], a2, gu2, 2 * kInter, s_gu, gu_stride);
     } else {
@@ -971,17 +1021,17 @@ extern "C" int qmk_batch_forward(const QmkBatchArgs *a, cudaStream_t stream) {
       if (rc == QMK_OK) rc = gemm(R2, kInter, kHidden, P[9], a2, gu2 + kInter, 2 * kInter, s_gu, gu_stride);
     }
     if (rc != QMK_OK) break;
-    silu_split_kernel<<<R, 256, 0, stream>>>(gu2, a2, s_gu, gu_stride);
+    launch_pdl(silu_split_kernel, dim3(R), dim3(256), 0, stream, gu2, a2, s_gu, gu_stride);
     rc = gemm(R2, kHidden, kInter, P[10], a2, c2, kHidden, ks, ks_stride);
     resid = c2;  // added to x by the next norm
   }
   if (rc != QMK_OK) return rc;
   if (O > 0) {
-    residual_norm_split_kernel<<<O, 256, 0, stream>>>(x, resid, a->out_rows, R, bf(a->final_norm_weight), lm2, ks,
+    launch_pdl(residual_norm_split_kernel, dim3(O), dim3(256), 0, stream, x, resid, a->out_rows, R, bf(a->final_norm_weight), lm2, ks,
                                                       ks_stride);
     rc = gemm(2 * O, kVocab, kHidden, a->lm_head_weight, lm2, logits2, kVocab, 1, 0);
     if (rc != QMK_OK) return rc;
-    argmax_kernel<<<O, 1024, 0, stream>>>(logits2, a->logits, a->out_tokens);
+    launch_pdl(argmax_kernel, dim3(O), dim3(1024), 0, stream, logits2, a->logits, a->out_tokens);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(QMK_ERR_CUDA, "qmk_batch_forward launch: %s", cudaGetErrorString(e));

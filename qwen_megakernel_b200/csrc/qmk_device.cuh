@@ -248,6 +248,15 @@ __device__ __forceinline__ void named_sync() {
 // Named barrier 2 over the first four warps (the TMEM readers).
 __device__ __forceinline__ void reader_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
+// ------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// its predecessor in the stream still runs: pdl_wait() blocks until every
+// prerequisite grid has completed and its memory is visible (call it before
+// touching anything a predecessor writes or reads); pdl_trigger() lets the
+// next such kernel be scheduled (its CTAs then run their own prologue).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------ math
 __device__ __forceinline__ float bf_lo(unsigned u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf_hi(unsigned u) { return __uint_as_float(u & 0xffff0000u); }
