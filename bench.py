@@ -714,6 +714,72 @@ def run_prefill(args) -> int:
     return 0
 
 
+def run_profile_prefill() -> int:
+    """Small case for ncu launch lists of the token-parallel prefill: one
+    warm 1024-token prefill, then ONE more between cudaProfilerStart/Stop
+    (capture with ncu --profile-from-start off)."""
+    torch.cuda.set_device(0)
+    from qwen_megakernel_b200 import Decoder
+    from qwen_megakernel_b200.weights import random_weights
+
+    weights = random_weights(seed=0, device="cuda", max_seq_len=2048)
+    dec = Decoder(weights, max_seq_len=2048)
+    prompt = prompt_for_rank(0)
+    dec.prefill_batched(prompt)
+    dec.reset()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    tok = dec.prefill_batched(prompt)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print(json.dumps({"profile_prefill": {"tokens": PROMPT_LEN, "next_token": tok}}))
+    return 0
+
+
+def run_profile_gemm(n: int, rows: int, k: int, reps: int = 8) -> int:
+    """The token-parallel path's tensor-core GEMM alone (qmk_gemm_bf16_nt,
+    C[rows, n] = A[rows, k] W[n, k]^T, bf16 in, fp32 out) on random operands:
+    `reps` launches timed with CUDA events, checked against torch fp32.  For
+    ncu: -k regex:gemm_kernel -s 2 -c 1."""
+    import ctypes
+
+    torch.cuda.set_device(0)
+    from qwen_megakernel_b200 import cdll
+
+    lib = cdll()
+    vp, i, ll = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+    lib.qmk_gemm_bf16_nt.restype = i
+    lib.qmk_gemm_bf16_nt.argtypes = [vp, ll, ll, i, vp, ll, ll, i, i, i, i, vp, ll, ll, ll, vp, vp]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    W = torch.randn(n, k, generator=g, device="cuda").to(torch.bfloat16)
+    A = torch.randn(rows, k, generator=g, device="cuda").to(torch.bfloat16)
+    C = torch.empty(rows, n, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def run():
+        rc = lib.qmk_gemm_bf16_nt(W.data_ptr(), k, 0, n, A.data_ptr(), k, 0, rows, k, 1, 1, C.data_ptr(), n, 0, 0,
+                                  None, stream)
+        if rc != 0:
+            raise RuntimeError(lib.qmk_get_last_error_message())
+
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / reps * 1000.0
+    err = (C - A.float() @ W.float().T).abs().max().item()
+    print(json.dumps({"profile_gemm": {"n": n, "rows": rows, "k": k, "us": round(us, 2),
+                                       "tflops": round(2 * n * rows * k / (us * 1e-6) / 1e12, 1),
+                                       "bytes_gbs": round((n * k + rows * k) * 2 / (us * 1e-6) / 1e9, 1),
+                                       "max_err": err}}))
+    return 0
+
+
 def measure_extras(args, rank: int, ws: int, distributed: bool) -> dict:
     """The secondary BASELINE configs as extra keys of the headline line.
     One GPU: configs[2] (ctx 8192 and 32768, 64 steps), configs[3] (B = 4,
@@ -761,7 +827,15 @@ def main(argv=None) -> int:
                     help="run only the small ncu case of the token-parallel path: one batched step of B rows")
     ap.add_argument("--trace", type=int, default=0, metavar="STEPS",
                     help="print the per-phase critical path of one traced step of a STEPS-token launch")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="run only the small ncu case of the token-parallel prefill")
+    ap.add_argument("--profile-gemm", type=int, nargs=3, default=None, metavar=("N", "ROWS", "K"),
+                    help="run only the tensor-core GEMM C[ROWS, N] = A[ROWS, K] W[N, K]^T")
     args = ap.parse_args(argv)
+    if args.profile_prefill:
+        return run_profile_prefill()
+    if args.profile_gemm:
+        return run_profile_gemm(*args.profile_gemm)
     if args.trace:
         return run_trace(args.trace)
     if args.profile_batch:
