@@ -801,6 +801,7 @@ def measure_extras(args, rank: int, ws: int, distributed: bool) -> dict:
                           clock_gpu=torch.cuda.current_device())
         total = 16 * 64 * ws
         r["value"] = round(total / (r["ms_per_step"] * 64 / 1000.0), 1)
+        r["e2e"]["value"] = round(r["e2e"]["value"] * ws, 1)  # per-rank rate over the slowest rank's time
         r["metric"] = "batched decode tok/s, batch-16 replicas (whole job)"
         r["n_gpus"] = ws
         extras["batch16_replicas"] = r
