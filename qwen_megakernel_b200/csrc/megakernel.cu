@@ -307,20 +307,21 @@ struct Waiter {
 };
 
 // ------------------------------------------------------------- ring (consumer)
+// No abort pre-check here or in the other waits: a strong shared-memory
+// access costs 80-170 SM cycles inside this kernel (measured), and the wait
+// loops see an abort at their next checkpoint anyway.
 __device__ __forceinline__ bool wait_full(Ctx &c, uint32_t tile) {
-  bool ok = (*c.abort_flag == 0);
+  bool ok = true;
   const uint32_t k = tile - c.trace_tile0;
   const bool stamp = c.trace && threadIdx.x == 0 && k < (uint32_t)kTraceTiles;
   if (stamp) c.trace[kTraceTileBase + 2 * k] = trace_now(c);
-  if (ok) {
-    const int slot = tile % kNumSlots;
-    const unsigned par = (tile / kNumSlots) & 1u;
-    Waiter w;
-    while (!mbar_try_wait(&c.full[slot], par)) {
-      if (!w.keep_going(c, kSiteFull)) {
-        ok = false;
-        break;
-      }
+  const int slot = tile % kNumSlots;
+  const unsigned par = (tile / kNumSlots) & 1u;
+  Waiter w;
+  while (!mbar_try_wait(&c.full[slot], par)) {
+    if (!w.keep_going(c, kSiteFull)) {
+      ok = false;
+      break;
     }
   }
   if (stamp) c.trace[kTraceTileBase + 2 * k + 1] = trace_now(c);
@@ -484,7 +485,6 @@ __device__ __forceinline__ float stage_vec(Ctx &c, float *dst, uint8_t *bop, con
 #pragma unroll
   for (int k = 0; k < P; ++k)
     if (k * kConsumerThreads + tid < kPairs) pending |= 1u << k;
-  if (*c.abort_flag) pending = 0;
   float keep[kSum ? P : 1][2];
 #pragma unroll
   for (int k = 0; k < (kSum ? P : 1); ++k) keep[k][0] = keep[k][1] = 0.f;
@@ -586,6 +586,27 @@ __device__ __forceinline__ void build_norm_xw(float *xw, const float *x, const N
   }
 }
 
+// Warp sums of four per-lane values v[0..3] (rows of a batch): lane l
+// returns the sum over all lanes of v[2 ((l >> 4) & 1) + ((l >> 3) & 1)].
+// Each level adds the same pairs in the same order on every run.
+__device__ __forceinline__ float reduce4_transpose(const float (&v)[4]) {
+  const int lane = threadIdx.x & 31;
+  const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
+  float w[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float send = hi16 ? v[j] : v[j + 2];
+    const float keep = hi16 ? v[j + 2] : v[j];
+    w[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  const float send = hi8 ? w[0] : w[1];
+  float u = (hi8 ? w[1] : w[0]) + __shfl_xor_sync(0xffffffffu, send, 8);
+  u += __shfl_xor_sync(0xffffffffu, u, 4);
+  u += __shfl_xor_sync(0xffffffffu, u, 2);
+  u += __shfl_xor_sync(0xffffffffu, u, 1);
+  return u;
+}
+
 // s0/s1 += 4 bf16 weights (w, two pairs) times 4 fp32 inputs (x), even and
 // odd elements in separate chains.
 __device__ __forceinline__ void dot4(float &s0, float &s1, const uint2 w, const float4 x) {
@@ -605,7 +626,6 @@ __device__ void stage_list(Ctx &c, float *dst, int n, AddrFn addr, unsigned flag
 #pragma unroll
   for (int k = 0; k < K; ++k)
     if (k * kConsumerThreads + tid < n) pending |= 1u << k;
-  if (*c.abort_flag) pending = 0;
   uint64_t v0[K];
   auto issue = [&](uint64_t (&v)[K]) {
 #pragma unroll
@@ -1117,13 +1137,39 @@ struct Consumer {
   // its tiles first and then gives every warp all of its work at once: the
   // loads of several rows are in flight together, which a single warp needs
   // to hide shared-memory latency.  The tiles are released at the end.
+  // Wait for the phase's tiles (ntiles <= kNumSlots).  The first pass tests
+  // every tile's barrier with independent try_waits, which overlap (a
+  // try_wait on a completed phase still costs ~120 cycles here); only tiles
+  // not landed yet take the bounded wait loop.
   __device__ __forceinline__ bool wait_tiles(int ntiles) {
+    unsigned miss = 0;
+    bool hit[kNumSlots];
+#pragma unroll
+    for (int t = 0; t < kNumSlots; ++t) {
+      const uint32_t tt = tile + (uint32_t)t;
+      hit[t] = (t < ntiles) ? mbar_try_wait(&c.full[tt % kNumSlots], (tt / kNumSlots) & 1u) : true;
+    }
+#pragma unroll
+    for (int t = 0; t < kNumSlots; ++t) miss |= hit[t] ? 0u : (1u << t);
     bool ok = true;
-    for (int t = 0; t < ntiles; ++t) ok = wait_full(c, tile + (uint32_t)t) && ok;
+    if (__any_sync(0xffffffffu, miss != 0u) || c.trace) {
+      for (int t = 0; t < ntiles; ++t) ok = wait_full(c, tile + (uint32_t)t) && ok;
+    }
     return ok;
   }
+  // Release the phase's tiles: one arrive per tile from lane 0 once the warp
+  // has finished reading them.
   __device__ __forceinline__ void release_tiles(int ntiles, bool ok) {
-    for (int t = 0; t < ntiles; ++t) release_tile(c, tile + (uint32_t)t, ok);
+    if (c.trace && tid == 0) {
+      for (int t = 0; t < ntiles; ++t) {
+        const uint32_t k = tile + (uint32_t)t - c.trace_tile0;
+        if (k < (uint32_t)kTraceTiles) c.trace[kTraceTileBase + 3 * kTraceTiles + k] = trace_now(c);
+      }
+    }
+    __syncwarp();
+    if (ok && lane == 0) {
+      for (int t = 0; t < ntiles; ++t) mbar_arrive(&c.empty[(tile + (uint32_t)t) % kNumSlots]);
+    }
     tile += (uint32_t)ntiles;
   }
   // Address of byte `off` of row i of the phase (tiles of tile_rows rows at
@@ -1141,6 +1187,7 @@ struct Consumer {
   __device__ void fma_rows_phase(const float *x, int r0, int r1, int tile_rows, int pitch, float scale,
                                  unsigned E) {
     constexpr bool kGU = (OUT == kOutGU);
+    static_assert(MR >= 1 && MR <= 4, "rows per warp batch");
     const TcJob job{kTcRow, OUT, r0, r1, tile_rows, scale, E};
     const int n = r1 - r0;
     const int ntiles = (n + tile_rows - 1) / tile_rows;
@@ -1185,26 +1232,23 @@ struct Consumer {
           }
         }
       }
-      float v[MR], v2[MR];
+      float v[4], v2[4];
 #pragma unroll
-      for (int r = 0; r < MR; ++r) {
-        v[r] = (s[r][0] + s[r][1]) + (s[r][2] + s[r][3]);
-        v2[r] = kGU ? (s[r][kGU ? 4 : 0] + s[r][kGU ? 5 : 1]) + (s[r][kGU ? 6 : 2] + s[r][kGU ? 7 : 3]) : 0.f;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int r = 0; r < MR; ++r) {
-          v[r] += __shfl_xor_sync(0xffffffffu, v[r], o);
-          if (kGU) v2[r] += __shfl_xor_sync(0xffffffffu, v2[r], o);
-        }
-      if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < MR; ++r) {
-          const int i = i0 + kConsumerWarps * r;
-          if (i < n) tc_emit(job, r0 + i, v[r], v2[r]);
+      for (int r = 0; r < 4; ++r) {
+        v[r] = v2[r] = 0.f;
+        if (r < MR) {
+          v[r] = (s[r][0] + s[r][1]) + (s[r][2] + s[r][3]);
+          v2[r] = kGU ? (s[r][kGU ? 4 : 0] + s[r][kGU ? 5 : 1]) + (s[r][kGU ? 6 : 2] + s[r][kGU ? 7 : 3]) : 0.f;
         }
       }
+      // Transposing butterfly: after it lane l holds the warp sum of row
+      // 2 ((l >> 4) & 1) + ((l >> 3) & 1) of the batch (6 shuffles per value
+      // instead of 5 per row), and lanes 0, 8, 16, 24 emit in parallel.
+      const int rr = 2 * ((lane >> 4) & 1) + ((lane >> 3) & 1);
+      const float sum = reduce4_transpose(v);
+      const float sum2 = kGU ? reduce4_transpose(v2) : 0.f;
+      const int i = i0 + kConsumerWarps * rr;
+      if ((lane & 7) == 0 && rr < MR && i < n) tc_emit(job, r0 + i, sum, sum2);
     }
     release_tiles(ntiles, ok);
   }
@@ -1221,6 +1265,7 @@ struct Consumer {
     constexpr int kBlocks = 8 * KC;  // 128-element blocks per row
     constexpr int kMine = (kBlocks + kConsumerWarps - 1) / kConsumerWarps;
     constexpr int RB = kKsplitRows;
+    static_assert(RB == 4, "the transposing reduction handles 4 rows");
     const TcJob job{kTcRow, OUT, r0, r1, tile_rows, 1.f, E};
     const int n = r1 - r0;
     const int ntiles = (n + tile_rows - 1) / tile_rows;
@@ -1259,17 +1304,11 @@ struct Consumer {
           }
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int r = 0; r < RB; ++r) v[r] += __shfl_xor_sync(0xffffffffu, v[r], o);
+      const float wsum = reduce4_transpose(v);
       float *part = sPart + (kpart_seq++ & 1) * (kConsumerWarps * RB);
-      if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < RB; ++r) part[warp * RB + r] = v[r];
-      }
+      if ((lane & 7) == 0) part[warp * RB + 2 * ((lane >> 4) & 1) + ((lane >> 3) & 1)] = wsum;
       consumer_sync();
-      if (tid < min(RB, n - i0) && ok && live()) {
+      if (tid < min(RB, n - i0) && ok) {
         float sum = 0.f;
 #pragma unroll
         for (int q = 0; q < kConsumerWarps; ++q) sum += part[q * RB + tid];
@@ -1402,10 +1441,8 @@ struct Consumer {
         const uint2 vw = make_uint2(vbits[0] | (vbits[1] << 16), vbits[2] | (vbits[3] << 16));
         reinterpret_cast<uint2 *>(sU + kUKn)[lane] = kw;
         reinterpret_cast<uint2 *>(sU + kUVn)[lane] = vw;
-        if (live()) {
-          *reinterpret_cast<uint2 *>(p.k_cache + off) = kw;
-          *reinterpret_cast<uint2 *>(p.v_cache + off) = vw;
-        }
+        *reinterpret_cast<uint2 *>(p.k_cache + off) = kw;
+        *reinterpret_cast<uint2 *>(p.v_cache + off) = vw;
       }
     }
     consumer_sync();
@@ -1595,7 +1632,7 @@ struct Consumer {
           }
         }
       }
-      if (live()) {
+      {
         uint64_t *part = c.wPart + (size_t)item * kPartWords;
         put(part + 4 + hh * kHeadDim + d, ll_pack(O0, E));
         put(part + 4 + hh * kHeadDim + d + 1, ll_pack(O1, E));
@@ -1638,7 +1675,7 @@ struct Consumer {
           O += sU[s * kMergeWordsPerSplit + 2 + tid] * f;
         }
       }
-      if (live()) put(c.wAtt + h * kHeadDim + half * kMergeDims + tid, ll_pack(O * fast_rcp(L), E));
+      put(c.wAtt + h * kHeadDim + half * kMergeDims + tid, ll_pack(O * fast_rcp(L), E));
     }
     consumer_sync();
     flush();
@@ -1842,10 +1879,8 @@ struct Consumer {
         }
       }
       if (bi == 0x7fffffff) bi = R.begin;  // CTA without rows (not on B200)
-      if (live()) {
-        put(c.wArg + 2 * c.cta, ll_pack_u(bk, E));
-        put(c.wArg + 2 * c.cta + 1, ll_pack_u((unsigned)bi, E));
-      }
+      put(c.wArg + 2 * c.cta, ll_pack_u(bk, E));
+      put(c.wArg + 2 * c.cta + 1, ll_pack_u((unsigned)bi, E));
     }
     flush();
     consumer_sync();
