@@ -1142,6 +1142,9 @@ struct Consumer {
   // try_wait on a completed phase still costs ~120 cycles here); only tiles
   // not landed yet take the bounded wait loop.
   __device__ __forceinline__ bool wait_tiles(int ntiles) {
+    const bool stamp = c.trace && tid == 0 && tile - c.trace_tile0 + (uint32_t)ntiles <= (uint32_t)kTraceTiles;
+    uint64_t t0 = 0;
+    if (stamp) t0 = trace_now(c);
     unsigned miss = 0;
     bool hit[kNumSlots];
 #pragma unroll
@@ -1152,11 +1155,24 @@ struct Consumer {
 #pragma unroll
     for (int t = 0; t < kNumSlots; ++t) miss |= hit[t] ? 0u : (1u << t);
     bool ok = true;
-    if (__any_sync(0xffffffffu, miss != 0u) || c.trace) {
+    if (__any_sync(0xffffffffu, miss != 0u)) {
       for (int t = 0; t < ntiles; ++t) ok = wait_full(c, tile + (uint32_t)t) && ok;
+    } else if (stamp) {
+      // same stamps as wait_full: wait entry and tile landed, per tile
+      const uint64_t t1 = trace_now(c);
+      for (int t = 0; t < ntiles; ++t) {
+        const uint32_t k = tile + (uint32_t)t - c.trace_tile0;
+        c.trace[kTraceTileBase + 2 * k] = t0;
+        c.trace[kTraceTileBase + 2 * k + 1] = t1;
+      }
     }
     return ok;
   }
+  // Tiles of a phase over rows [R.begin, R.end) at tile_rows rows per tile.
+  static __device__ __forceinline__ int tiles_of(const Range &R, int tile_rows) {
+    return (R.end - R.begin + tile_rows - 1) / tile_rows;
+  }
+
   // Release the phase's tiles: one arrive per tile from lane 0 once the warp
   // has finished reading them.
   __device__ __forceinline__ void release_tiles(int ntiles, bool ok) {
@@ -1184,7 +1200,7 @@ struct Consumer {
   // gate row and, 2048 bytes further, an up row per output row.  No barrier
   // between the warps.
   template <int OUT, int MR>
-  __device__ void fma_rows_phase(const float *x, int r0, int r1, int tile_rows, int pitch, float scale,
+  __device__ void fma_rows_phase(bool ok, const float *x, int r0, int r1, int tile_rows, int pitch, float scale,
                                  unsigned E) {
     constexpr bool kGU = (OUT == kOutGU);
     static_assert(MR >= 1 && MR <= 4, "rows per warp batch");
@@ -1194,7 +1210,6 @@ struct Consumer {
     float4 xv[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) xv[j] = reinterpret_cast<const float4 *>(x)[lane + 32 * j];
-    const bool ok = wait_tiles(ntiles);
     for (int i0 = warp; ok && i0 < n; i0 += kConsumerWarps * MR) {
       // rows i0 + 7r of this batch; rows past the end repeat row i0 (no
       // branch inside the loop, so the rows' FMA chains interleave)
@@ -1261,7 +1276,7 @@ struct Consumer {
   // kKsplitRows rows; thread r then adds row r's partials in warp order
   // (deterministic) and emits it.
   template <int KC, int OUT>
-  __device__ void fma_ksplit_phase(const float *x, int r0, int r1, int tile_rows, int pitch, unsigned E) {
+  __device__ void fma_ksplit_phase(bool ok, const float *x, int r0, int r1, int tile_rows, int pitch, unsigned E) {
     constexpr int kBlocks = 8 * KC;  // 128-element blocks per row
     constexpr int kMine = (kBlocks + kConsumerWarps - 1) / kConsumerWarps;
     constexpr int RB = kKsplitRows;
@@ -1275,7 +1290,6 @@ struct Consumer {
       const int b = warp + kConsumerWarps * q;
       xv[q] = (b < kBlocks) ? reinterpret_cast<const float4 *>(x)[lane + 32 * b] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const bool ok = wait_tiles(ntiles);
     for (int i0 = 0; i0 < n; i0 += RB) {  // every warp runs every batch (barrier inside)
       float v[RB];
 #pragma unroll
@@ -1354,6 +1368,10 @@ struct Consumer {
   __device__ void phase_qkv(const LDGLayerWeights &w, unsigned E, int l, unsigned x_flag, float x_ss) {
     const NormPairs nw = nw_pref;  // fetched one phase ahead
     const Range R = qkv_rows(c.cta, c.ncta);
+    // The weight tiles have normally landed long before the input: their
+    // barrier tests (strong shared-memory operations, ~120+ cycles each)
+    // run before the dataflow wait instead of after it, likewise below.
+    const bool tiles = wait_tiles(tiles_of(R, kQKVTileRows));
     if (x_flag) {
       x_ss = stage_vec<kHidden, kStageNorm>(c, sX, reinterpret_cast<uint8_t *>(sXW), c.wX, x_flag, kSiteX, red_x, nw);
     } else {
@@ -1361,7 +1379,7 @@ struct Consumer {
       consumer_sync();
     }
     trace_stamp(c, tid == 0, l * 16 + 0);
-    fma_rows_phase<kOutQKV, 4>(sXW, R.begin, R.end, kQKVTileRows, 2048, rsqrtf(x_ss / (float)kHidden + kRmsEps), E);
+    fma_rows_phase<kOutQKV, 4>(tiles, sXW, R.begin, R.end, kQKVTileRows, 2048, rsqrtf(x_ss / (float)kHidden + kRmsEps), E);
     flush();
     trace_stamp(c, tid == 0, l * 16 + 1);
   }
@@ -1687,10 +1705,11 @@ struct Consumer {
     // RMSNorm weights of P4, fetched now so that their latency is hidden.
     nw_pref = load_norm_pairs((const __nv_bfloat16 *)w.post_attn_layernorm_weight, tid);
     const Range R = o_rows(c.cta, c.ncta);
+    const bool tiles = wait_tiles(tiles_of(R, kOTileRows));
     // Test hook: 0xFFFFFFFF is never an epoch, so this wait can only expire.
     stage_vec<kQSize, kStageCopy>(c, sAtt, nullptr, c.wAtt, stall ? 0xFFFFFFFFu : E, kSiteAtt, nullptr, NormPairs{});
     trace_stamp(c, tid == 0, l * 16 + 6);
-    fma_ksplit_phase<2, kOutO>(sAtt, R.begin, R.end, kOTileRows, kQSize * 2, E);
+    fma_ksplit_phase<2, kOutO>(tiles, sAtt, R.begin, R.end, kOTileRows, kQSize * 2, E);
     flush();
     trace_stamp(c, tid == 0, l * 16 + 7);
   }
@@ -1699,9 +1718,10 @@ struct Consumer {
   __device__ void phase_gate_up(const LDGLayerWeights &w, unsigned E, int l) {
     const NormPairs nw = nw_pref;  // fetched in P3
     const Range R = gu_rows(c.cta, c.ncta);
+    const bool tiles = wait_tiles(tiles_of(R, kGUTileRows));
     const float ss = stage_vec<kHidden, kStageNorm>(c, sA, reinterpret_cast<uint8_t *>(sXW), c.wA, E, kSiteA, red_a, nw);
     trace_stamp(c, tid == 0, l * 16 + 8);
-    fma_rows_phase<kOutGU, 3>(sXW, R.begin, R.end, kGUTileRows, 4096, rsqrtf(ss / (float)kHidden + kRmsEps), E);
+    fma_rows_phase<kOutGU, 3>(tiles, sXW, R.begin, R.end, kGUTileRows, 4096, rsqrtf(ss / (float)kHidden + kRmsEps), E);
     flush();
     trace_stamp(c, tid == 0, l * 16 + 9);
   }
@@ -1712,9 +1732,10 @@ struct Consumer {
     nw_pref = load_norm_pairs(
         (l + 1 < p.num_layers) ? (const __nv_bfloat16 *)p.layers[l + 1].input_layernorm_weight : p.final_norm, tid);
     const Range R = d_rows(c.cta, c.ncta);
+    const bool tiles = wait_tiles(tiles_of(R, kDTileRows));
     stage_vec<kInter, kStageCopy>(c, sU, nullptr, c.wM, E, kSiteM, nullptr, NormPairs{});
     trace_stamp(c, tid == 0, l * 16 + 10);
-    fma_ksplit_phase<3, kOutDown>(sU, R.begin, R.end, kDTileRows, kDRowPitch, E);
+    fma_ksplit_phase<3, kOutDown>(tiles, sU, R.begin, R.end, kDTileRows, kDRowPitch, E);
     flush();
     trace_stamp(c, tid == 0, l * 16 + 11);
   }
