@@ -128,9 +128,10 @@ constexpr int kMiscMmaBar = kMiscRed + 256;  // [kTmemBufs] tensor-core completi
 constexpr int kMiscTmemFree = kMiscMmaBar + 64; // [kTmemBufs] accumulator read by warps 0-3 (count 4)
 constexpr int kMiscTmem = kMiscTmemFree + 64;
 static_assert(kConsumerWarps <= 16, "per-warp misc slots hold 16 warps");
-constexpr int kMiscPart = kMiscTmem + 64;  // [2][kConsumerWarps][kKsplitRows] fp32: per-warp partial row sums (K split)
-constexpr int kKsplitRows = 4;     // rows of a K-split GEMV batch
-constexpr int kMiscBytes = kMiscPart + 2 * 16 * kKsplitRows * 4;
+constexpr int kMiscPart = kMiscTmem + 64;  // [2][16][kKsplitGroupRows] fp32: per-warp partial row sums (K split)
+constexpr int kKsplitRows = 4;       // rows of a K-split GEMV register batch
+constexpr int kKsplitGroupRows = 8;  // rows whose partial sums meet behind one barrier
+constexpr int kMiscBytes = kMiscPart + 2 * 16 * kKsplitGroupRows * 4;
 // A CUDA-core GEMV phase holds all of its ring tiles at once: they must fit
 // in the ring for the smallest grid.
 static_assert((kQKVRows / kMinCtas + 1 + kQKVTileRows - 1) / kQKVTileRows <= kNumSlots, "q|k|v tiles exceed the ring");
@@ -900,7 +901,7 @@ struct Consumer {
   const Params &p;
   uint8_t *smem;
   float *sX, *sA, *sAtt, *sU, *sXW;
-  float *sPart;  // [2][kConsumerWarps][8] K-split partial sums
+  float *sPart;  // [2][16][kKsplitGroupRows] K-split partial sums
   unsigned kpart_seq = 0;  // K-split phases run so far (selects the partials buffer)
   float *red_x, *red_a, *red_lm, *red_e;  // block-reduction slots, one per call site
   uint32_t tile = 0;
@@ -1271,16 +1272,18 @@ struct Consumer {
   // K split (O: K = 2048, down: K = 3072; about as many rows per CTA as
   // warps): the 128-element blocks of K are dealt to the warps round-robin
   // and every warp multiplies its blocks of all rows, so x and the weights
-  // are read once per CTA.  The warps' partial row sums meet in shared
-  // memory (double-buffered) behind one consumer barrier per batch of
-  // kKsplitRows rows; thread r then adds row r's partials in warp order
-  // (deterministic) and emits it.
+  // are read once per CTA.  Rows go through registers in batches of
+  // kKsplitRows; the warps' partial row sums of up to kKsplitGroupRows rows
+  // meet in shared memory (double-buffered) behind one consumer barrier, and
+  // thread r then adds row r's partials in warp order (deterministic) and
+  // emits it.  148 CTAs: 6-7 rows, one barrier per phase.
   template <int KC, int OUT>
   __device__ void fma_ksplit_phase(bool ok, const float *x, int r0, int r1, int tile_rows, int pitch, unsigned E) {
     constexpr int kBlocks = 8 * KC;  // 128-element blocks per row
     constexpr int kMine = (kBlocks + kConsumerWarps - 1) / kConsumerWarps;
     constexpr int RB = kKsplitRows;
-    static_assert(RB == 4, "the transposing reduction handles 4 rows");
+    constexpr int RG = kKsplitGroupRows;
+    static_assert(RB == 4 && RG % RB == 0, "the transposing reduction handles 4 rows");
     const TcJob job{kTcRow, OUT, r0, r1, tile_rows, 1.f, E};
     const int n = r1 - r0;
     const int ntiles = (n + tile_rows - 1) / tile_rows;
@@ -1290,43 +1293,47 @@ struct Consumer {
       const int b = warp + kConsumerWarps * q;
       xv[q] = (b < kBlocks) ? reinterpret_cast<const float4 *>(x)[lane + 32 * b] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    for (int i0 = 0; i0 < n; i0 += RB) {  // every warp runs every batch (barrier inside)
-      float v[RB];
+    for (int g0 = 0; g0 < n; g0 += RG) {  // every warp runs every group (barrier inside)
+      float *part = sPart + (kpart_seq++ & 1) * (16 * RG);
+      const int gn = min(RG, n - g0);
+      for (int b0 = 0; b0 < gn; b0 += RB) {
+        const int i0 = g0 + b0;
+        float v[RB];
 #pragma unroll
-      for (int r = 0; r < RB; ++r) v[r] = 0.f;
-      if (ok) {
-        uint2 w[RB][kMine];
+        for (int r = 0; r < RB; ++r) v[r] = 0.f;
+        if (ok) {
+          uint2 w[RB][kMine];
 #pragma unroll
-        for (int r = 0; r < RB; ++r) {
-          if (i0 + r < n) {
-            const uint8_t *rp = row_ptr(i0 + r, tile_rows, pitch, 8 * lane);
+          for (int r = 0; r < RB; ++r) {
+            if (i0 + r < n) {
+              const uint8_t *rp = row_ptr(i0 + r, tile_rows, pitch, 8 * lane);
 #pragma unroll
-            for (int q = 0; q < kMine; ++q) {
-              const int b = warp + kConsumerWarps * q;
-              if (b < kBlocks) w[r][q] = *reinterpret_cast<const uint2 *>(rp + 256 * b);
+              for (int q = 0; q < kMine; ++q) {
+                const int b = warp + kConsumerWarps * q;
+                if (b < kBlocks) w[r][q] = *reinterpret_cast<const uint2 *>(rp + 256 * b);
+              }
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            if (i0 + r < n) {
+              float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+              for (int q = 0; q < kMine; ++q)
+                if (warp + kConsumerWarps * q < kBlocks) dot4(s0, s1, w[r][q], xv[q]);
+              v[r] = s0 + s1;
             }
           }
         }
-#pragma unroll
-        for (int r = 0; r < RB; ++r) {
-          if (i0 + r < n) {
-            float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-            for (int q = 0; q < kMine; ++q)
-              if (warp + kConsumerWarps * q < kBlocks) dot4(s0, s1, w[r][q], xv[q]);
-            v[r] = s0 + s1;
-          }
-        }
+        const float wsum = reduce4_transpose(v);
+        if ((lane & 7) == 0) part[warp * RG + b0 + 2 * ((lane >> 4) & 1) + ((lane >> 3) & 1)] = wsum;
       }
-      const float wsum = reduce4_transpose(v);
-      float *part = sPart + (kpart_seq++ & 1) * (kConsumerWarps * RB);
-      if ((lane & 7) == 0) part[warp * RB + 2 * ((lane >> 4) & 1) + ((lane >> 3) & 1)] = wsum;
       consumer_sync();
-      if (tid < min(RB, n - i0) && ok) {
+      if (tid < gn && ok) {
         float sum = 0.f;
 #pragma unroll
-        for (int q = 0; q < kConsumerWarps; ++q) sum += part[q * RB + tid];
-        tc_emit(job, r0 + i0 + tid, sum, 0.f);
+        for (int q = 0; q < kConsumerWarps; ++q) sum += part[q * RG + tid];
+        tc_emit(job, r0 + g0 + tid, sum, 0.f);
       }
     }
     release_tiles(ntiles, ok);
