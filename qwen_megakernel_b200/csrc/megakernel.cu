@@ -138,6 +138,11 @@ static_assert((kQKVRows / kMinCtas + 1 + kQKVTileRows - 1) / kQKVTileRows <= kNu
 static_assert((kHidden / kMinCtas + 1 + kOTileRows - 1) / kOTileRows <= kNumSlots, "O tiles exceed the ring");
 static_assert((kInter / kMinCtas + kGUTileRows - 1) / kGUTileRows <= kNumSlots, "gate/up tiles exceed the ring");
 static_assert((kHidden / kMinCtas + 1 + kDTileRows - 1) / kDTileRows <= kNumSlots, "down tiles exceed the ring");
+#ifndef QMK_LM_PREFETCH_TILES
+#define QMK_LM_PREFETCH_TILES 16
+#endif
+constexpr int kLmPrefetchTiles = QMK_LM_PREFETCH_TILES;  // LM-head tiles per CTA prefetched into L2
+constexpr int kLmPrefetchLayers = 4;                     // ... spread over the last layers
 constexpr int kTmemBufs = 8;       // GEMV units (M blocks) in flight
 constexpr int kTmemBufCols = 64;   // D of one unit: 128 lanes x N (<= 48) fp32 columns
 constexpr int kTmemCols = kTmemBufs * kTmemBufCols;
@@ -750,6 +755,21 @@ struct Producer {
   }
   __device__ __forceinline__ uint64_t *bar() { return &c.full[tile % kNumSlots]; }
 
+  // Part j (of kLmPrefetchLayers) of the L2 prefetch of this CTA's first
+  // kLmPrefetchTiles LM-head tiles.
+  __device__ void lm_prefetch(int j) {
+    const Range r = lm_rows(c.cta, c.ncta);
+    const int per = (kLmPrefetchTiles + kLmPrefetchLayers - 1) / kLmPrefetchLayers;
+    const uint64_t keep = l2_policy_evict_last();
+    for (int t = j * per; t < min(kLmPrefetchTiles, (j + 1) * per); ++t) {
+      const int r0 = r.begin + t * kLMTileRows;
+      const int n = min(kLMTileRows, r.end - r0);
+      if (n <= 0) break;
+      bulk_prefetch_l2(reinterpret_cast<const uint8_t *>(p.lm_head) + (size_t)r0 * (kHidden * 2),
+                       (unsigned)(n * kHidden * 2), keep);
+    }
+  }
+
   // Rows of `mat` in tiles of tile_rows; row k of a tile lands at
   // k * dst_pitch (one copy when the rows are contiguous in the tile).
   __device__ void rows(const __nv_bfloat16 *mat, int row_bytes, Range r, int tile_rows, int dst_pitch) {
@@ -859,6 +879,11 @@ struct Producer {
       for (int l = 0; l < p.num_layers && alive; ++l) {
         c.cur_layer = l;
         const LDGLayerWeights w = p.layers[l];
+        // The layers leave most of the HBM bandwidth unused while the LM head
+        // is bound by it: during the last layers the first LM-head tiles of
+        // this CTA are requested into L2 (evict-last), so that the LM-head
+        // phase reads them from L2.
+        if (l >= p.num_layers - kLmPrefetchLayers) lm_prefetch(l - (p.num_layers - kLmPrefetchLayers));
         trace_stamp(c, true, l * 16 + 12);
         qkv(w, qkv_rows(c.cta, c.ncta));
         if (item >= 0) kv(t, l, item / p.splits, kv_chunk(pos, item % p.splits, p.splits));
