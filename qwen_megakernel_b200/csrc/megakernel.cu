@@ -1184,12 +1184,12 @@ struct Consumer {
     if (__any_sync(0xffffffffu, miss != 0u)) {
       for (int t = 0; t < ntiles; ++t) ok = wait_full(c, tile + (uint32_t)t) && ok;
     } else if (stamp) {
-      // same stamps as wait_full: wait entry and tile landed, per tile
-      const uint64_t t1 = trace_now(c);
+      // the stamps of wait_full (wait entry, tile seen landed): every tile
+      // had landed when the warp first tested it
       for (int t = 0; t < ntiles; ++t) {
         const uint32_t k = tile + (uint32_t)t - c.trace_tile0;
         c.trace[kTraceTileBase + 2 * k] = t0;
-        c.trace[kTraceTileBase + 2 * k + 1] = t1;
+        c.trace[kTraceTileBase + 2 * k + 1] = t0;
       }
     }
     return ok;
