@@ -538,7 +538,7 @@ def measure_batch(B: int, steps: int, warmup: int, seed_base: int = 100, distrib
     t0 = time.perf_counter()
     out = bd.generate(first, steps).cpu()
     e2e_ms = reduce_max((time.perf_counter() - t0) * 1000.0, distributed)
-    bd.fw.check_status()
+    bd.check_status()
     step_bytes = [WEIGHT_BYTES + B * KV_BYTES_PER_POS * (p + 1) for p in range(p_start, p_start + steps)]
     achieved = sum(step_bytes) / (ms / 1000.0) / 1e9
     peak, peak_kind = measured_peak()
@@ -548,7 +548,10 @@ def measure_batch(B: int, steps: int, warmup: int, seed_base: int = 100, distrib
         "value": round(B * steps / (ms / 1000.0), 1), "unit": "tok/s", "steps": steps, "warmup": warmup,
         "ms_per_step": round(ms / steps, 4), "batch": B,
         "workload": f"configs[3]-style: {B} sequences, 1024-token prompts, {steps} greedy steps "
-                    f"(cache positions {p_start}..{p_start + steps - 1}), CUDA-graph step",
+                    f"(cache positions {p_start}..{p_start + steps - 1}), "
+                    + ("one launch of the persistent decode kernel (batched instance)" if bd.decode_mode == "megakernel"
+                       else "token-parallel kernels, CUDA-graph step"),
+        "decode_path": bd.decode_mode,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_step": int(sum(step_bytes) / steps)},

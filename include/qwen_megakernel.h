@@ -197,6 +197,44 @@ int qmk_workspace_init(void *workspace, size_t workspace_bytes, cudaStream_t str
  * errors are reported through args->status after the stream completes. */
 int qmk_run(const QmkRunArgs *args, cudaStream_t stream);
 
+/* ---- batched decode in the persistent kernel (no reference counterpart) --
+ * QMK_BATCH_SEQS sequences decoded together greedily, each with its own K/V
+ * cache (sequence s at element offset s * cache_seq_stride of k_cache /
+ * v_cache, each in the reference layout [num_layers, 8, max_seq_len, 128])
+ * and its own position.  Step t of sequence s consumes its step-t token at
+ * cache position start_positions[s] + t (step 0: first_tokens[s], then the
+ * greedy token of step t - 1) and writes that position's K/V; the greedy
+ * token of step t goes to output_log[t * QMK_BATCH_SEQS + s].  Same kernel
+ * as qmk_run: every weight tile is streamed once per step for all
+ * sequences.  Uses the workspace of qmk_workspace_bytes(); device errors
+ * are reported through status as for qmk_run. */
+#define QMK_BATCH_SEQS 4
+
+typedef struct QmkBatchRunArgs {
+  const void *embed_weight;              /* bf16 [151936, 1024]               */
+  const LDGLayerWeights *layer_weights;  /* device array [num_layers]         */
+  const void *final_norm_weight;         /* bf16 [1024]                       */
+  const void *lm_head_weight;            /* bf16 [151936, 1024]               */
+  const void *cos_table;                 /* bf16 [>= max position + 1, 128]   */
+  const void *sin_table;
+  void *k_cache;                         /* bf16, see above                   */
+  void *v_cache;
+  long long cache_seq_stride;            /* elements between sequences' caches */
+  void *workspace;                       /* device, qmk_workspace_bytes()     */
+  size_t workspace_bytes;
+  const int *first_tokens;               /* device int32 [QMK_BATCH_SEQS]     */
+  int start_positions[QMK_BATCH_SEQS];   /* host values                       */
+  int num_steps;
+  int num_layers;
+  int max_seq_len;
+  float attn_scale;
+  int *output_log;                       /* device int32 [num_steps][QMK_BATCH_SEQS] or NULL */
+  QmkStatus *status;                     /* mapped pinned host memory or NULL */
+  unsigned long long timeout_ns;         /* per-wait limit; 0 = 1 s default   */
+} QmkBatchRunArgs;
+
+int qmk_run_batch(const QmkBatchRunArgs *args, cudaStream_t stream);
+
 /* Host-side error of the last qmk_* / launch_ldg_* call on this thread. */
 int qmk_get_last_error(void);
 const char *qmk_get_last_error_message(void);
@@ -252,7 +290,7 @@ int qmk_trace_words(void);
  *    the last call) and of the QmkStatus block (device memory: copy it to
  *    the host after the stream completes). */
 #define QMK_STATIC_MAX_STEPS 4096
-#define QMK_STATIC_SCRATCH_BYTES (512 * 1024)
+#define QMK_STATIC_SCRATCH_BYTES (1024 * 1024)
 
 int qmk_generate_static(int first_token_id, int num_steps, const void *embed_weight,
                         const LDGLayerWeights *layer_weights, const void *final_norm_weight,

@@ -11,7 +11,11 @@ sequence; these are the "batched prefill" and "batch > 1" extensions of its
 * ``Decoder.prefill_batched`` (model.py) uses it for a prompt
 * ``BatchDecoder``      B independent sequences, one row each per step; the
                         step is captured in a CUDA graph (device-side token
-                        feedback, no host round trip per step)
+                        feedback, no host round trip per step).  With B =
+                        MEGAKERNEL_SEQS its decode steps run instead in the
+                        persistent decode kernel (``qmk_run_batch``): one
+                        launch for all steps, every weight tile streamed
+                        once per step for all sequences.
 """
 
 from __future__ import annotations
@@ -27,6 +31,7 @@ MAX_ROWS = 4096  # QMK_BATCH_MAX_ROWS
 BAD_TOKEN = 1  # QMK_BATCH_BAD_TOKEN
 BAD_ROW = 2  # QMK_BATCH_BAD_ROW
 TIMEOUT = 4  # QMK_BATCH_TIMEOUT
+MEGAKERNEL_SEQS = 4  # QMK_BATCH_SEQS: sequences of the persistent kernel's batched instance
 
 
 class BatchError(RuntimeError):
@@ -118,9 +123,18 @@ class BatchDecoder:
     token-parallel rows (all sequences' prompts in one pass), ``step`` one
     row per sequence."""
 
-    def __init__(self, weights, batch_size: int, max_seq_len: int | None = None, use_graphs: bool = True):
+    def __init__(self, weights, batch_size: int, max_seq_len: int | None = None, use_graphs: bool = True,
+                 decode: str = "auto"):
+        """decode: "token_parallel" (one row per sequence through the
+        token-parallel kernels), "megakernel" (the persistent decode kernel's
+        batched instance, B == MEGAKERNEL_SEQS only) or "auto" (the persistent
+        kernel when B == MEGAKERNEL_SEQS)."""
         if batch_size < 1 or batch_size > MAX_ROWS:
             raise ValueError(f"batch_size must be in [1, {MAX_ROWS}]")
+        if decode not in ("auto", "token_parallel", "megakernel"):
+            raise ValueError("decode must be 'auto', 'token_parallel' or 'megakernel'")
+        if decode == "megakernel" and batch_size != MEGAKERNEL_SEQS:
+            raise ValueError(f"the persistent kernel decodes exactly {MEGAKERNEL_SEQS} sequences")
         self.B = int(batch_size)
         self.fw = BatchForward(weights, int(max_seq_len or weights["cos_table"].shape[0]))
         self.device = self.fw.device
@@ -138,6 +152,29 @@ class BatchDecoder:
         self._ws_step = torch.empty(int(self.fw._ops.batch_workspace_bytes(self.B, self.B)), dtype=torch.uint8,
                                     device=self.device)
         self._graph = None
+        self.decode_mode = "megakernel" if (decode == "megakernel" or (decode == "auto" and self.B == MEGAKERNEL_SEQS)) \
+            else "token_parallel"
+        if self.decode_mode == "megakernel":
+            from .model import _pack_layer_weights
+
+            self._mk_layers = _pack_layer_weights(weights["layer_weights"], self.device)
+            self._mk_ws = torch.zeros(int(self.fw._ops.workspace_bytes()), dtype=torch.uint8, device=self.device)
+            self._mk_status = torch.zeros(4, dtype=torch.int32).pin_memory()
+            self._mk_first = torch.zeros(self.B, dtype=torch.int32, device=self.device)
+
+    def check_status(self) -> None:
+        """Raise if the last completed step (token-parallel) or launch
+        (persistent kernel) reported a device error; call after a stream
+        synchronize."""
+        self.fw.check_status()
+        if self.decode_mode == "megakernel":
+            from .model import _ERROR_NAMES, DecodeError
+
+            code = int(self._mk_status[0])
+            if code != 0:
+                info = int(self._mk_status[1]) & 0xFFFFFFFF
+                raise DecodeError(f"qwen_megakernel device error {code} ({_ERROR_NAMES.get(code, '?')}): "
+                                  f"cta {info >> 16}, site {(info >> 8) & 0xFF}, layer {info & 0xFF}")
 
     def reset(self) -> None:
         self.k_cache.zero_()
@@ -222,6 +259,15 @@ class BatchDecoder:
         if any(p + n > self.max_seq_len for p in self.positions):
             raise ValueError("generation would exceed max_seq_len")
         log = torch.empty(n, self.B, dtype=torch.int32, device=self.device)
+        if self.decode_mode == "megakernel":
+            # one launch of the persistent kernel for all n steps
+            fw = self.fw
+            self._mk_first.copy_(torch.as_tensor(first_tokens, dtype=torch.int32).to(self.device, non_blocking=True))
+            fw._ops.run_batch(self._mk_ws, fw.embed, self._mk_layers, fw.final_norm, fw.lm_head, fw.cos, fw.sin,
+                              self.k_cache, self.v_cache, self._mk_first, [int(p) for p in self.positions], n,
+                              fw.num_layers, self.max_seq_len, fw.attn_scale, log, self._mk_status, 0)
+            self.positions = [p + n for p in self.positions]
+            return log
         self._tok.copy_(torch.as_tensor(first_tokens, dtype=torch.int32).to(self.device, non_blocking=True))
         self._pos.copy_(_int32(self.positions, self.device))
         if not self.use_graphs:

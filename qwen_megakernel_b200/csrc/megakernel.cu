@@ -108,6 +108,11 @@ struct Params {
   int top_k;            // sampling restricted to the top_k logits (0: all)
   int eos_token;        // stop after a generated token equal to this (-1: never)
   int *steps_done;      // optional: steps executed (< num_steps after an EOS stop)
+  // Batched instance (NB > 1 sequences): per-sequence start positions, the
+  // elements between sequences' caches and the step-0 tokens (device [NB]).
+  int start_pos_b[kMaxSeqs];
+  long long cache_seq_stride;
+  const int *first_tokens_b;
 };
 
 // Dynamic shared memory plan (bytes).
@@ -131,7 +136,9 @@ static_assert(kConsumerWarps <= 16, "per-warp misc slots hold 16 warps");
 constexpr int kMiscPart = kMiscTmem + 64;  // [2][16][kKsplitGroupRows] fp32: per-warp partial row sums (K split)
 constexpr int kKsplitRows = 4;       // rows of a K-split GEMV register batch
 constexpr int kKsplitGroupRows = 8;  // rows whose partial sums meet behind one barrier
-constexpr int kMiscBytes = kMiscPart + 2 * 16 * kKsplitGroupRows * 4;
+constexpr int kMiscRes = kMiscPart + 2 * 16 * kKsplitGroupRows * 4;  // [2][kMaxSeqs][16] fp32: residual rows (batched)
+constexpr int kMaxResRows = 8;   // O / down rows per CTA the batched instance keeps residuals of (>= 128 CTAs)
+constexpr int kMiscBytes = kMiscRes + 2 * kMaxSeqs * kMaxResRows * 4;
 // A CUDA-core GEMV phase holds all of its ring tiles at once: they must fit
 // in the ring for the smallest grid.
 static_assert((kQKVRows / kMinCtas + 1 + kQKVTileRows - 1) / kQKVTileRows <= kNumSlots, "q|k|v tiles exceed the ring");
@@ -147,7 +154,9 @@ constexpr int kTmemBufs = 8;       // GEMV units (M blocks) in flight
 constexpr int kTmemBufCols = 64;   // D of one unit: 128 lanes x N (<= 48) fp32 columns
 constexpr int kTmemCols = kTmemBufs * kTmemBufCols;
 constexpr int kSmBytes = kSmMisc + kMiscBytes;
-static_assert(kSmBytes <= 232448, "shared memory plan exceeds the sm_100 per-block limit");
+// 227 KB per block on sm_100, of which the kernel's static __shared__ data
+// (argmax exchange, abort/stop flags) takes up to 1 KB.
+static_assert(kSmBytes + 1024 <= 232448, "shared memory plan exceeds the sm_100 per-block limit");
 
 // Attention scratch inside the U region (floats).
 constexpr int kUQ = 0;      // q, 2 heads [256]
@@ -667,18 +676,18 @@ __device__ __forceinline__ bool arg_better(unsigned ka, int ia, unsigned kb, int
 
 // Poll every CTA's (key, index) pair for epoch `flag`; all consumer threads
 // return the grid-wide argmax (largest logit, lowest index on ties).
-__device__ int read_argmax(Ctx &c, unsigned flag) {
+__device__ int read_argmax(Ctx &c, unsigned flag, int b = 0) {
   const int tid = threadIdx.x;
   unsigned key = 0;
   int idx = 0x7fffffff;
   if (tid < c.ncta && *c.abort_flag == 0) {
     Waiter w;
     while (true) {
-      uint64_t a, b;
-      ll_load2(c.wArg + 2 * tid, a, b);
-      if (ll_flag(a) == flag && ll_flag(b) == flag) {
+      uint64_t a, bw;
+      ll_load2(c.wArg + (size_t)b * kWordsArg + 2 * tid, a, bw);
+      if (ll_flag(a) == flag && ll_flag(bw) == flag) {
         key = (unsigned)(a & 0xffffffffu);
-        idx = (int)(b & 0xffffffffu);
+        idx = (int)(bw & 0xffffffffu);
         break;
       }
       if (!w.keep_going(c, kSiteArg)) break;
@@ -716,7 +725,8 @@ __device__ int read_argmax(Ctx &c, unsigned flag) {
 }
 
 // ------------------------------------------------------------- producer
-template <bool kFeat>
+// NB: sequences of the batched instance (1 = the single-sequence kernel).
+template <bool kFeat, int NB = 1>
 struct Producer {
   Ctx &c;
   const Params &p;
@@ -838,14 +848,15 @@ struct Producer {
     }
   }
 
-  // K/V rows [chunk) of (layer, kv head g).  Positions written earlier in this
-  // launch are read only after their writer published kv_ready.
-  __device__ void kv(int step, int layer, int g, Range ch) {
+  // K/V rows [chunk) of (sequence b, layer, kv head g).  Positions written
+  // earlier in this launch are read only after their writer published kv_ready.
+  __device__ void kv(int step, int layer, int b, int g, Range ch) {
     if (ch.end <= ch.begin || !alive) return;
-    if (ch.end > p.start_pos && step > 0) {
+    const int start = (NB > 1) ? p.start_pos_b[b] : p.start_pos;
+    if (ch.end > start && step > 0) {
       const unsigned e_prev = epoch_of(c, step - 1, layer, p.num_layers);
       const unsigned e_cur = epoch_of(c, step, layer, p.num_layers);
-      const unsigned *flag = &c.ctrl->kv_ready[layer * kNumKVHeads + g];
+      const unsigned *flag = &c.ctrl->kv_ready[(b * kMaxLayers + layer) * kNumKVHeads + g];
       Waiter w;
       while (true) {
         const unsigned v = ld_acquire_u32(flag);
@@ -858,11 +869,12 @@ struct Producer {
       fence_proxy_async_global();
     }
     const size_t head_off = ((size_t)layer * kNumKVHeads + g) * (size_t)p.max_seq_len;
+    const size_t seq_off = (NB > 1) ? (size_t)b * (size_t)p.cache_seq_stride : 0;
     for (int j0 = ch.begin; j0 < ch.end && alive; j0 += kKVTilePos) {
       const int n = min(kKVTilePos, ch.end - j0);
       uint8_t *dst = begin((unsigned)(2 * n * kHeadDim * 2));
       if (!dst) return;
-      const size_t off = (head_off + j0) * kHeadDim;
+      const size_t off = (head_off + j0) * kHeadDim + seq_off;
       bulk_g2s(dst, p.k_cache + off, (unsigned)(n * kHeadDim * 2), bar(), pol);
       bulk_g2s(dst + kKVTileVOffset, p.v_cache + off, (unsigned)(n * kHeadDim * 2), bar(), pol);
       ++tile;
@@ -870,10 +882,12 @@ struct Producer {
   }
 
   __device__ void run() {
-    const int item = item_of_cta(c.cta, p.splits);
+    const int item = item_of_cta(c.cta, p.splits, NB);
+    const int ib = (item >= 0) ? item / (kNumKVHeads * p.splits) : 0;  // sequence of the item
+    const int ig = (item >= 0) ? (item / p.splits) % kNumKVHeads : 0;
     for (int t = 0; t < p.num_steps && alive && *c.stop_step > t; ++t) {
       cur_step = t;
-      const int pos = p.start_pos + t;
+      const int pos = ((NB > 1) ? p.start_pos_b[ib] : p.start_pos) + t;
       c.trace = (kFeat && p.trace && t == p.trace_step) ? p.trace + (size_t)c.cta * kTraceStride : nullptr;
       c.trace_tile0 = tile;
       for (int l = 0; l < p.num_layers && alive; ++l) {
@@ -886,7 +900,7 @@ struct Producer {
         if (l >= p.num_layers - kLmPrefetchLayers) lm_prefetch(l - (p.num_layers - kLmPrefetchLayers));
         trace_stamp(c, true, l * 16 + 12);
         qkv(w, qkv_rows(c.cta, c.ncta));
-        if (item >= 0) kv(t, l, item / p.splits, kv_chunk(pos, item % p.splits, p.splits));
+        if (item >= 0) kv(t, l, ib, ig, kv_chunk(pos, item % p.splits, p.splits));
         rows((const __nv_bfloat16 *)w.o_proj_weight, kQSize * 2, o_rows(c.cta, c.ncta), kOTileRows, kQSize * 2);
         gate_up(w, gu_rows(c.cta, c.ncta));
         rows((const __nv_bfloat16 *)w.down_proj_weight, kInter * 2, d_rows(c.cta, c.ncta), kDTileRows,
@@ -894,7 +908,8 @@ struct Producer {
         trace_stamp(c, true, l * 16 + 13);
       }
       trace_stamp(c, true, p.num_layers * 16 + 3);
-      rows(p.lm_head, kHidden * 2, lm_rows(c.cta, c.ncta), kLMTileRows, kHidden * 2);
+      for (int b = 0; b < NB; ++b)  // one LM-head pass per sequence
+        rows(p.lm_head, kHidden * 2, lm_rows(c.cta, c.ncta), kLMTileRows, kHidden * 2);
       trace_stamp(c, true, p.num_layers * 16 + 4);
     }
     // Drain: the last tile issued into each slot must land before the CTA exits.
@@ -920,12 +935,16 @@ struct Producer {
 // carries none of that code: the kernel cycles through nearly all of its code
 // every layer, and on B200 every KB less in that loop is measurable (the
 // optional features cost ~17 us/token when compiled into the common path).
-template <bool kFeat>
+template <bool kFeat, int NB = 1>
 struct Consumer {
   Ctx &c;
   const Params &p;
   uint8_t *smem;
   float *sX, *sA, *sAtt, *sU, *sXW;
+  // Batched instance: the sequence a phase is working on, and per sequence
+  // the residual inputs of this CTA's O rows (from X) and down rows (from A).
+  int cur_b = 0;
+  float *sResO, *sResD;  // [kMaxSeqs][kMaxResRows]
   float *sPart;  // [2][16][kKsplitGroupRows] K-split partial sums
   unsigned kpart_seq = 0;  // K-split phases run so far (selects the partials buffer)
   float *red_x, *red_a, *red_lm, *red_e;  // block-reduction slots, one per call site
@@ -948,6 +967,8 @@ struct Consumer {
     sU = reinterpret_cast<float *>(smem + kSmU);
     sXW = reinterpret_cast<float *>(smem + kSmXW);
     sPart = reinterpret_cast<float *>(smem + kSmMisc + kMiscPart);
+    sResO = reinterpret_cast<float *>(smem + kSmMisc + kMiscRes);
+    sResD = sResO + kMaxSeqs * kMaxResRows;
     float *red = reinterpret_cast<float *>(smem + kSmMisc + kMiscRed);
     red_x = red;
     red_a = red + 16;
@@ -1032,20 +1053,24 @@ struct Consumer {
   __device__ void tc_emit(const TcJob &job, int row, float v, float v2) {
     switch (job.out) {
       case kOutQKV:
-        put(c.wQKV + row, ll_pack(v * job.scale, job.E));
+        put(c.wQKV + (NB > 1 ? (size_t)cur_b * kWordsQKV : 0) + row, ll_pack(v * job.scale, job.E));
         break;
-      case kOutO:
-        put(c.wA + row, ll_pack(v + sX[row], job.E));
+      case kOutO: {
+        const float res = (NB > 1) ? sResO[cur_b * kMaxResRows + (row - job.r0)] : sX[row];
+        put(c.wA + (NB > 1 ? (size_t)cur_b * kWordsA : 0) + row, ll_pack(v + res, job.E));
         break;
+      }
       case kOutGU: {
         const float gs = v * job.scale, us = v2 * job.scale;
         const float silu = gs * fast_rcp(1.0f + fast_exp2(-gs * kLog2e));
-        put(c.wM + row, ll_pack(silu * us, job.E));
+        put(c.wM + (NB > 1 ? (size_t)cur_b * kWordsM : 0) + row, ll_pack(silu * us, job.E));
         break;
       }
-      case kOutDown:
-        put(c.wX + row, ll_pack(v + sA[row], job.E));
+      case kOutDown: {
+        const float res = (NB > 1) ? sResD[cur_b * kMaxResRows + (row - job.r0)] : sA[row];
+        put(c.wX + (NB > 1 ? (size_t)cur_b * kWordsX : 0) + row, ll_pack(v + res, job.E));
         break;
+      }
       default: {  // kOutLM
         const float y = v * job.scale;
         if constexpr (kFeat) {
@@ -1227,7 +1252,7 @@ struct Consumer {
   // between the warps.
   template <int OUT, int MR>
   __device__ void fma_rows_phase(bool ok, const float *x, int r0, int r1, int tile_rows, int pitch, float scale,
-                                 unsigned E) {
+                                 unsigned E, bool release = true) {
     constexpr bool kGU = (OUT == kOutGU);
     static_assert(MR >= 1 && MR <= 4, "rows per warp batch");
     const TcJob job{kTcRow, OUT, r0, r1, tile_rows, scale, E};
@@ -1291,7 +1316,7 @@ struct Consumer {
       const int i = i0 + kConsumerWarps * rr;
       if ((lane & 7) == 0 && rr < MR && i < n) tc_emit(job, r0 + i, sum, sum2);
     }
-    release_tiles(ntiles, ok);
+    if (release) release_tiles(ntiles, ok);
   }
 
   // K split (O: K = 2048, down: K = 3072; about as many rows per CTA as
@@ -1303,7 +1328,8 @@ struct Consumer {
   // thread r then adds row r's partials in warp order (deterministic) and
   // emits it.  148 CTAs: 6-7 rows, one barrier per phase.
   template <int KC, int OUT>
-  __device__ void fma_ksplit_phase(bool ok, const float *x, int r0, int r1, int tile_rows, int pitch, unsigned E) {
+  __device__ void fma_ksplit_phase(bool ok, const float *x, int r0, int r1, int tile_rows, int pitch, unsigned E,
+                                   bool release = true) {
     constexpr int kBlocks = 8 * KC;  // 128-element blocks per row
     constexpr int kMine = (kBlocks + kConsumerWarps - 1) / kConsumerWarps;
     constexpr int RB = kKsplitRows;
@@ -1361,7 +1387,7 @@ struct Consumer {
         tc_emit(job, r0 + g0 + tid, sum, 0.f);
       }
     }
-    release_tiles(ntiles, ok);
+    if (release) release_tiles(ntiles, ok);
   }
 
   // Issuer threads: wait (bounded) for the last MMAs they issued, so that
@@ -1418,11 +1444,12 @@ struct Consumer {
 
   // P2: one split-KV attention item for KV head g (q heads 2g, 2g+1).
   __device__ void phase_attention(const LDGLayerWeights &w, int layer, int step, unsigned E) {
-    const int item = item_of_cta(c.cta, p.splits);
+    const int item = item_of_cta(c.cta, p.splits, NB);
     if (item < 0) return;
-    const int g = item / p.splits, s = item % p.splits;
+    const int g = (item / p.splits) % kNumKVHeads, s = item % p.splits;
+    const int b = (NB > 1) ? item / (kNumKVHeads * p.splits) : 0;  // sequence
     const bool last = (s == p.splits - 1);
-    const int pos = p.start_pos + step;
+    const int pos = ((NB > 1) ? p.start_pos_b[b] : p.start_pos) + step;
     const Range ch = kv_chunk(pos, s, p.splits);
     float *sQ = sU + kUQ;
     float *sPW = sU + kUPW;
@@ -1446,7 +1473,7 @@ struct Consumer {
           const int row = (i < 256) ? (g * 256 + i)
                                     : (i < 384) ? (kQSize + g * 128 + (i - 256))
                                                 : (kQSize + kKVSize + g * 128 + (i - 384));
-          return c.wQKV + row;
+          return c.wQKV + (NB > 1 ? (size_t)b * kWordsQKV : 0) + row;
         },
         E, kSiteQKV);
     trace_stamp(c, tid == 0, layer * 16 + 2);
@@ -1479,8 +1506,8 @@ struct Consumer {
       } else {
         // New K/V row of this position, bf16: into the cache and, in the
         // cache's row format, into smem for this step's softmax.
-        const size_t off =
-            (((size_t)layer * kNumKVHeads + g) * (size_t)p.max_seq_len + pos) * kHeadDim + d0;
+        const size_t off = (((size_t)layer * kNumKVHeads + g) * (size_t)p.max_seq_len + pos) * kHeadDim + d0 +
+                           (NB > 1 ? (size_t)b * (size_t)p.cache_seq_stride : 0);
         unsigned kbits[4], vbits[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -1699,8 +1726,9 @@ struct Consumer {
 
   // P2.5: merge the split partials of (q head h, 64 dims) -> ATT words.
   __device__ void phase_merge(unsigned E, int l) {
-    const int j = merge_task_of_cta(c.cta, c.ncta);
-    if (j < 0) return;
+    const int jt = merge_task_of_cta(c.cta, c.ncta, NB);
+    if (jt < 0) return;
+    const int b = jt / kMergeTasks, j = jt % kMergeTasks;  // sequence, task within it
     const int h = j >> 1, half = j & 1, g = h >> 1, hl = h & 1;
     const int S = p.splits;
     const int n = S * kMergeWordsPerSplit;
@@ -1709,7 +1737,7 @@ struct Consumer {
         [&](int i) -> const uint64_t * {
           const int s = i / kMergeWordsPerSplit, k = i % kMergeWordsPerSplit;
           const int word = (k < 2) ? (2 * hl + k) : (4 + hl * kHeadDim + half * kMergeDims + (k - 2));
-          return c.wPart + (size_t)(g * S + s) * kPartWords + word;
+          return c.wPart + (size_t)((b * kNumKVHeads + g) * S + s) * kPartWords + word;
         },
         E, kSitePart);
     trace_stamp(c, tid == 0, l * 16 + 4);
@@ -1725,7 +1753,8 @@ struct Consumer {
           O += sU[s * kMergeWordsPerSplit + 2 + tid] * f;
         }
       }
-      put(c.wAtt + h * kHeadDim + half * kMergeDims + tid, ll_pack(O * fast_rcp(L), E));
+      put(c.wAtt + (NB > 1 ? (size_t)b * kWordsAtt : 0) + h * kHeadDim + half * kMergeDims + tid,
+          ll_pack(O * fast_rcp(L), E));
     }
     consumer_sync();
     flush();
@@ -1937,19 +1966,25 @@ struct Consumer {
     }
     flush();
     consumer_sync();
-    // Publish this step's K/V rows for the next step's TMA reads, after the
-    // ARG words (off the step's critical path): one gpu-scope fence orders
-    // every row written since (the CTA synchronized with their writers at
-    // the named barriers in between), then the flags as relaxed stores.
+    publish_kv(step);
+    trace_stamp(c, tid == 0, p.num_layers * 16 + 1);
+  }
+
+  // Publish this step's K/V rows for the next step's TMA reads, after the
+  // ARG words (off the step's critical path): one gpu-scope fence orders
+  // every row written since (the CTA synchronized with their writers at the
+  // named barriers in between), then the flags as relaxed stores.
+  __device__ void publish_kv(int step) {
     if (kv_written && tid == 0 && live()) {
       __threadfence();
-      const int g = item_of_cta(c.cta, p.splits) / p.splits;
+      const int item = item_of_cta(c.cta, p.splits, NB);
+      const int g = (item / p.splits) % kNumKVHeads;
+      const int b = (NB > 1) ? item / (kNumKVHeads * p.splits) : 0;
       for (int l = 0; l < p.num_layers; ++l)
         if (kv_written & (1ull << l))
-          st_relaxed_u32(&c.ctrl->kv_ready[l * kNumKVHeads + g], epoch_of(c, step, l, p.num_layers));
+          st_relaxed_u32(&c.ctrl->kv_ready[(b * kMaxLayers + l) * kNumKVHeads + g], epoch_of(c, step, l, p.num_layers));
     }
     kv_written = 0;
-    trace_stamp(c, tid == 0, p.num_layers * 16 + 1);
   }
 
   // Token consumed by step t.
@@ -1972,6 +2007,10 @@ struct Consumer {
   int steps_run = 0;  // steps executed (num_steps unless stopped at EOS)
 
   __device__ void run() {
+    if constexpr (NB > 1) {
+      run_nb();
+      return;
+    }
     const int L = p.num_layers;
     steps_run = p.num_steps;
     for (int t = 0; t < p.num_steps; ++t) {
@@ -2039,9 +2078,215 @@ struct Consumer {
       if (tid == 0 && !live() && p.out_token) *p.out_token = -1;
     }
   }
+
+  // ---------------------------------------------------- batched instance
+  // NB > 1 sequences decoded together (greedy).  A GEMV phase tests its ring
+  // tiles once, runs once per sequence on them and releases them after the
+  // last sequence, so every weight byte is read from HBM once per step for
+  // all sequences; while this CTA works on sequence b the other CTAs'
+  // outputs for sequence b + 1 arrive, so most dataflow waits after the
+  // first sequence find their words already written.  Attention items and
+  // merge tasks are per (sequence, ...); the LM head runs one pass per
+  // sequence over the same rows.
+
+  // Layer-0 input: the embedding row of `tok` into sX; returns its sum of
+  // squares (a consumer barrier inside).
+  __device__ float embed_row(int tok) {
+    const __nv_bfloat16 *erow = p.embed + (size_t)tok * kHidden;
+    float ss = 0.f;
+    for (int i = tid; i < kHidden / 4; i += kConsumerThreads) {
+      const uint2 v = __ldg(reinterpret_cast<const uint2 *>(erow) + i);
+      const float e0 = bf_lo(v.x), e1 = bf_hi(v.x), e2 = bf_lo(v.y), e3 = bf_hi(v.y);
+      sX[4 * i + 0] = e0;
+      sX[4 * i + 1] = e1;
+      sX[4 * i + 2] = e2;
+      sX[4 * i + 3] = e3;
+      ss += e0 * e0 + e1 * e1 + e2 * e2 + e3 * e3;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red_e[warp] = ss;
+    consumer_sync();
+    float total = 0.f;
+#pragma unroll
+    for (int q = 0; q < kConsumerWarps; ++q) total += red_e[q];
+    return total;
+  }
+
+  __device__ void phase_qkv_nb(unsigned E, unsigned x_flag, const int (&toks)[NB]) {
+    const NormPairs nw = nw_pref;
+    const Range R = qkv_rows(c.cta, c.ncta), Ro = o_rows(c.cta, c.ncta);
+    const int ntiles = tiles_of(R, kQKVTileRows);
+    const bool tiles = wait_tiles(ntiles);
+#pragma unroll 1
+    for (int b = 0; b < NB; ++b) {
+      cur_b = b;
+      if (b > 0) consumer_sync();  // every warp has read sequence b-1's sXW
+      float x_ss;
+      if (x_flag) {
+        x_ss = stage_vec<kHidden, kStageNorm>(c, sX, reinterpret_cast<uint8_t *>(sXW), c.wX + (size_t)b * kWordsX,
+                                              x_flag, kSiteX, red_x, nw);
+      } else {
+        x_ss = embed_row(toks[b]);
+        build_norm_xw(sXW, sX, nw, tid);
+        consumer_sync();
+      }
+      if (tid < Ro.end - Ro.begin) sResO[b * kMaxResRows + tid] = sX[Ro.begin + tid];
+      fma_rows_phase<kOutQKV, 4>(tiles, sXW, R.begin, R.end, kQKVTileRows, 2048,
+                                 rsqrtf(x_ss / (float)kHidden + kRmsEps), E, false);
+    }
+    release_tiles(ntiles, tiles);
+  }
+
+  __device__ void phase_o_nb(const LDGLayerWeights &w, unsigned E) {
+    nw_pref = load_norm_pairs((const __nv_bfloat16 *)w.post_attn_layernorm_weight, tid);
+    const Range R = o_rows(c.cta, c.ncta);
+    const int ntiles = tiles_of(R, kOTileRows);
+    const bool tiles = wait_tiles(ntiles);
+#pragma unroll 1
+    for (int b = 0; b < NB; ++b) {
+      cur_b = b;
+      // (the K-split phase's barrier comes after every warp read its inputs)
+      stage_vec<kQSize, kStageCopy>(c, sAtt, nullptr, c.wAtt + (size_t)b * kWordsAtt, E, kSiteAtt, nullptr, NormPairs{});
+      fma_ksplit_phase<2, kOutO>(tiles, sAtt, R.begin, R.end, kOTileRows, kQSize * 2, E, false);
+    }
+    release_tiles(ntiles, tiles);
+  }
+
+  __device__ void phase_gu_nb(unsigned E) {
+    const NormPairs nw = nw_pref;
+    const Range R = gu_rows(c.cta, c.ncta), Rd = d_rows(c.cta, c.ncta);
+    const int ntiles = tiles_of(R, kGUTileRows);
+    const bool tiles = wait_tiles(ntiles);
+#pragma unroll 1
+    for (int b = 0; b < NB; ++b) {
+      cur_b = b;
+      if (b > 0) consumer_sync();  // every warp has read sequence b-1's sXW
+      const float ss = stage_vec<kHidden, kStageNorm>(c, sA, reinterpret_cast<uint8_t *>(sXW),
+                                                      c.wA + (size_t)b * kWordsA, E, kSiteA, red_a, nw);
+      if (tid < Rd.end - Rd.begin) sResD[b * kMaxResRows + tid] = sA[Rd.begin + tid];
+      fma_rows_phase<kOutGU, 3>(tiles, sXW, R.begin, R.end, kGUTileRows, 4096, rsqrtf(ss / (float)kHidden + kRmsEps),
+                                E, false);
+    }
+    release_tiles(ntiles, tiles);
+  }
+
+  __device__ void phase_down_nb(unsigned E, int l) {
+    nw_pref = load_norm_pairs(
+        (l + 1 < p.num_layers) ? (const __nv_bfloat16 *)p.layers[l + 1].input_layernorm_weight : p.final_norm, tid);
+    const Range R = d_rows(c.cta, c.ncta);
+    const int ntiles = tiles_of(R, kDTileRows);
+    const bool tiles = wait_tiles(ntiles);
+#pragma unroll 1
+    for (int b = 0; b < NB; ++b) {
+      cur_b = b;
+      stage_vec<kInter, kStageCopy>(c, sU, nullptr, c.wM + (size_t)b * kWordsM, E, kSiteM, nullptr, NormPairs{});
+      fma_ksplit_phase<3, kOutDown>(tiles, sU, R.begin, R.end, kDTileRows, kDRowPitch, E, false);
+    }
+    release_tiles(ntiles, tiles);
+  }
+
+  // LM head, one pass per sequence over this CTA's vocabulary rows; the
+  // per-CTA argmax of sequence b goes to its ARG words.
+  __device__ void phase_lm_nb(int step, unsigned E_x, unsigned E) {
+    const NormPairs nw = nw_pref;  // fetched in the last P5
+    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
+    const Range R = lm_rows(c.cta, c.ncta);
+#pragma unroll 1
+    for (int b = 0; b < NB; ++b) {
+      cur_b = b;
+      tc_prewait(R.begin, R.end, kLMTileRows);
+      const float ss = stage_vec<kHidden, kStageNormFrag>(c, sX, bop, c.wX + (size_t)b * kWordsX, E_x, kSiteX, red_lm, nw);
+      const float rstd = rsqrtf(ss / (float)kHidden + kRmsEps);
+      lm_best = -INFINITY;
+      lm_best_i = 0x7fffffff;
+      lm_logits = nullptr;
+      lm_pos = p.start_pos_b[b] + step;
+      const TcJob job{kTcRow, kOutLM, R.begin, R.end, kLMTileRows, rstd, E};
+      tc_phase(job, bop);
+      float best = lm_best;
+      int best_i = lm_best_i;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+        if (ov > best || (ov == best && oi < best_i)) {
+          best = ov;
+          best_i = oi;
+        }
+      }
+      if (lane == 0) {
+        c.warp_best_v[warp] = best;
+        c.warp_best_i[warp] = best_i;
+      }
+      consumer_sync();
+      if (tid == 0) {
+        unsigned bk = 0;
+        int bi = 0x7fffffff;
+        for (int q = 0; q < kConsumerWarps; ++q) {
+          const float v = c.warp_best_v[q];
+          const int i = c.warp_best_i[q];
+          if (i == 0x7fffffff) continue;
+          const unsigned k = float_order_key(v);
+          if (arg_better(k, i, bk, bi)) {
+            bk = k;
+            bi = i;
+          }
+        }
+        if (bi == 0x7fffffff) bi = R.begin;
+        uint64_t *arg = c.wArg + (size_t)b * kWordsArg;
+        put(arg + 2 * c.cta, ll_pack_u(bk, E));
+        put(arg + 2 * c.cta + 1, ll_pack_u((unsigned)bi, E));
+      }
+      consumer_sync();  // warp_best and the B operand are reused by the next pass
+    }
+    publish_kv(step);
+  }
+
+  __device__ void run_nb() {
+    const int L = p.num_layers;
+    steps_run = p.num_steps;
+    int toks[NB];
+    for (int t = 0; t < p.num_steps; ++t) {
+      c.trace_tile0 = tile;
+      nw_pref = load_norm_pairs((const __nv_bfloat16 *)p.layers[0].input_layernorm_weight, tid);
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        int tok = (t == 0) ? __ldg(p.first_tokens_b + b) : read_argmax(c, epoch_of(c, t - 1, L, L), b);
+        if (tok < 0 || tok >= kVocab) {
+          if (tid == 0) raise_error(c, QMK_ERR_TOKEN, kSiteToken);
+          tok = 0;
+        }
+        toks[b] = tok;
+      }
+      // CTA 0 records the previous step's tokens
+      if (t > 0 && c.cta == 0 && tid == 0 && p.out_log) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b) p.out_log[(size_t)(t - 1) * NB + b] = toks[b];
+      }
+      for (int l = 0; l < L; ++l) {
+        c.cur_layer = l;
+        const LDGLayerWeights w = p.layers[l];
+        const unsigned E = epoch_of(c, t, l, L);
+        phase_qkv_nb(E, l > 0 ? epoch_of(c, t, l - 1, L) : 0u, toks);
+        phase_attention(w, l, t, E);
+        phase_merge(E, l);
+        phase_o_nb(w, E);
+        phase_gu_nb(E);
+        phase_down_nb(E, l);
+      }
+      phase_lm_nb(t, epoch_of(c, t, L - 1, L), epoch_of(c, t, L, L));
+    }
+    if (c.cta == 0) {
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const int last = read_argmax(c, epoch_of(c, p.num_steps - 1, L, L), b);
+        if (tid == 0 && p.out_log) p.out_log[(size_t)(p.num_steps - 1) * NB + b] = last;
+      }
+    }
+  }
 };
 
-template <bool kFeat>
+template <bool kFeat, int NB = 1>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ int s_abort;
@@ -2103,11 +2348,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 
   if (threadIdx.x >= kConsumerThreads) {
     if ((threadIdx.x & 31) == 0) {
-      Producer<kFeat> prod(c, p);
+      Producer<kFeat, NB> prod(c, p);
       prod.run();
     }
   } else {
-    Consumer<kFeat> cons(c, p, smem);
+    Consumer<kFeat, NB> cons(c, p, smem);
     cons.run();
     cons.drain_mma();
   }
@@ -2219,6 +2464,9 @@ int prepare_device(int dev) {
                                        qmk::kSmBytes - 0);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(qmk::decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, qmk::kSmBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(qmk::decode_kernel<false, qmk::kBatchSeqs>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             qmk::kSmBytes);
   if (e != cudaSuccess)
     return set_error(QMK_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem %d): %s", qmk::kSmBytes,
                      cudaGetErrorString(e));
@@ -2401,6 +2649,92 @@ int qmk_run(const QmkRunArgs *a, cudaStream_t stream) {
   const bool feat = p.top_k > 0 || p.inv_temp > 0.f || p.trace || p.tuning || p.poll_backoff_ns;
   const void *kernel = feat ? (const void *)qmk::decode_kernel<true> : (const void *)qmk::decode_kernel<false>;
   cudaError_t e = cudaLaunchCooperativeKernel(kernel, dim3(ncta),
+                                              dim3(qmk::kThreads), kargs, qmk::kSmBytes, stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(e == cudaErrorCooperativeLaunchTooLarge ? QMK_ERR_LAUNCH : QMK_ERR_CUDA,
+                     "cooperative launch of %d x %d: %s", ncta, qmk::kThreads, cudaGetErrorString(e));
+  }
+  return clear_error();
+}
+
+static_assert(qmk::kBatchSeqs == QMK_BATCH_SEQS, "batched sequence count");
+
+int qmk_run_batch(const QmkBatchRunArgs *a, cudaStream_t stream) {
+  constexpr int NB = qmk::kBatchSeqs;
+  if (!a) return set_error(QMK_ERR_ARGS, "qmk_run_batch: null args");
+  if (!a->embed_weight || !a->layer_weights || !a->final_norm_weight || !a->lm_head_weight || !a->cos_table ||
+      !a->sin_table || !a->k_cache || !a->v_cache || !a->workspace || !a->first_tokens)
+    return set_error(QMK_ERR_ARGS, "qmk_run_batch: null pointer argument");
+  if (a->workspace_bytes < (size_t)qmk::kWorkspaceBytes)
+    return set_error(QMK_ERR_WORKSPACE, "qmk_run_batch: workspace %zu < %lld bytes", a->workspace_bytes,
+                     (long long)qmk::kWorkspaceBytes);
+  if (!aligned(a->workspace, 256)) return set_error(QMK_ERR_WORKSPACE, "qmk_run_batch: workspace misaligned");
+  if (a->num_layers < 1 || a->num_layers > qmk::kMaxLayers)
+    return set_error(QMK_ERR_ARGS, "qmk_run_batch: num_layers=%d outside [1, %d]", a->num_layers, qmk::kMaxLayers);
+  if (a->num_steps < 1) return set_error(QMK_ERR_ARGS, "qmk_run_batch: num_steps=%d", a->num_steps);
+  if (a->max_seq_len < 1) return set_error(QMK_ERR_ARGS, "qmk_run_batch: max_seq_len=%d", a->max_seq_len);
+  if (a->cache_seq_stride < (long long)a->num_layers * qmk::kNumKVHeads * a->max_seq_len * qmk::kHeadDim ||
+      a->cache_seq_stride % 8)
+    return set_error(QMK_ERR_ARGS, "qmk_run_batch: cache_seq_stride %lld too small or not 16-byte aligned",
+                     a->cache_seq_stride);
+  int max_pos = 0;
+  for (int b = 0; b < NB; ++b) {
+    const int s0 = a->start_positions[b];
+    if (s0 < 0 || (long long)s0 + a->num_steps > a->max_seq_len)
+      return set_error(QMK_ERR_ARGS, "qmk_run_batch: sequence %d: positions [%d, %d) outside [0, %d)", b, s0,
+                       s0 + a->num_steps, a->max_seq_len);
+    if (s0 + a->num_steps - 1 > max_pos) max_pos = s0 + a->num_steps - 1;
+  }
+  if (!(a->attn_scale == a->attn_scale) || a->attn_scale <= 0.f)
+    return set_error(QMK_ERR_ARGS, "qmk_run_batch: attn_scale must be positive");
+  const void *ptrs[] = {a->embed_weight, a->final_norm_weight, a->lm_head_weight, a->cos_table,
+                        a->sin_table,    a->k_cache,           a->v_cache};
+  for (const void *q : ptrs)
+    if (!aligned(q, 16)) return set_error(QMK_ERR_ARGS, "qmk_run_batch: tensor not 16-byte aligned");
+  if (!aligned(a->layer_weights, 8)) return set_error(QMK_ERR_ARGS, "qmk_run_batch: layer table misaligned");
+
+  int dev = 0;
+  if (current_device(&dev) != QMK_OK) return g_last_error;
+  int ncta;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (prepare_device(dev) != QMK_OK) return g_last_error;
+    ncta = g_devices[dev].num_sms;
+  }
+  if (ncta > qmk::kMaxCtas) ncta = qmk::kMaxCtas;
+  // attention items (NB x 8 KV heads) and merge tasks (NB x 32) one per CTA;
+  // O / down rows per CTA within the residual slots
+  if (ncta < NB * qmk::kMergeTasks || (qmk::kHidden + ncta - 1) / ncta > qmk::kMaxResRows || ncta < qmk::kMinCtas)
+    return set_error(QMK_ERR_LAUNCH, "qmk_run_batch: %d SMs < %d required", ncta, NB * qmk::kMergeTasks);
+
+  qmk::Params p;
+  memset(&p, 0, sizeof(p));
+  p.embed = (const __nv_bfloat16 *)a->embed_weight;
+  p.layers = a->layer_weights;
+  p.final_norm = (const __nv_bfloat16 *)a->final_norm_weight;
+  p.lm_head = (const __nv_bfloat16 *)a->lm_head_weight;
+  p.cos_t = (const __nv_bfloat16 *)a->cos_table;
+  p.sin_t = (const __nv_bfloat16 *)a->sin_table;
+  p.k_cache = (__nv_bfloat16 *)a->k_cache;
+  p.v_cache = (__nv_bfloat16 *)a->v_cache;
+  p.ws = (uint8_t *)a->workspace;
+  p.num_steps = a->num_steps;
+  p.num_layers = a->num_layers;
+  p.max_seq_len = a->max_seq_len;
+  p.attn_scale = a->attn_scale;
+  p.splits = qmk::attention_splits(ncta, max_pos, NB);
+  p.out_log = a->output_log;
+  p.status = a->status;
+  p.timeout_ns = a->timeout_ns ? a->timeout_ns : qmk::kDefaultTimeoutNs;
+  p.eos_token = -1;
+  for (int b = 0; b < NB; ++b) p.start_pos_b[b] = a->start_positions[b];
+  p.start_pos = a->start_positions[0];
+  p.cache_seq_stride = a->cache_seq_stride;
+  p.first_tokens_b = a->first_tokens;
+
+  void *kargs[] = {&p};
+  cudaError_t e = cudaLaunchCooperativeKernel((const void *)qmk::decode_kernel<false, NB>, dim3(ncta),
                                               dim3(qmk::kThreads), kargs, qmk::kSmBytes, stream);
   if (e != cudaSuccess) {
     cudaGetLastError();

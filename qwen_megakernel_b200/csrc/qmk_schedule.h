@@ -28,6 +28,11 @@ constexpr int kMaxLayers = 64;
 
 constexpr int kMaxCtas = 160;
 constexpr int kMinCtas = 64;
+// Sequences of the batched instance (qmk_run_batch): every phase runs once
+// per sequence on the same weight tiles; attention items and merge tasks are
+// per (sequence, ...).
+constexpr int kBatchSeqs = 4;
+constexpr int kMaxSeqs = kBatchSeqs;
 constexpr int kMaxSplits = 18;
 constexpr int kMergeTasks = 32;                     // 16 q heads x 2 halves
 constexpr int kMergeDims = kHeadDim / 2;            // 64 dims per merge task
@@ -67,15 +72,17 @@ QMK_HD Range gu_rows(int cta, int ncta) { return split_rows(kInter, cta, ncta); 
 QMK_HD Range d_rows(int cta, int ncta) { return split_rows(kHidden, cta, ncta); }
 QMK_HD Range lm_rows(int cta, int ncta) { return split_rows(kVocab, cta, ncta); }
 
-// Attention items: item i = g * splits + s lives on CTA i.
-QMK_HD int item_of_cta(int cta, int splits) {
-  return (cta < kNumKVHeads * splits) ? cta : -1;
+// Attention items: item i = (b * 8 + g) * splits + s (sequence b of nb) lives
+// on CTA i.
+QMK_HD int item_of_cta(int cta, int splits, int nb = 1) {
+  return (cta < nb * kNumKVHeads * splits) ? cta : -1;
 }
 
-// Merge task j lives on CTA ncta-1-j: q head j/2, dims [(j%2)*64, +64).
-QMK_HD int merge_task_of_cta(int cta, int ncta) {
+// Merge task j lives on CTA ncta-1-j: sequence j/32, q head (j%32)/2, dims
+// [(j%2)*64, +64).
+QMK_HD int merge_task_of_cta(int cta, int ncta, int nb = 1) {
   int j = ncta - 1 - cta;
-  return (j >= 0 && j < kMergeTasks) ? j : -1;
+  return (j >= 0 && j < nb * kMergeTasks) ? j : -1;
 }
 
 // Previous positions [0, prev) of a KV head are cut into `splits` chunks.
@@ -93,9 +100,9 @@ QMK_HD Range kv_chunk(int prev, int s, int splits) {
 
 // Splits per KV head for a launch whose largest "previous positions" count is
 // max_prev: ~64 positions per split, at most kMaxSplits and at most ncta/8.
-QMK_HD int attention_splits(int ncta, int max_prev) {
+QMK_HD int attention_splits(int ncta, int max_prev, int nb = 1) {
   int s = (max_prev + 63) / 64;
-  int cap = ncta / kNumKVHeads;
+  int cap = ncta / (kNumKVHeads * nb);
   if (cap > kMaxSplits) cap = kMaxSplits;
   if (s > cap) s = cap;
   if (s < 1) s = 1;
@@ -104,10 +111,12 @@ QMK_HD int attention_splits(int ncta, int max_prev) {
 
 // Workspace layout (bytes).  Control block first, then the 8-byte dataflow
 // ("LL": value | flag << 32) buffers.
-constexpr int kCtrlBytes = 8192;
+// Per-sequence buffers are kMaxSeqs consecutive copies (sequence b at b x
+// the per-sequence size).
+constexpr int kCtrlBytes = 16384;
 constexpr int kWordsX = kHidden;
 constexpr int kWordsQKV = kQKVRows;
-constexpr int kWordsPart = kNumKVHeads * kMaxSplits * kPartWords;
+constexpr int kWordsPart = kMaxCtas * kPartWords;  // one PART record per attention item (<= one per CTA)
 constexpr int kWordsAtt = kQSize;
 constexpr int kWordsA = kHidden;
 constexpr int kWordsM = kInter;
@@ -115,13 +124,13 @@ constexpr int kWordsArg = 2 * kMaxCtas;
 constexpr int kMaxTopK = 64;                       // top-k sampling: candidate keys per CTA
 constexpr int kWordsTopk = kMaxTopK * kMaxCtas;
 constexpr long long kOffX = kCtrlBytes;
-constexpr long long kOffQKV = kOffX + 8LL * kWordsX;
-constexpr long long kOffPart = kOffQKV + 8LL * kWordsQKV;
+constexpr long long kOffQKV = kOffX + 8LL * kMaxSeqs * kWordsX;
+constexpr long long kOffPart = kOffQKV + 8LL * kMaxSeqs * kWordsQKV;
 constexpr long long kOffAtt = kOffPart + 8LL * kWordsPart;
-constexpr long long kOffA = kOffAtt + 8LL * kWordsAtt;
-constexpr long long kOffM = kOffA + 8LL * kWordsA;
-constexpr long long kOffArg = kOffM + 8LL * kWordsM;
-constexpr long long kOffTopk = kOffArg + 8LL * kWordsArg;
+constexpr long long kOffA = kOffAtt + 8LL * kMaxSeqs * kWordsAtt;
+constexpr long long kOffM = kOffA + 8LL * kMaxSeqs * kWordsA;
+constexpr long long kOffArg = kOffM + 8LL * kMaxSeqs * kWordsM;
+constexpr long long kOffTopk = kOffArg + 8LL * kMaxSeqs * kWordsArg;
 constexpr long long kOffLLEnd = kOffTopk + 8LL * kWordsTopk;  // end of the dataflow words
 constexpr long long kWorkspaceBytes = (kOffLLEnd + 4095) / 4096 * 4096;
 
@@ -133,7 +142,7 @@ struct Ctrl {
   unsigned err_info;
   unsigned launches;
   unsigned pad[27];
-  unsigned kv_ready[kMaxLayers * kNumKVHeads];  // epoch of the last K/V row written
+  unsigned kv_ready[kMaxSeqs * kMaxLayers * kNumKVHeads];  // [seq][layer][kv head]: epoch of the last K/V row written
 };
 static_assert(sizeof(Ctrl) <= kCtrlBytes, "control block too large");
 

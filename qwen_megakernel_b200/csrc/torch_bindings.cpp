@@ -11,6 +11,8 @@
 // Added operators (no reference counterpart):
 //   run(...)             -> qmk_run with a caller-owned workspace, optional
 //                           forced-token stream, fp32 logits, status block, trace
+//   run_batch(...)       -> qmk_run_batch: QMK_BATCH_SEQS sequences decoded
+//                           together in the persistent kernel
 //   workspace_bytes()    -> qmk_workspace_bytes
 //   workspace_init(ws)   -> qmk_workspace_init
 //   default_status()     -> qmk_read_default_status (after a synchronize)
@@ -310,6 +312,75 @@ void run(torch::Tensor workspace, torch::Tensor embed_weight, torch::Tensor laye
   raise_if_error(qmk_run(&a, c10::cuda::getCurrentCUDAStream().stream()));
 }
 
+// Batched decode in the persistent kernel: k_cache / v_cache are
+// [QMK_BATCH_SEQS, num_layers, 8, max_seq_len, 128] (one reference-layout
+// cache per sequence), first_tokens int32 [QMK_BATCH_SEQS] on the device,
+// output_log int32 [num_steps, QMK_BATCH_SEQS].
+void run_batch(torch::Tensor workspace, torch::Tensor embed_weight, torch::Tensor layer_weights_packed,
+               torch::Tensor final_norm_weight, torch::Tensor lm_head_weight, torch::Tensor cos_table,
+               torch::Tensor sin_table, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor first_tokens,
+               std::vector<int64_t> start_positions, int64_t num_steps, int64_t num_layers, int64_t max_seq_len,
+               double attn_scale, std::optional<torch::Tensor> output_log, std::optional<torch::Tensor> status,
+               int64_t timeout_ns) {
+  QMK_CHECK(num_steps >= 1, "num_steps must be >= 1");
+  QMK_CHECK((int)start_positions.size() == QMK_BATCH_SEQS, "start_positions must have %d entries", QMK_BATCH_SEQS);
+  QMK_CHECK(k_cache.dim() == 5 && k_cache.size(0) == QMK_BATCH_SEQS && v_cache.sizes() == k_cache.sizes(),
+            "k_cache / v_cache must be [%d, num_layers, 8, max_seq_len, 128]", QMK_BATCH_SEQS);
+  QMK_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "caches must be contiguous");
+  int64_t last = 0;
+  for (int64_t s0 : start_positions) {
+    QMK_CHECK(s0 >= 0, "start positions must be >= 0");
+    last = std::max<int64_t>(last, s0 + num_steps - 1);
+  }
+  check_model(embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight, cos_table, sin_table,
+              k_cache.select(0, 0), v_cache.select(0, 0), num_layers, last, max_seq_len);
+  check_cuda(workspace, "workspace");
+  check_same_device(workspace, embed_weight, "workspace");
+  QMK_CHECK(workspace.nbytes() >= qmk_workspace_bytes(), "workspace holds %lld bytes; needs %lld",
+            (ll)workspace.nbytes(), (ll)qmk_workspace_bytes());
+  check_dtype(first_tokens, torch::kInt32, "first_tokens", "int32");
+  check_same_device(first_tokens, embed_weight, "first_tokens");
+  QMK_CHECK(first_tokens.numel() >= QMK_BATCH_SEQS, "first_tokens must have %d elements", QMK_BATCH_SEQS);
+  QmkBatchRunArgs a;
+  memset(&a, 0, sizeof(a));
+  if (output_log.has_value()) {
+    check_dtype(*output_log, torch::kInt32, "output_log", "int32");
+    check_same_device(*output_log, embed_weight, "output_log");
+    QMK_CHECK(output_log->numel() >= num_steps * QMK_BATCH_SEQS, "output_log must have >= num_steps * %d elements",
+              QMK_BATCH_SEQS);
+    a.output_log = static_cast<int *>(output_log->data_ptr());
+  }
+  if (status.has_value()) {
+    const auto &st = *status;
+    QMK_CHECK(!st.is_cuda() && st.is_pinned(), "status must be a pinned CPU tensor");
+    QMK_CHECK(st.nbytes() >= sizeof(QmkStatus), "status must hold >= %d bytes", (int)sizeof(QmkStatus));
+    void *dev = nullptr;
+    cudaError_t e = cudaHostGetDevicePointer(&dev, st.data_ptr(), 0);
+    QMK_CHECK(e == cudaSuccess, "status: cudaHostGetDevicePointer: %s", cudaGetErrorString(e));
+    a.status = static_cast<QmkStatus *>(dev);
+  }
+  a.embed_weight = embed_weight.data_ptr();
+  a.layer_weights = reinterpret_cast<const LDGLayerWeights *>(layer_weights_packed.data_ptr());
+  a.final_norm_weight = final_norm_weight.data_ptr();
+  a.lm_head_weight = lm_head_weight.data_ptr();
+  a.cos_table = cos_table.data_ptr();
+  a.sin_table = sin_table.data_ptr();
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.cache_seq_stride = k_cache.stride(0);
+  a.workspace = workspace.data_ptr();
+  a.workspace_bytes = workspace.nbytes();
+  a.first_tokens = static_cast<const int *>(first_tokens.data_ptr());
+  for (int b = 0; b < QMK_BATCH_SEQS; ++b) a.start_positions[b] = (int)start_positions[b];
+  a.num_steps = (int)num_steps;
+  a.num_layers = (int)num_layers;
+  a.max_seq_len = (int)max_seq_len;
+  a.attn_scale = (float)attn_scale;
+  a.timeout_ns = (unsigned long long)std::max<int64_t>(timeout_ns, 0);
+  c10::cuda::CUDAGuard guard(embed_weight.device());
+  raise_if_error(qmk_run_batch(&a, c10::cuda::getCurrentCUDAStream().stream()));
+}
+
 // Token-parallel forward (prefill / batched decode): qmk_batch_forward.
 // layer_ptrs: the num_layers * 11 device pointers in LDGLayerWeights order
 // (the GEMMs are launched from the host, so the table is passed by value).
@@ -472,6 +543,14 @@ TORCH_LIBRARY(qwen_megakernel_C, ops) {
       "int trace_step=0, int poll_backoff_ns=0, int tuning=0, float temperature=0.0, int seed=0, "
       "int stop_at_eos=0, int eos_token=0, Tensor? steps_done=None, int top_k=0) -> ()");
   ops.impl("run", torch::kCUDA, &run);
+
+  ops.def(
+      "run_batch(Tensor workspace, Tensor embed_weight, Tensor layer_weights_packed, "
+      "Tensor final_norm_weight, Tensor lm_head_weight, Tensor cos_table, Tensor sin_table, "
+      "Tensor k_cache, Tensor v_cache, Tensor first_tokens, int[] start_positions, int num_steps, "
+      "int num_layers, int max_seq_len, float attn_scale, Tensor? output_log, Tensor? status, "
+      "int timeout_ns=0) -> ()");
+  ops.impl("run_batch", torch::kCUDA, &run_batch);
 
   ops.def(
       "batch_forward(Tensor workspace, Tensor embed_weight, int[] layer_ptrs, int[] fused_ptrs, "
