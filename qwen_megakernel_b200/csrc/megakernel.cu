@@ -908,8 +908,7 @@ struct Producer {
         trace_stamp(c, true, l * 16 + 13);
       }
       trace_stamp(c, true, p.num_layers * 16 + 3);
-      for (int b = 0; b < NB; ++b)  // one LM-head pass per sequence
-        rows(p.lm_head, kHidden * 2, lm_rows(c.cta, c.ncta), kLMTileRows, kHidden * 2);
+      rows(p.lm_head, kHidden * 2, lm_rows(c.cta, c.ncta), kLMTileRows, kHidden * 2);
       trace_stamp(c, true, p.num_layers * 16 + 4);
     }
     // Drain: the last tile issued into each slot must land before the CTA exits.
@@ -2185,60 +2184,108 @@ struct Consumer {
     release_tiles(ntiles, tiles);
   }
 
-  // LM head, one pass per sequence over this CTA's vocabulary rows; the
-  // per-CTA argmax of sequence b goes to its ARG words.
+  // LM head of all NB sequences in one pass over this CTA's vocabulary rows,
+  // on the CUDA cores (the tensor-core LM head takes one vector): the NB
+  // inputs x_b * w (final norm weight) sit side by side in shared memory
+  // (the U and x*w regions, contiguous); as each 16-row tile lands, warp w
+  // takes rows w, w + 7, w + 14 and multiplies every row with all NB
+  // inputs (each weight read once from shared memory), a transposing
+  // butterfly leaves sequence b's row sum in lane 8b, which keeps that
+  // sequence's running argmax.  The weights cross HBM once per step.
   __device__ void phase_lm_nb(int step, unsigned E_x, unsigned E) {
+    static_assert(NB == 4, "one lane group of 8 per sequence");
+    static_assert(kSmXW == kSmU + 4 * kInter && NB * kHidden <= kInter + kHidden, "LM-head inputs");
     const NormPairs nw = nw_pref;  // fetched in the last P5
-    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
-    const Range R = lm_rows(c.cta, c.ncta);
+    float *sV = sU;                // [NB][kHidden]
+    float rstd_mine = 0.f;         // rstd of this lane's sequence (lane >> 3)
 #pragma unroll 1
     for (int b = 0; b < NB; ++b) {
-      cur_b = b;
-      tc_prewait(R.begin, R.end, kLMTileRows);
-      const float ss = stage_vec<kHidden, kStageNormFrag>(c, sX, bop, c.wX + (size_t)b * kWordsX, E_x, kSiteX, red_lm, nw);
-      const float rstd = rsqrtf(ss / (float)kHidden + kRmsEps);
-      lm_best = -INFINITY;
-      lm_best_i = 0x7fffffff;
-      lm_logits = nullptr;
-      lm_pos = p.start_pos_b[b] + step;
-      const TcJob job{kTcRow, kOutLM, R.begin, R.end, kLMTileRows, rstd, E};
-      tc_phase(job, bop);
-      float best = lm_best;
-      int best_i = lm_best_i;
+      // alternate reduction slots: back-to-back calls, one barrier each
+      const float ss = stage_vec<kHidden, kStageNorm>(c, sX, reinterpret_cast<uint8_t *>(sV + b * kHidden),
+                                                      c.wX + (size_t)b * kWordsX, E_x, kSiteX,
+                                                      (b & 1) ? red_e : red_lm, nw);
+      if ((lane >> 3) == b) rstd_mine = rsqrtf(ss / (float)kHidden + kRmsEps);
+    }
+    const Range R = lm_rows(c.cta, c.ncta);
+    const int ntiles = (R.end - R.begin + kLMTileRows - 1) / kLMTileRows;
+    lm_best = -INFINITY;
+    lm_best_i = 0x7fffffff;
+    const int mb = lane >> 3;  // sequence whose sums this lane receives
+#pragma unroll 1
+    for (int t = 0; t < ntiles; ++t) {
+      const int r0 = R.begin + t * kLMTileRows;
+      const int n = min(kLMTileRows, R.end - r0);
+      const bool ok = wait_full(c, tile);
+      const uint8_t *tb = slot_ptr(c, tile) + 8 * lane;
+      float acc[3][NB][2];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-        if (ov > best || (ov == best && oi < best_i)) {
-          best = ov;
-          best_i = oi;
-        }
-      }
-      if (lane == 0) {
-        c.warp_best_v[warp] = best;
-        c.warp_best_i[warp] = best_i;
-      }
-      consumer_sync();
-      if (tid == 0) {
-        unsigned bk = 0;
-        int bi = 0x7fffffff;
-        for (int q = 0; q < kConsumerWarps; ++q) {
-          const float v = c.warp_best_v[q];
-          const int i = c.warp_best_i[q];
-          if (i == 0x7fffffff) continue;
-          const unsigned k = float_order_key(v);
-          if (arg_better(k, i, bk, bi)) {
-            bk = k;
-            bi = i;
+      for (int r = 0; r < 3; ++r)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) acc[r][b][0] = acc[r][b][1] = 0.f;
+      if (ok) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint2 wv[3];
+#pragma unroll
+          for (int r = 0; r < 3; ++r) {
+            const int i = warp + kConsumerWarps * r;
+            wv[r] = *reinterpret_cast<const uint2 *>(tb + (size_t)(i < n ? i : warp) * (kHidden * 2) + 256 * j);
+          }
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            const float4 xv = reinterpret_cast<const float4 *>(sV + b * kHidden)[lane + 32 * j];
+#pragma unroll
+            for (int r = 0; r < 3; ++r) dot4(acc[r][b][0], acc[r][b][1], wv[r], xv);
           }
         }
-        if (bi == 0x7fffffff) bi = R.begin;
-        uint64_t *arg = c.wArg + (size_t)b * kWordsArg;
-        put(arg + 2 * c.cta, ll_pack_u(bk, E));
-        put(arg + 2 * c.cta + 1, ll_pack_u((unsigned)bi, E));
       }
-      consumer_sync();  // warp_best and the B operand are reused by the next pass
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&c.empty[tile % kNumSlots]);
+      ++tile;
+#pragma unroll
+      for (int r = 0; r < 3; ++r) {
+        float v[4];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) v[b] = acc[r][b][0] + acc[r][b][1];
+        const float sum = reduce4_transpose(v);  // lane 8b: sequence b (its row order is 2 ((l >> 4) & 1) + ((l >> 3) & 1) = l >> 3)
+        const int i = warp + kConsumerWarps * r;
+        const int row = r0 + i;
+        if (ok && (lane & 7) == 0 && i < n) {
+          const float y = sum * rstd_mine;
+          if (y > lm_best || (y == lm_best && row < lm_best_i)) {
+            lm_best = y;
+            lm_best_i = row;
+          }
+        }
+      }
     }
+    // per sequence: CTA argmax over the warps' lanes 8b
+    float *bv = sPart;  // [kConsumerWarps][NB] (the K-split partials are free here)
+    int *bi = reinterpret_cast<int *>(sPart + 64);
+    static_assert(kConsumerWarps * NB <= 64, "argmax slots");
+    if ((lane & 7) == 0) {
+      bv[warp * NB + mb] = lm_best;
+      bi[warp * NB + mb] = lm_best_i;
+    }
+    consumer_sync();
+    if (tid < NB) {
+      unsigned bk = 0;
+      int bidx = 0x7fffffff;
+      for (int q = 0; q < kConsumerWarps; ++q) {
+        const int i = bi[q * NB + tid];
+        if (i == 0x7fffffff) continue;
+        const unsigned k = float_order_key(bv[q * NB + tid]);
+        if (arg_better(k, i, bk, bidx)) {
+          bk = k;
+          bidx = i;
+        }
+      }
+      if (bidx == 0x7fffffff) bidx = R.begin;
+      uint64_t *arg = c.wArg + (size_t)tid * kWordsArg;
+      put(arg + 2 * c.cta, ll_pack_u(bk, E));
+      put(arg + 2 * c.cta + 1, ll_pack_u((unsigned)bidx, E));
+    }
+    consumer_sync();  // the argmax slots and the inputs are reused next step
     publish_kv(step);
   }
 
