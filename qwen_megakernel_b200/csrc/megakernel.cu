@@ -2088,27 +2088,100 @@ struct Consumer {
   // merge tasks are per (sequence, ...); the LM head runs one pass per
   // sequence over the same rows.
 
-  // Layer-0 input: the embedding row of `tok` into sX; returns its sum of
-  // squares (a consumer barrier inside).
-  __device__ float embed_row(int tok) {
+  // Layer-0 input: the embedding row of `tok` into dst; returns its sum of
+  // squares (one consumer barrier, reduction slots `red`).
+  __device__ float embed_row(int tok, float *dst, float *red) {
     const __nv_bfloat16 *erow = p.embed + (size_t)tok * kHidden;
     float ss = 0.f;
     for (int i = tid; i < kHidden / 4; i += kConsumerThreads) {
       const uint2 v = __ldg(reinterpret_cast<const uint2 *>(erow) + i);
       const float e0 = bf_lo(v.x), e1 = bf_hi(v.x), e2 = bf_lo(v.y), e3 = bf_hi(v.y);
-      sX[4 * i + 0] = e0;
-      sX[4 * i + 1] = e1;
-      sX[4 * i + 2] = e2;
-      sX[4 * i + 3] = e3;
+      dst[4 * i + 0] = e0;
+      dst[4 * i + 1] = e1;
+      dst[4 * i + 2] = e2;
+      dst[4 * i + 3] = e3;
       ss += e0 * e0 + e1 * e1 + e2 * e2 + e3 * e3;
     }
     ss = warp_sum(ss);
-    if (lane == 0) red_e[warp] = ss;
+    if (lane == 0) red[warp] = ss;
     consumer_sync();
     float total = 0.f;
 #pragma unroll
-    for (int q = 0; q < kConsumerWarps; ++q) total += red_e[q];
+    for (int q = 0; q < kConsumerWarps; ++q) total += red[q];
     return total;
+  }
+
+  // Inputs of a normalized row phase for all NB sequences, staged side by
+  // side: raw x_b at sX + b * kHidden (the X, A and ATT regions, 16 KB) and
+  // x_b * w at sU + b * kHidden (the U and x*w regions, 16 KB).
+  static_assert(kSmA == kSmX + 4 * kHidden && kSmAtt == kSmA + 4 * kHidden && kSmU == kSmAtt + 4 * kQSize &&
+                    kSmXW == kSmU + 4 * kInter,
+                "activation regions are contiguous");
+  static_assert(NB * kHidden <= 2 * kHidden + kQSize && NB * kHidden <= kInter + kHidden, "staged inputs fit");
+
+  // Row GEMV of all NB staged inputs in one pass over the phase's tiles:
+  // warp w takes rows w, w + 7, ..., MR at a time, each weight (8 bytes per
+  // lane per j) read once from shared memory and multiplied with the NB
+  // inputs; per row a transposing butterfly leaves sequence b's sum in
+  // lane 8b, which scales it by its own 1/rms and emits it.
+  template <int OUT, int MR>
+  __device__ void fma_rows_nb(bool ok, const float *xw, float scale_mine, int r0, int r1, int tile_rows, int pitch,
+                              unsigned E) {
+    static_assert(NB == 4, "one lane group of 8 per sequence");
+    constexpr bool kGU = (OUT == kOutGU);
+    const int n = r1 - r0;
+    const int mb = lane >> 3;
+    const TcJob job{kTcRow, OUT, r0, r1, tile_rows, scale_mine, E};
+    for (int i0 = warp; ok && i0 < n; i0 += kConsumerWarps * MR) {
+      const uint8_t *rp[MR];
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        const int i = i0 + kConsumerWarps * r;
+        rp[r] = row_ptr(i < n ? i : i0, tile_rows, pitch, 8 * lane);
+      }
+      float acc[MR][NB][2], accu[kGU ? MR : 1][NB][2];
+#pragma unroll
+      for (int r = 0; r < MR; ++r)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          acc[r][b][0] = acc[r][b][1] = 0.f;
+          accu[kGU ? r : 0][b][0] = accu[kGU ? r : 0][b][1] = 0.f;
+        }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint2 w[MR], u[kGU ? MR : 1];
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+          w[r] = *reinterpret_cast<const uint2 *>(rp[r] + 256 * j);
+          if (kGU) u[kGU ? r : 0] = *reinterpret_cast<const uint2 *>(rp[r] + 2048 + 256 * j);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          const float4 x = reinterpret_cast<const float4 *>(xw + b * kHidden)[lane + 32 * j];
+#pragma unroll
+          for (int r = 0; r < MR; ++r) {
+            dot4(acc[r][b][0], acc[r][b][1], w[r], x);
+            if (kGU) dot4(accu[kGU ? r : 0][b][0], accu[kGU ? r : 0][b][1], u[kGU ? r : 0], x);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        float v[4], v2[4];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          v[b] = acc[r][b][0] + acc[r][b][1];
+          v2[b] = kGU ? accu[kGU ? r : 0][b][0] + accu[kGU ? r : 0][b][1] : 0.f;
+        }
+        const float sum = reduce4_transpose(v);  // lane 8b: sequence b
+        const float sum2 = kGU ? reduce4_transpose(v2) : 0.f;
+        const int i = i0 + kConsumerWarps * r;
+        if ((lane & 7) == 0 && i < n) {
+          cur_b = mb;
+          tc_emit(job, r0 + i, sum, sum2);
+        }
+      }
+    }
   }
 
   __device__ void phase_qkv_nb(unsigned E, unsigned x_flag, const int (&toks)[NB]) {
@@ -2116,24 +2189,26 @@ struct Consumer {
     const Range R = qkv_rows(c.cta, c.ncta), Ro = o_rows(c.cta, c.ncta);
     const int ntiles = tiles_of(R, kQKVTileRows);
     const bool tiles = wait_tiles(ntiles);
+    float scale_mine = 0.f;  // 1/rms of this lane's sequence (lane >> 3)
 #pragma unroll 1
     for (int b = 0; b < NB; ++b) {
-      cur_b = b;
-      if (b > 0) consumer_sync();  // every warp has read sequence b-1's sXW
-      float x_ss;
+      // back-to-back stagings alternate their reduction slots
+      float ss;
       if (x_flag) {
-        x_ss = stage_vec<kHidden, kStageNorm>(c, sX, reinterpret_cast<uint8_t *>(sXW), c.wX + (size_t)b * kWordsX,
-                                              x_flag, kSiteX, red_x, nw);
+        ss = stage_vec<kHidden, kStageNorm>(c, sX + b * kHidden, reinterpret_cast<uint8_t *>(sU + b * kHidden),
+                                            c.wX + (size_t)b * kWordsX, x_flag, kSiteX, (b & 1) ? red_e : red_x, nw);
       } else {
-        x_ss = embed_row(toks[b]);
-        build_norm_xw(sXW, sX, nw, tid);
-        consumer_sync();
+        ss = embed_row(toks[b], sX + b * kHidden, (b & 1) ? red_e : red_x);
+        build_norm_xw(sU + b * kHidden, sX + b * kHidden, nw, tid);
       }
-      if (tid < Ro.end - Ro.begin) sResO[b * kMaxResRows + tid] = sX[Ro.begin + tid];
-      fma_rows_phase<kOutQKV, 4>(tiles, sXW, R.begin, R.end, kQKVTileRows, 2048,
-                                 rsqrtf(x_ss / (float)kHidden + kRmsEps), E, false);
+      if ((lane >> 3) == b) scale_mine = rsqrtf(ss / (float)kHidden + kRmsEps);
     }
+    if (!x_flag) consumer_sync();  // x * w of the embeddings
+    const int no = Ro.end - Ro.begin;
+    if (tid < NB * no) sResO[(tid / no) * kMaxResRows + tid % no] = sX[(tid / no) * kHidden + Ro.begin + tid % no];
+    fma_rows_nb<kOutQKV, 4>(tiles, sU, scale_mine, R.begin, R.end, kQKVTileRows, 2048, E);
     release_tiles(ntiles, tiles);
+    consumer_sync();  // the next phase writes its scratch over the staged inputs
   }
 
   __device__ void phase_o_nb(const LDGLayerWeights &w, unsigned E) {
@@ -2156,17 +2231,18 @@ struct Consumer {
     const Range R = gu_rows(c.cta, c.ncta), Rd = d_rows(c.cta, c.ncta);
     const int ntiles = tiles_of(R, kGUTileRows);
     const bool tiles = wait_tiles(ntiles);
+    float scale_mine = 0.f;
 #pragma unroll 1
     for (int b = 0; b < NB; ++b) {
-      cur_b = b;
-      if (b > 0) consumer_sync();  // every warp has read sequence b-1's sXW
-      const float ss = stage_vec<kHidden, kStageNorm>(c, sA, reinterpret_cast<uint8_t *>(sXW),
-                                                      c.wA + (size_t)b * kWordsA, E, kSiteA, red_a, nw);
-      if (tid < Rd.end - Rd.begin) sResD[b * kMaxResRows + tid] = sA[Rd.begin + tid];
-      fma_rows_phase<kOutGU, 3>(tiles, sXW, R.begin, R.end, kGUTileRows, 4096, rsqrtf(ss / (float)kHidden + kRmsEps),
-                                E, false);
+      const float ss = stage_vec<kHidden, kStageNorm>(c, sX + b * kHidden, reinterpret_cast<uint8_t *>(sU + b * kHidden),
+                                                      c.wA + (size_t)b * kWordsA, E, kSiteA, (b & 1) ? red_e : red_a, nw);
+      if ((lane >> 3) == b) scale_mine = rsqrtf(ss / (float)kHidden + kRmsEps);
     }
+    const int nd = Rd.end - Rd.begin;
+    if (tid < NB * nd) sResD[(tid / nd) * kMaxResRows + tid % nd] = sX[(tid / nd) * kHidden + Rd.begin + tid % nd];
+    fma_rows_nb<kOutGU, 3>(tiles, sU, scale_mine, R.begin, R.end, kGUTileRows, 4096, E);
     release_tiles(ntiles, tiles);
+    consumer_sync();  // the next phase stages over the inputs
   }
 
   __device__ void phase_down_nb(unsigned E, int l) {
