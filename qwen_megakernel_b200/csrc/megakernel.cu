@@ -2184,6 +2184,77 @@ struct Consumer {
     }
   }
 
+  // K-split GEMV of all NB staged inputs (x_b at xin + b * K, K = 1024 KC)
+  // in one pass: the 128-element blocks of K go round-robin to the warps,
+  // every warp multiplies its blocks of every row with the NB inputs (each
+  // weight read once), per row a transposing butterfly leaves sequence b's
+  // partial in lane 8b, the partials of all rows and sequences meet in
+  // shared memory behind one barrier, and thread (row, b) adds its row's
+  // partials in warp order and emits.  Rows per CTA <= kKsplitGroupRows.
+  template <int KC, int OUT>
+  __device__ void fma_ksplit_nb(bool ok, const float *xin, int r0, int r1, int tile_rows, int pitch, unsigned E) {
+    static_assert(NB == 4, "one lane group of 8 per sequence");
+    constexpr int K = 1024 * KC;
+    constexpr int kBlocks = 8 * KC;
+    constexpr int kMine = (kBlocks + kConsumerWarps - 1) / kConsumerWarps;
+    constexpr int RB = kKsplitRows;
+    constexpr int RG = kKsplitGroupRows;
+    static_assert(kConsumerWarps * RG * NB <= 2 * 16 * RG, "partials fit the K-split slots");
+    const TcJob job{kTcRow, OUT, r0, r1, tile_rows, 1.f, E};
+    const int n = r1 - r0;  // <= RG (checked on the host)
+    float *part = sPart;    // [warp][row][b]
+    float4 xv[kMine][NB];
+#pragma unroll
+    for (int q = 0; q < kMine; ++q) {
+      const int blk = warp + kConsumerWarps * q;
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+        xv[q][b] = (blk < kBlocks) ? reinterpret_cast<const float4 *>(xin + b * K)[lane + 32 * blk]
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int i0 = 0; i0 < n; i0 += RB) {
+      float acc[RB][NB][2];
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) acc[r][b][0] = acc[r][b][1] = 0.f;
+      if (ok) {
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (i0 + r < n) {
+            const uint8_t *rp = row_ptr(i0 + r, tile_rows, pitch, 8 * lane);
+#pragma unroll
+            for (int q = 0; q < kMine; ++q) {
+              const int blk = warp + kConsumerWarps * q;
+              if (blk < kBlocks) {
+                const uint2 wv = *reinterpret_cast<const uint2 *>(rp + 256 * blk);
+#pragma unroll
+                for (int b = 0; b < NB; ++b) dot4(acc[r][b][0], acc[r][b][1], wv, xv[q][b]);
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        float v[4];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) v[b] = acc[r][b][0] + acc[r][b][1];
+        const float wsum = reduce4_transpose(v);  // lane 8b: sequence b
+        if ((lane & 7) == 0 && i0 + r < n) part[(warp * RG + i0 + r) * NB + (lane >> 3)] = wsum;
+      }
+    }
+    consumer_sync();
+    if (ok && tid < n * NB) {
+      const int i = tid / NB, b = tid % NB;
+      float sum = 0.f;
+#pragma unroll
+      for (int q = 0; q < kConsumerWarps; ++q) sum += part[(q * RG + i) * NB + b];
+      cur_b = b;
+      tc_emit(job, r0 + i, sum, 0.f);
+    }
+  }
+
   __device__ void phase_qkv_nb(unsigned E, unsigned x_flag, const int (&toks)[NB]) {
     const NormPairs nw = nw_pref;
     const Range R = qkv_rows(c.cta, c.ncta), Ro = o_rows(c.cta, c.ncta);
@@ -2216,13 +2287,13 @@ struct Consumer {
     const Range R = o_rows(c.cta, c.ncta);
     const int ntiles = tiles_of(R, kOTileRows);
     const bool tiles = wait_tiles(ntiles);
+    // the NB attention outputs side by side over all activation regions (32 KB)
+    static_assert(NB * kQSize * 4 == kSmMisc - kSmX, "attention outputs fill the activation regions");
 #pragma unroll 1
-    for (int b = 0; b < NB; ++b) {
-      cur_b = b;
-      // (the K-split phase's barrier comes after every warp read its inputs)
-      stage_vec<kQSize, kStageCopy>(c, sAtt, nullptr, c.wAtt + (size_t)b * kWordsAtt, E, kSiteAtt, nullptr, NormPairs{});
-      fma_ksplit_phase<2, kOutO>(tiles, sAtt, R.begin, R.end, kOTileRows, kQSize * 2, E, false);
-    }
+    for (int b = 0; b < NB; ++b)
+      stage_vec<kQSize, kStageCopy>(c, sX + b * kQSize, nullptr, c.wAtt + (size_t)b * kWordsAtt, E, kSiteAtt, nullptr,
+                                    NormPairs{});
+    fma_ksplit_nb<2, kOutO>(tiles, sX, R.begin, R.end, kOTileRows, kQSize * 2, E);
     release_tiles(ntiles, tiles);
   }
 
