@@ -2184,40 +2184,40 @@ struct Consumer {
     }
   }
 
-  // K-split GEMV of all NB staged inputs (x_b at xin + b * K, K = 1024 KC)
-  // in one pass: the 128-element blocks of K go round-robin to the warps,
-  // every warp multiplies its blocks of every row with the NB inputs (each
-  // weight read once), per row a transposing butterfly leaves sequence b's
-  // partial in lane 8b, the partials of all rows and sequences meet in
-  // shared memory behind one barrier, and thread (row, b) adds its row's
-  // partials in warp order and emits.  Rows per CTA <= kKsplitGroupRows.
-  template <int KC, int OUT>
-  __device__ void fma_ksplit_nb(bool ok, const float *xin, int r0, int r1, int tile_rows, int pitch, unsigned E) {
-    static_assert(NB == 4, "one lane group of 8 per sequence");
+  // K-split GEMV of NV staged inputs (x_j at xin + j * K, K = 1024 KC;
+  // sequences b0 .. b0 + NV - 1) in one pass: the 128-element blocks of K go
+  // round-robin to the warps, every warp multiplies its blocks of every row
+  // with the NV inputs (each weight read once), per row a transposing
+  // butterfly leaves input j's partial in lane 8j, the partials of all rows
+  // and inputs meet in shared memory (`part`) behind one barrier, and thread
+  // (row, j) adds its row's partials in warp order and emits.  Rows per CTA
+  // <= kKsplitGroupRows.
+  template <int KC, int OUT, int NV>
+  __device__ void fma_ksplit_nb(bool ok, const float *xin, int b0, float *part, int r0, int r1, int tile_rows,
+                                int pitch, unsigned E) {
+    static_assert(NV >= 1 && NV <= 4, "one lane group of 8 per input");
     constexpr int K = 1024 * KC;
     constexpr int kBlocks = 8 * KC;
     constexpr int kMine = (kBlocks + kConsumerWarps - 1) / kConsumerWarps;
     constexpr int RB = kKsplitRows;
     constexpr int RG = kKsplitGroupRows;
-    static_assert(kConsumerWarps * RG * NB <= 2 * 16 * RG, "partials fit the K-split slots");
     const TcJob job{kTcRow, OUT, r0, r1, tile_rows, 1.f, E};
     const int n = r1 - r0;  // <= RG (checked on the host)
-    float *part = sPart;    // [warp][row][b]
-    float4 xv[kMine][NB];
+    float4 xv[kMine][NV];
 #pragma unroll
     for (int q = 0; q < kMine; ++q) {
       const int blk = warp + kConsumerWarps * q;
 #pragma unroll
-      for (int b = 0; b < NB; ++b)
+      for (int b = 0; b < NV; ++b)
         xv[q][b] = (blk < kBlocks) ? reinterpret_cast<const float4 *>(xin + b * K)[lane + 32 * blk]
                                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     for (int i0 = 0; i0 < n; i0 += RB) {
-      float acc[RB][NB][2];
+      float acc[RB][NV][2];
 #pragma unroll
       for (int r = 0; r < RB; ++r)
 #pragma unroll
-        for (int b = 0; b < NB; ++b) acc[r][b][0] = acc[r][b][1] = 0.f;
+        for (int b = 0; b < NV; ++b) acc[r][b][0] = acc[r][b][1] = 0.f;
       if (ok) {
 #pragma unroll
         for (int r = 0; r < RB; ++r) {
@@ -2229,7 +2229,7 @@ struct Consumer {
               if (blk < kBlocks) {
                 const uint2 wv = *reinterpret_cast<const uint2 *>(rp + 256 * blk);
 #pragma unroll
-                for (int b = 0; b < NB; ++b) dot4(acc[r][b][0], acc[r][b][1], wv, xv[q][b]);
+                for (int b = 0; b < NV; ++b) dot4(acc[r][b][0], acc[r][b][1], wv, xv[q][b]);
               }
             }
           }
@@ -2239,18 +2239,18 @@ struct Consumer {
       for (int r = 0; r < RB; ++r) {
         float v[4];
 #pragma unroll
-        for (int b = 0; b < NB; ++b) v[b] = acc[r][b][0] + acc[r][b][1];
-        const float wsum = reduce4_transpose(v);  // lane 8b: sequence b
-        if ((lane & 7) == 0 && i0 + r < n) part[(warp * RG + i0 + r) * NB + (lane >> 3)] = wsum;
+        for (int b = 0; b < 4; ++b) v[b] = (b < NV) ? acc[r][b < NV ? b : 0][0] + acc[r][b < NV ? b : 0][1] : 0.f;
+        const float wsum = reduce4_transpose(v);  // lane 8j: input j
+        if ((lane & 7) == 0 && (lane >> 3) < NV && i0 + r < n) part[(warp * RG + i0 + r) * NV + (lane >> 3)] = wsum;
       }
     }
     consumer_sync();
-    if (ok && tid < n * NB) {
-      const int i = tid / NB, b = tid % NB;
+    if (ok && tid < n * NV) {
+      const int i = tid / NV, b = tid % NV;
       float sum = 0.f;
 #pragma unroll
-      for (int q = 0; q < kConsumerWarps; ++q) sum += part[(q * RG + i) * NB + b];
-      cur_b = b;
+      for (int q = 0; q < kConsumerWarps; ++q) sum += part[(q * RG + i) * NV + b];
+      cur_b = b0 + b;
       tc_emit(job, r0 + i, sum, 0.f);
     }
   }
@@ -2293,7 +2293,8 @@ struct Consumer {
     for (int b = 0; b < NB; ++b)
       stage_vec<kQSize, kStageCopy>(c, sX + b * kQSize, nullptr, c.wAtt + (size_t)b * kWordsAtt, E, kSiteAtt, nullptr,
                                     NormPairs{});
-    fma_ksplit_nb<2, kOutO>(tiles, sX, R.begin, R.end, kOTileRows, kQSize * 2, E);
+    static_assert(kConsumerWarps * kKsplitGroupRows * NB <= 2 * 16 * kKsplitGroupRows, "partials fit");
+    fma_ksplit_nb<2, kOutO, NB>(tiles, sX, 0, sPart, R.begin, R.end, kOTileRows, kQSize * 2, E);
     release_tiles(ntiles, tiles);
   }
 
@@ -2322,11 +2323,18 @@ struct Consumer {
     const Range R = d_rows(c.cta, c.ncta);
     const int ntiles = tiles_of(R, kDTileRows);
     const bool tiles = wait_tiles(ntiles);
+    // two sequences per pass: their MLP inputs (2 x 12 KB) in the activation
+    // regions, the partials of the two passes in separate halves of the slots
+    constexpr int kPer = 2;
+    static_assert(NB % kPer == 0 && kPer * kInter * 4 <= kSmMisc - kSmX, "MLP inputs fit");
+    static_assert(2 * kConsumerWarps * kKsplitGroupRows * kPer <= 2 * 16 * kKsplitGroupRows, "partials fit");
 #pragma unroll 1
-    for (int b = 0; b < NB; ++b) {
-      cur_b = b;
-      stage_vec<kInter, kStageCopy>(c, sU, nullptr, c.wM + (size_t)b * kWordsM, E, kSiteM, nullptr, NormPairs{});
-      fma_ksplit_phase<3, kOutDown>(tiles, sU, R.begin, R.end, kDTileRows, kDRowPitch, E, false);
+    for (int b0 = 0; b0 < NB; b0 += kPer) {
+      for (int j = 0; j < kPer; ++j)
+        stage_vec<kInter, kStageCopy>(c, sX + j * kInter, nullptr, c.wM + (size_t)(b0 + j) * kWordsM, E, kSiteM,
+                                      nullptr, NormPairs{});
+      fma_ksplit_nb<3, kOutDown, kPer>(tiles, sX, b0, sPart + (b0 / kPer & 1) * (kConsumerWarps * kKsplitGroupRows * kPer),
+                                       R.begin, R.end, kDTileRows, kDRowPitch, E);
     }
     release_tiles(ntiles, tiles);
   }
