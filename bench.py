@@ -823,7 +823,8 @@ def main(argv=None) -> int:
     ap.add_argument("--profile-case", type=int, default=0, metavar="STEPS",
                     help="run only the small ncu case: one decode launch of STEPS tokens")
     ap.add_argument("--batch", type=int, default=0, metavar="B",
-                    help="config 4 instead of the headline: B sequences decoded together (token-parallel path)")
+                    help="config 4 instead of the headline: B sequences decoded together (B = 4: the decode kernel's "
+                         "batched instance; otherwise the token-parallel kernels)")
     ap.add_argument("--prefill", action="store_true", help="time the token-parallel 1024-token prefill instead")
     ap.add_argument("--ctx", type=int, default=0, metavar="L",
                     help="config 3 instead of the headline: batch-1 decode after L cached positions of random K/V")
