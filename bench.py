@@ -455,6 +455,33 @@ def run_profile_case(steps: int) -> int:
     return 0
 
 
+def run_profile_ctx(L: int, steps: int = 4) -> int:
+    """Small long-context case for ncu captures: K/V cache of bf16 N(0, 1)
+    at positions [0, L) (as `--ctx L`), one warm-up launch, then ONE launch
+    of `steps` tokens (capture with ncu -k regex:decode_kernel -s 1 -c 1)."""
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    from qwen_megakernel_b200 import Decoder
+    from qwen_megakernel_b200.weights import random_weights, rope_tables
+
+    msl = L + steps + 8
+    weights = random_weights(seed=0, device=dev, max_seq_len=2048)
+    weights["cos_table"], weights["sin_table"] = rope_tables(msl, device=dev)
+    dec = Decoder(weights, max_seq_len=msl)
+    gen = torch.Generator(device=dev).manual_seed(2)
+    dec.k_cache[:, :, :L].normal_(generator=gen)
+    dec.v_cache[:, :, :L].normal_(generator=gen)
+    first = torch.tensor([17], dtype=torch.int32, device=dev)
+    log = torch.empty(steps, dtype=torch.int32, device=dev)
+    for _ in range(2):
+        dec.decode_steps(steps, forced_tokens=first, start_position=L, output_log=log)
+    torch.cuda.synchronize(dev)
+    dec.check_status()
+    print(json.dumps({"profile_ctx": {"ctx": L, "steps": steps, "tokens": log.tolist(),
+                                      "max_memory_gb": round(torch.cuda.max_memory_allocated() / 1e9, 3)}}))
+    return 0
+
+
 def run_trace(steps: int) -> int:
     """Per-phase critical path of the decode kernel: the bench model and
     prompt, then launches of `steps` greedy tokens at ctx ~1k whose middle
@@ -832,6 +859,8 @@ def main(argv=None) -> int:
                     help="run only the small ncu case of the token-parallel path: one batched step of B rows")
     ap.add_argument("--trace", type=int, default=0, metavar="STEPS",
                     help="print the per-phase critical path of one traced step of a STEPS-token launch")
+    ap.add_argument("--profile-ctx", type=int, default=0, metavar="L",
+                    help="run only the small ncu case of a long context: 4-token launches after L random K/V positions")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="run only the small ncu case of the token-parallel prefill")
     ap.add_argument("--profile-gemm", type=int, nargs=3, default=None, metavar=("N", "ROWS", "K"),
@@ -839,6 +868,8 @@ def main(argv=None) -> int:
     args = ap.parse_args(argv)
     if args.profile_prefill:
         return run_profile_prefill()
+    if args.profile_ctx:
+        return run_profile_ctx(args.profile_ctx)
     if args.profile_gemm:
         return run_profile_gemm(*args.profile_gemm)
     if args.trace:
