@@ -214,3 +214,88 @@ def test_torch_ops_keep_reference_schemas():
     assert str(o.generate_nosync.default._schema) == "qwen_megakernel_C::" + REF_GENERATE
     run = str(o.run.default._schema)
     assert run.startswith("qwen_megakernel_C::run(Tensor workspace")
+
+
+class QmkBatchRunArgs(ctypes.Structure):
+    _fields_ = [
+        ("embed_weight", ctypes.c_void_p),
+        ("layer_weights", ctypes.c_void_p),
+        ("final_norm_weight", ctypes.c_void_p),
+        ("lm_head_weight", ctypes.c_void_p),
+        ("cos_table", ctypes.c_void_p),
+        ("sin_table", ctypes.c_void_p),
+        ("k_cache", ctypes.c_void_p),
+        ("v_cache", ctypes.c_void_p),
+        ("cache_seq_stride", ctypes.c_longlong),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+        ("first_tokens", ctypes.c_void_p),
+        ("start_positions", ctypes.c_int * 4),
+        ("num_steps", ctypes.c_int),
+        ("num_layers", ctypes.c_int),
+        ("max_seq_len", ctypes.c_int),
+        ("attn_scale", ctypes.c_float),
+        ("output_log", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("timeout_ns", ctypes.c_ulonglong),
+    ]
+
+
+def _valid_batch_args(lib) -> QmkBatchRunArgs:
+    a = QmkBatchRunArgs()
+    fake = 0x10000  # never dereferenced: validation fails before any launch
+    for f in ("embed_weight", "layer_weights", "final_norm_weight", "lm_head_weight", "cos_table",
+              "sin_table", "k_cache", "v_cache", "workspace", "first_tokens"):
+        setattr(a, f, fake)
+    a.workspace_bytes = lib.qmk_workspace_bytes()
+    a.num_layers = 28
+    a.max_seq_len = 2048
+    a.cache_seq_stride = 28 * 8 * 2048 * 128
+    a.num_steps = 4
+    a.attn_scale = 0.088
+    for s in range(4):
+        a.start_positions[s] = 100 * s
+    return a
+
+
+@pytest.mark.parametrize(
+    "field,value,code",
+    [
+        ("embed_weight", 0, 1),
+        ("first_tokens", 0, 1),
+        ("workspace", 0, 1),
+        ("workspace_bytes", 16, 6),
+        ("num_layers", 0, 1),
+        ("num_steps", 0, 1),
+        ("cache_seq_stride", 1024, 1),  # smaller than one sequence's cache
+        ("cache_seq_stride", 28 * 8 * 2048 * 128 + 4, 1),  # not 16-byte aligned
+        ("attn_scale", -1.0, 1),
+        ("v_cache", 0x10008, 1),  # misaligned tensor
+    ],
+)
+def test_qmk_run_batch_rejects_bad_arguments(lib, field, value, code):
+    a = _valid_batch_args(lib)
+    setattr(a, field, value)
+    assert lib.qmk_run_batch(ctypes.byref(a), None) == code
+    assert lib.qmk_get_last_error() == code
+
+
+def test_qmk_run_batch_rejects_positions_past_max_seq_len(lib):
+    a = _valid_batch_args(lib)
+    a.start_positions[3] = 2045  # 2045 + 4 steps > 2048
+    assert lib.qmk_run_batch(ctypes.byref(a), None) == 1
+    assert b"sequence 3" in lib.qmk_get_last_error_message()
+    a = _valid_batch_args(lib)
+    a.start_positions[1] = -1
+    assert lib.qmk_run_batch(ctypes.byref(a), None) == 1
+
+
+def test_batch_decoder_megakernel_mode_needs_four_sequences():
+    from qwen_megakernel_b200 import BatchDecoder
+    from qwen_megakernel_b200.weights import random_weights
+
+    w = random_weights(seed=1, device="cpu", max_seq_len=64, num_layers=1)
+    with pytest.raises(ValueError, match="exactly 4"):
+        BatchDecoder(w, 3, max_seq_len=64, decode="megakernel")
+    with pytest.raises(ValueError, match="decode must be"):
+        BatchDecoder(w, 4, max_seq_len=64, decode="fast")
