@@ -13,8 +13,9 @@
 //
 // A tile is 128 x TN of C^T: W rows m0 .. m0+127 are the MMA's M = 128
 // operand (TMEM lane = W row), A rows n0 .. n0+TN-1 the N operand (TMEM
-// column = A row).  A persistent grid (one CTA per SM) walks the tiles; warp
-// 0 (one lane) issues the TMA loads of 64-element K blocks, warp 1 the MMAs
+// column = A row).  A persistent grid (one CTA per SM; two for prompt-sized
+// GEMMs, see qmk_internal_gemm) walks the tiles; warp 0 (one lane) issues
+// the TMA loads of 64-element K blocks, warp 1 the MMAs
 // (4 of K = 16 per block) and tcgen05.commit, which frees a ring stage once
 // its MMAs have read it and hands a finished accumulator to the epilogue
 // warps 2-5, which read it (tcgen05.ld, lane = W row) and store C column by
@@ -361,7 +362,7 @@ int make_map(CUtensorMap *m, const void *base, long long k, long long rows, long
   return QMK_OK;
 }
 
-template <int TN, int STAGES>
+template <int TN, int STAGES, int CPS = 1>
 int launch(const Args &a, int tiles_m, int tiles_n, int z, cudaStream_t stream, int dev) {
   constexpr int kSmem = smem_bytes<TN, STAGES>();
   static_assert(kSmem <= 232448, "GEMM ring exceeds shared memory");
@@ -379,7 +380,8 @@ int launch(const Args &a, int tiles_m, int tiles_n, int z, cudaStream_t stream, 
   if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return qmk_internal_set_error(QMK_ERR_CUDA, "SM count");
   const long long total = (long long)tiles_m * tiles_n * z;
-  const int grid = (int)(total < sms[dev] ? total : sms[dev]);
+  const long long slots = (long long)CPS * sms[dev];  // CPS CTAs per SM (shared memory and TMEM permitting)
+  const int grid = (int)(total < slots ? total : slots);
   // programmatic stream serialization: see the producer's weight prefetch
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
@@ -421,7 +423,13 @@ __attribute__((visibility("hidden"))) int qmk_internal_gemm(
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return qmk_internal_set_error(QMK_ERR_CUDA, "qmk_gemm: cudaGetDevice");
-  const int tn = rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 ? 128 : 256;
+  // Activation tile: the rows rounded up to 32 / 64 / 128; more than 128
+  // rows use 128-row tiles with two CTAs per SM (3 ring stages each), which
+  // measured faster than one CTA per SM with 256-row tiles (1024-token
+  // prefill 9.95 -> 7.87 ms) or with 128-row tiles (8.9 ms): the two CTAs'
+  // producers and MMA issuers overlap each other's waits.
+  const bool big = rows > 128;
+  const int tn = rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
   Args a;
   memset(&a, 0, sizeof(a));
   if (make_map(&a.tw, W, k, n, ldw, batch, w_batch_stride, kBM) != QMK_OK) return QMK_ERR_ARGS;
@@ -447,8 +455,9 @@ __attribute__((visibility("hidden"))) int qmk_internal_gemm(
   switch (tn) {
     case 32: return launch<32, 8>(a, tiles_m, tiles_n, (int)z, stream, dev);
     case 64: return launch<64, 8>(a, tiles_m, tiles_n, (int)z, stream, dev);
-    case 128: return launch<128, 6>(a, tiles_m, tiles_n, (int)z, stream, dev);
-    default: return launch<256, 4>(a, tiles_m, tiles_n, (int)z, stream, dev);
+    default:
+      return big ? launch<128, 3, 2>(a, tiles_m, tiles_n, (int)z, stream, dev)
+                 : launch<128, 6>(a, tiles_m, tiles_n, (int)z, stream, dev);
   }
 }
 
