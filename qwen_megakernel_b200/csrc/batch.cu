@@ -785,7 +785,7 @@ struct Layout {
 // chunks multiply the CTAs (up to ~one wave of 148 SMs) and the consumer of
 // the output adds the partial products in split order.
 constexpr int kMaxSplitK = 8;
-int gemm_tile_n(int rows2) { return rows2 <= 32 ? 32 : rows2 <= 64 ? 64 : 128; }  // activation tile of qmk_internal_gemm
+int gemm_tile_n(int rows2) { return rows2 <= 32 ? 32 : rows2 <= 64 ? 64 : rows2 <= 128 ? 128 : 64; }  // activation tile of qmk_internal_gemm
 int split_k(int n, int rows2, int k) {
   const int tiles = ((n + 127) / 128) * ((rows2 + gemm_tile_n(rows2) - 1) / gemm_tile_n(rows2));
   int s = 1;

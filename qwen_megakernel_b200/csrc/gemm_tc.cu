@@ -13,7 +13,7 @@
 //
 // A tile is 128 x TN of C^T: W rows m0 .. m0+127 are the MMA's M = 128
 // operand (TMEM lane = W row), A rows n0 .. n0+TN-1 the N operand (TMEM
-// column = A row).  A persistent grid (one CTA per SM; two for prompt-sized
+// column = A row).  A persistent grid (one CTA per SM; three for prompt-sized
 // GEMMs, see qmk_internal_gemm) walks the tiles; warp 0 (one lane) issues
 // the TMA loads of 64-element K blocks, warp 1 the MMAs
 // (4 of K = 16 per block) and tcgen05.commit, which frees a ring stage once
@@ -423,13 +423,15 @@ __attribute__((visibility("hidden"))) int qmk_internal_gemm(
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return qmk_internal_set_error(QMK_ERR_CUDA, "qmk_gemm: cudaGetDevice");
-  // Activation tile: the rows rounded up to 32 / 64 / 128; more than 128
-  // rows use 128-row tiles with two CTAs per SM (3 ring stages each), which
-  // measured faster than one CTA per SM with 256-row tiles (1024-token
-  // prefill 9.95 -> 7.87 ms) or with 128-row tiles (8.9 ms): the two CTAs'
-  // producers and MMA issuers overlap each other's waits.
+  // Activation tile: the rows rounded up to 32 / 64 / 128.  More than 128
+  // rows (prompts) use 64-row tiles with three CTAs per SM (3 ring stages
+  // each; their producers and MMA issuers overlap each other's waits).
+  // 1024-token prefill, measured: one CTA per SM with 256-row tiles 9.95 ms,
+  // with 128-row tiles 8.9 ms; 128-row tiles x 2 CTAs x 3 stages 8.2 ms,
+  // x 2 stages 11.0 ms; 64-row tiles x 4 CTAs x 2 stages 9.0 ms, x 2 CTAs x
+  // 4 stages 7.9 ms, x 3 CTAs x 3 stages 7.7 ms.
   const bool big = rows > 128;
-  const int tn = rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
+  const int tn = big ? 64 : rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
   Args a;
   memset(&a, 0, sizeof(a));
   if (make_map(&a.tw, W, k, n, ldw, batch, w_batch_stride, kBM) != QMK_OK) return QMK_ERR_ARGS;
@@ -452,12 +454,11 @@ __attribute__((visibility("hidden"))) int qmk_internal_gemm(
   const long long z = (long long)batch * splits;
   if ((long long)tiles_m * tiles_n * z > (1LL << 31) - 1)
     return qmk_internal_set_error(QMK_ERR_ARGS, "qmk_gemm: too many tiles");
+  if (big) return launch<64, 3, 3>(a, tiles_m, tiles_n, (int)z, stream, dev);
   switch (tn) {
     case 32: return launch<32, 8>(a, tiles_m, tiles_n, (int)z, stream, dev);
     case 64: return launch<64, 8>(a, tiles_m, tiles_n, (int)z, stream, dev);
-    default:
-      return big ? launch<128, 3, 2>(a, tiles_m, tiles_n, (int)z, stream, dev)
-                 : launch<128, 6>(a, tiles_m, tiles_n, (int)z, stream, dev);
+    default: return launch<128, 6>(a, tiles_m, tiles_n, (int)z, stream, dev);
   }
 }
 
