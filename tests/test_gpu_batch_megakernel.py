@@ -113,3 +113,22 @@ def test_megakernel_batch_rejects_bad_arguments():
     bd.prefill([[1, 2, 3]] * SEQS)
     with pytest.raises(ValueError):
         bd.generate([1, 2, 3, 4], 62)  # past max_seq_len
+
+
+def test_megakernel_batch_reports_bad_token():
+    """An out-of-range first token of one sequence: the launch completes
+    (token 0 is used in its place, nothing is read out of bounds) and the
+    status block reports QMK_ERR_TOKEN; the next launch on the same
+    workspace is clean."""
+    from qwen_megakernel_b200 import BatchDecoder, DecodeError
+
+    w = small_model(1, seed=7)
+    bd = BatchDecoder(w, SEQS, max_seq_len=64, decode="megakernel")
+    first = bd.prefill([[1, 2, 3]] * SEQS)
+    bd.generate([first[0], V, first[2], first[3]], 2)
+    torch.cuda.synchronize()
+    with pytest.raises(DecodeError, match="error 5"):
+        bd.check_status()
+    bd.generate(first, 2)
+    torch.cuda.synchronize()
+    bd.check_status()
