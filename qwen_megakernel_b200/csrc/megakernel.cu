@@ -561,6 +561,92 @@ __device__ __forceinline__ float stage_vec(Ctx &c, float *dst, uint8_t *bop, con
   return total;
 }
 
+// NV vectors of N words in one staging (batched instance): vector b's words
+// at src + b * src_stride are polled together (pair q of the NV * N / 2 pairs
+// by thread q % kConsumerThreads) and stored as fp32 at dst + b * N; with
+// kStageNorm also x * w (w: the bf16 norm weight in global memory, fetched
+// before the wait) at dst2 + b * N, and ss[b] = the sum of squares of vector
+// b (per thread in pair order, per warp by butterfly, over the warps in warp
+// order through red[b * 16 + warp]).  One consumer barrier for all vectors.
+template <int N, int NV, int MODE>
+__device__ __forceinline__ void stage_vecs(Ctx &c, float *dst, float *dst2, const uint64_t *src, size_t src_stride,
+                                           unsigned flag, unsigned site, float *red, const __nv_bfloat16 *nw,
+                                           float (&ss)[NV]) {
+  constexpr int kHalf = N / 2;  // pairs per vector
+  constexpr int kPairs = NV * kHalf;
+  constexpr int P = (kPairs + kConsumerThreads - 1) / kConsumerThreads;
+  constexpr bool kNorm = (MODE == kStageNorm);
+  static_assert((MODE == kStageNorm || MODE == kStageCopy) && P <= 32 && NV <= 4, "stage_vecs");
+  const int tid = threadIdx.x;
+  unsigned pending = 0;
+  uint32_t wn[kNorm ? P : 1];
+#pragma unroll
+  for (int k = 0; k < P; ++k) {
+    const int q = k * kConsumerThreads + tid;
+    if (q < kPairs) pending |= 1u << k;
+    if (kNorm) wn[kNorm ? k : 0] = (q < kPairs) ? __ldg(reinterpret_cast<const unsigned *>(nw) + q % kHalf) : 0u;
+  }
+  float acc[NV];
+#pragma unroll
+  for (int b = 0; b < NV; ++b) acc[b] = 0.f;
+  float keep[kNorm ? P : 1][2];
+#pragma unroll
+  for (int k = 0; k < (kNorm ? P : 1); ++k) keep[k][0] = keep[k][1] = 0.f;
+  uint64_t a0[P], b0[P];
+  auto addr = [&](int q) { return src + (size_t)(q / kHalf) * src_stride + 2 * (q % kHalf); };
+  Waiter w;
+  while (pending) {
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      a0[k] = 0;
+      b0[k] = 0;
+      if (pending & (1u << k)) ll_load2(addr(k * kConsumerThreads + tid), a0[k], b0[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      if ((pending & (1u << k)) && ll_flag(a0[k]) == flag && ll_flag(b0[k]) == flag) {
+        const int q = k * kConsumerThreads + tid;
+        const int bq = q / kHalf, qq = q % kHalf;
+        const float v0 = ll_value(a0[k]), v1 = ll_value(b0[k]);
+        reinterpret_cast<float2 *>(dst + bq * N)[qq] = make_float2(v0, v1);
+        if (kNorm) {
+          const uint32_t wk = wn[kNorm ? k : 0];
+          reinterpret_cast<float2 *>(dst2 + bq * N)[qq] = make_float2(v0 * bf_lo(wk), v1 * bf_hi(wk));
+          keep[kNorm ? k : 0][0] = v0;
+          keep[kNorm ? k : 0][1] = v1;
+        }
+        pending &= ~(1u << k);
+      }
+    }
+    if (!pending) break;
+    if (!w.keep_going(c, site)) break;
+  }
+  if (kNorm) {
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      const int bq = (k * kConsumerThreads + tid) / kHalf;  // >= NV for pairs past the end (keep = 0)
+      const float s2 = fmaf(keep[kNorm ? k : 0][0], keep[kNorm ? k : 0][0], keep[kNorm ? k : 0][1] * keep[kNorm ? k : 0][1]);
+#pragma unroll
+      for (int b = 0; b < NV; ++b) acc[b] += (bq == b) ? s2 : 0.f;
+    }
+#pragma unroll
+    for (int b = 0; b < NV; ++b) {
+      const float t = warp_sum(acc[b]);
+      if ((tid & 31) == 0) red[b * 16 + (tid >> 5)] = t;
+    }
+  }
+  consumer_sync();
+#pragma unroll
+  for (int b = 0; b < NV; ++b) {
+    float total = 0.f;
+    if (kNorm) {
+#pragma unroll
+      for (int q = 0; q < kConsumerWarps; ++q) total += red[b * 16 + q];
+    }
+    ss[b] = total;
+  }
+}
+
 // Norm weights (bf16 pairs) of the word pairs thread `tid` stages
 // (q = tid + j * kConsumerThreads), fetched before the dataflow wait.
 __device__ __forceinline__ NormPairs load_norm_pairs(const __nv_bfloat16 *nw, int tid) {
@@ -2255,26 +2341,28 @@ struct Consumer {
     }
   }
 
-  __device__ void phase_qkv_nb(unsigned E, unsigned x_flag, const int (&toks)[NB]) {
+  __device__ void phase_qkv_nb(unsigned E, unsigned x_flag, const int (&toks)[NB], const __nv_bfloat16 *nw_ptr) {
     const NormPairs nw = nw_pref;
     const Range R = qkv_rows(c.cta, c.ncta), Ro = o_rows(c.cta, c.ncta);
     const int ntiles = tiles_of(R, kQKVTileRows);
     const bool tiles = wait_tiles(ntiles);
     float scale_mine = 0.f;  // 1/rms of this lane's sequence (lane >> 3)
+    if (x_flag) {
+      float ss[NB];
+      stage_vecs<kHidden, NB, kStageNorm>(c, sX, sU, c.wX, kWordsX, x_flag, kSiteX, red_x, nw_ptr, ss);
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+        if ((lane >> 3) == b) scale_mine = rsqrtf(ss[b] / (float)kHidden + kRmsEps);
+    } else {
 #pragma unroll 1
-    for (int b = 0; b < NB; ++b) {
-      // back-to-back stagings alternate their reduction slots
-      float ss;
-      if (x_flag) {
-        ss = stage_vec<kHidden, kStageNorm>(c, sX + b * kHidden, reinterpret_cast<uint8_t *>(sU + b * kHidden),
-                                            c.wX + (size_t)b * kWordsX, x_flag, kSiteX, (b & 1) ? red_e : red_x, nw);
-      } else {
-        ss = embed_row(toks[b], sX + b * kHidden, (b & 1) ? red_e : red_x);
+      for (int b = 0; b < NB; ++b) {
+        // back-to-back embeddings alternate their reduction slots
+        const float ss = embed_row(toks[b], sX + b * kHidden, (b & 1) ? red_e : red_x);
         build_norm_xw(sU + b * kHidden, sX + b * kHidden, nw, tid);
+        if ((lane >> 3) == b) scale_mine = rsqrtf(ss / (float)kHidden + kRmsEps);
       }
-      if ((lane >> 3) == b) scale_mine = rsqrtf(ss / (float)kHidden + kRmsEps);
+      consumer_sync();  // x * w of the embeddings
     }
-    if (!x_flag) consumer_sync();  // x * w of the embeddings
     const int no = Ro.end - Ro.begin;
     if (tid < NB * no) sResO[(tid / no) * kMaxResRows + tid % no] = sX[(tid / no) * kHidden + Ro.begin + tid % no];
     fma_rows_nb<kOutQKV, 4>(tiles, sU, scale_mine, R.begin, R.end, kQKVTileRows, 2048, E);
@@ -2289,27 +2377,23 @@ struct Consumer {
     const bool tiles = wait_tiles(ntiles);
     // the NB attention outputs side by side over all activation regions (32 KB)
     static_assert(NB * kQSize * 4 == kSmMisc - kSmX, "attention outputs fill the activation regions");
-#pragma unroll 1
-    for (int b = 0; b < NB; ++b)
-      stage_vec<kQSize, kStageCopy>(c, sX + b * kQSize, nullptr, c.wAtt + (size_t)b * kWordsAtt, E, kSiteAtt, nullptr,
-                                    NormPairs{});
+    float unused[NB];
+    stage_vecs<kQSize, NB, kStageCopy>(c, sX, nullptr, c.wAtt, kWordsAtt, E, kSiteAtt, nullptr, nullptr, unused);
     static_assert(kConsumerWarps * kKsplitGroupRows * NB <= 2 * 16 * kKsplitGroupRows, "partials fit");
     fma_ksplit_nb<2, kOutO, NB>(tiles, sX, 0, sPart, R.begin, R.end, kOTileRows, kQSize * 2, E);
     release_tiles(ntiles, tiles);
   }
 
-  __device__ void phase_gu_nb(unsigned E) {
-    const NormPairs nw = nw_pref;
+  __device__ void phase_gu_nb(unsigned E, const __nv_bfloat16 *nw_ptr) {
     const Range R = gu_rows(c.cta, c.ncta), Rd = d_rows(c.cta, c.ncta);
     const int ntiles = tiles_of(R, kGUTileRows);
     const bool tiles = wait_tiles(ntiles);
     float scale_mine = 0.f;
-#pragma unroll 1
-    for (int b = 0; b < NB; ++b) {
-      const float ss = stage_vec<kHidden, kStageNorm>(c, sX + b * kHidden, reinterpret_cast<uint8_t *>(sU + b * kHidden),
-                                                      c.wA + (size_t)b * kWordsA, E, kSiteA, (b & 1) ? red_e : red_a, nw);
-      if ((lane >> 3) == b) scale_mine = rsqrtf(ss / (float)kHidden + kRmsEps);
-    }
+    float ss[NB];
+    stage_vecs<kHidden, NB, kStageNorm>(c, sX, sU, c.wA, kWordsA, E, kSiteA, red_x, nw_ptr, ss);
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      if ((lane >> 3) == b) scale_mine = rsqrtf(ss[b] / (float)kHidden + kRmsEps);
     const int nd = Rd.end - Rd.begin;
     if (tid < NB * nd) sResD[(tid / nd) * kMaxResRows + tid % nd] = sX[(tid / nd) * kHidden + Rd.begin + tid % nd];
     fma_rows_nb<kOutGU, 3>(tiles, sU, scale_mine, R.begin, R.end, kGUTileRows, 4096, E);
@@ -2330,9 +2414,9 @@ struct Consumer {
     static_assert(2 * kConsumerWarps * kKsplitGroupRows * kPer <= 2 * 16 * kKsplitGroupRows, "partials fit");
 #pragma unroll 1
     for (int b0 = 0; b0 < NB; b0 += kPer) {
-      for (int j = 0; j < kPer; ++j)
-        stage_vec<kInter, kStageCopy>(c, sX + j * kInter, nullptr, c.wM + (size_t)(b0 + j) * kWordsM, E, kSiteM,
-                                      nullptr, NormPairs{});
+      float unused[kPer];
+      stage_vecs<kInter, kPer, kStageCopy>(c, sX, nullptr, c.wM + (size_t)b0 * kWordsM, kWordsM, E, kSiteM, nullptr,
+                                           nullptr, unused);
       fma_ksplit_nb<3, kOutDown, kPer>(tiles, sX, b0, sPart + (b0 / kPer & 1) * (kConsumerWarps * kKsplitGroupRows * kPer),
                                        R.begin, R.end, kDTileRows, kDRowPitch, E);
     }
@@ -2469,11 +2553,12 @@ struct Consumer {
         c.cur_layer = l;
         const LDGLayerWeights w = p.layers[l];
         const unsigned E = epoch_of(c, t, l, L);
-        phase_qkv_nb(E, l > 0 ? epoch_of(c, t, l - 1, L) : 0u, toks);
+        phase_qkv_nb(E, l > 0 ? epoch_of(c, t, l - 1, L) : 0u, toks,
+                     (const __nv_bfloat16 *)w.input_layernorm_weight);
         phase_attention(w, l, t, E);
         phase_merge(E, l);
         phase_o_nb(w, E);
-        phase_gu_nb(E);
+        phase_gu_nb(E, (const __nv_bfloat16 *)w.post_attn_layernorm_weight);
         phase_down_nb(E, l);
       }
       phase_lm_nb(t, epoch_of(c, t, L - 1, L), epoch_of(c, t, L, L));
