@@ -206,7 +206,8 @@ int qmk_run(const QmkRunArgs *args, cudaStream_t stream);
  * greedy token of step t - 1) and writes that position's K/V; the greedy
  * token of step t goes to output_log[t * QMK_BATCH_SEQS + s].  Same kernel
  * as qmk_run: every weight tile is streamed once per step for all
- * sequences.  Uses the workspace of qmk_workspace_bytes(); device errors
+ * sequences (q|k|v, gate/up and the LM head as tensor-core GEMVs with the
+ * sequences as the N columns, O and down on the CUDA cores).  Uses the workspace of qmk_workspace_bytes(); device errors
  * are reported through status as for qmk_run. */
 #define QMK_BATCH_SEQS 4
 
@@ -311,8 +312,9 @@ int qmk_static_scratch_ptrs(int **output_log, QmkStatus **status);
  * [0, row_pos[r]] of it.  Rows of one sequence at consecutive positions are
  * a causal prefill (every row sees the K/V the earlier rows write in the same
  * call); one row per sequence is a batched decode step.  The projections are
- * tensor-core GEMMs (cuBLAS, bf16 operands: activations as a bf16 hi + lo
- * pair, fp32 accumulate, so they keep the decode kernel's fp32 precision);
+ * tensor-core GEMMs (this library's tcgen05 kernel, bf16 operands:
+ * activations as a bf16 hi + lo pair, fp32 accumulate, so they keep the
+ * decode kernel's fp32 precision);
  * norms, QK-norm + RoPE + K/V append, attention, SiLU and argmax are this
  * library's kernels.  Output rows out_rows[i] (i < num_out) get the final
  * RMSNorm, the LM head and the greedy argmax (lowest index on ties).

@@ -565,9 +565,13 @@ __device__ __forceinline__ float stage_vec(Ctx &c, float *dst, uint8_t *bop, con
 // at src + b * src_stride are polled together (pair q of the NV * N / 2 pairs
 // by thread q % kConsumerThreads) and stored as fp32 at dst + b * N; with
 // kStageNorm also x * w (w: the bf16 norm weight in global memory, fetched
-// before the wait) at dst2 + b * N, and ss[b] = the sum of squares of vector
-// b (per thread in pair order, per warp by butterfly, over the warps in warp
-// order through red[b * 16 + warp]).  One consumer barrier for all vectors.
+// before the wait) at dst2 + b * N, with kStageNormFrag x * w as the
+// tensor-core B operand of the NV vectors side by side (N = 1024, slot b =
+// vector b: element e of vector b is element 1024 b + e of a K = 1024 NV
+// operand, N = 16 NV columns) at dst2, fenced for the async proxy; and
+// ss[b] = the sum of squares of vector b (per thread in pair order, per warp
+// by butterfly, over the warps in warp order through red[b * 16 + warp]).
+// One consumer barrier for all vectors.
 template <int N, int NV, int MODE>
 __device__ __forceinline__ void stage_vecs(Ctx &c, float *dst, float *dst2, const uint64_t *src, size_t src_stride,
                                            unsigned flag, unsigned site, float *red, const __nv_bfloat16 *nw,
@@ -575,8 +579,11 @@ __device__ __forceinline__ void stage_vecs(Ctx &c, float *dst, float *dst2, cons
   constexpr int kHalf = N / 2;  // pairs per vector
   constexpr int kPairs = NV * kHalf;
   constexpr int P = (kPairs + kConsumerThreads - 1) / kConsumerThreads;
-  constexpr bool kNorm = (MODE == kStageNorm);
-  static_assert((MODE == kStageNorm || MODE == kStageCopy) && P <= 32 && NV <= 4, "stage_vecs");
+  constexpr bool kFrag = (MODE == kStageNormFrag);
+  constexpr bool kNorm = (MODE == kStageNorm || kFrag);
+  static_assert((MODE == kStageNorm || MODE == kStageNormFrag || MODE == kStageCopy) && P <= 32 && NV <= 4,
+                "stage_vecs");
+  static_assert(!kFrag || N == 1024, "B operand of K = 1024 inputs");
   const int tid = threadIdx.x;
   unsigned pending = 0;
   uint32_t wn[kNorm ? P : 1];
@@ -611,7 +618,10 @@ __device__ __forceinline__ void stage_vecs(Ctx &c, float *dst, float *dst2, cons
         reinterpret_cast<float2 *>(dst + bq * N)[qq] = make_float2(v0, v1);
         if (kNorm) {
           const uint32_t wk = wn[kNorm ? k : 0];
-          reinterpret_cast<float2 *>(dst2 + bq * N)[qq] = make_float2(v0 * bf_lo(wk), v1 * bf_hi(wk));
+          if (kFrag)
+            store_bop_pair<NV>(reinterpret_cast<uint8_t *>(dst2), 2 * q, v0 * bf_lo(wk), v1 * bf_hi(wk));
+          else
+            reinterpret_cast<float2 *>(dst2 + bq * N)[qq] = make_float2(v0 * bf_lo(wk), v1 * bf_hi(wk));
           keep[kNorm ? k : 0][0] = v0;
           keep[kNorm ? k : 0][1] = v1;
         }
@@ -621,6 +631,7 @@ __device__ __forceinline__ void stage_vecs(Ctx &c, float *dst, float *dst2, cons
     if (!pending) break;
     if (!w.keep_going(c, site)) break;
   }
+  if (kFrag) fence_proxy_async_smem();
   if (kNorm) {
 #pragma unroll
     for (int k = 0; k < P; ++k) {
@@ -674,6 +685,22 @@ __device__ __forceinline__ void build_norm_bop(uint8_t *bop, const float *x, con
   fence_proxy_async_smem();
 }
 
+// Slot `slot` of a B operand with S inputs side by side (K = 1024 S) <- x * w
+// (K = 1024); the caller fences it for the tensor cores and publishes it
+// with its next consumer_sync.
+template <int S>
+__device__ __forceinline__ void build_norm_bop_slot(uint8_t *bop, int slot, const float *x, const NormPairs &nw,
+                                                    int tid) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int q = tid + j * kConsumerThreads;
+    if (q < kHidden / 2) {
+      const float2 v = reinterpret_cast<const float2 *>(x)[q];
+      store_bop_pair<S>(bop, 1024 * slot + 2 * q, v.x * bf_lo(nw.w[j]), v.y * bf_hi(nw.w[j]));
+    }
+  }
+}
+
 // xw <- x * w (the RMSNorm weight; 1/rms is applied to the GEMV results),
 // fp32; the caller's next consumer_sync publishes it.  K = 1024.
 __device__ __forceinline__ void build_norm_xw(float *xw, const float *x, const NormPairs &nw, int tid) {
@@ -704,6 +731,20 @@ __device__ __forceinline__ float reduce4_transpose(const float (&v)[4]) {
   float u = (hi8 ? w[1] : w[0]) + __shfl_xor_sync(0xffffffffu, send, 8);
   u += __shfl_xor_sync(0xffffffffu, u, 4);
   u += __shfl_xor_sync(0xffffffffu, u, 2);
+  u += __shfl_xor_sync(0xffffffffu, u, 1);
+  return u;
+}
+
+// Sums over the 8 lanes of an aligned lane group of four per-lane values
+// v[0..3]: lane q (= lane & 7) of the group returns the group's sum of
+// v[q >> 1].  Three levels of one exchange each (4 shuffles), the same
+// pairs added in the same order on every run.
+__device__ __forceinline__ float reduce4_oct(const float (&v)[4]) {
+  const int q = threadIdx.x & 7;
+  const bool h4 = (q & 4) != 0, h2 = (q & 2) != 0;
+  const float a0 = (h4 ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, h4 ? v[0] : v[2], 4);
+  const float a1 = (h4 ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, h4 ? v[1] : v[3], 4);
+  float u = (h2 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, h2 ? a0 : a1, 2);
   u += __shfl_xor_sync(0xffffffffu, u, 1);
   return u;
 }
@@ -1253,6 +1294,83 @@ struct Consumer {
           mbar_arrive(&c.tmem_free[(seq + 1u) % kTmemBufs]);
         }
         if (tstamp) c.trace[kTraceTileBase + 5 * kTraceTiles + tk] = trace_now(c);
+      }
+    }
+    tile += (uint32_t)ntiles;
+    mma_seq += (unsigned)nunits;
+  }
+
+  // Batched instance: a K = 1024 GEMV phase (kTcRow or kTcGU tiles) of all
+  // NB staged inputs on the tensor cores in one pass over the tiles.  The B
+  // operand holds the NB inputs side by side (stage_vecs kStageNormFrag:
+  // slot b = sequence b, N = 16 NB), so each unit (one M block, 4 MMAs)
+  // multiplies its half-tile with every input and D[8j + q][16b + 8g + q]
+  // is segment j's partial (part g) for sequence b.  Issuers as in
+  // tc_phase; each reader lane loads its TMEM lane's 16 NB columns of both
+  // units, adds its 2 NB diagonal entries per sequence, and an 8-lane
+  // transposing reduction leaves sequence q >> 1's segment sum in lane q of
+  // the segment (q = lane & 7), which emits it scaled by that sequence's
+  // 1/rms (`scale`).  Rows as in tc_phase: a tile row per segment (kTcRow),
+  // or gate (segment 2k) and up (2k + 1) of output row k (kTcGU).
+  __device__ __forceinline__ void tc_phase_nb(const TcJob &job, const uint8_t *bop, const float (&scale)[NB]) {
+    static_assert(NB == 4, "one sequence per lane pair of a segment");
+    const int ntiles = (job.r1 - job.r0 + job.tile_rows - 1) / job.tile_rows;
+    constexpr int kIssuers = kConsumerWarps - 4;
+    const unsigned seq0 = mma_seq;
+    const int nunits = 2 * ntiles;
+    if (warp >= 4) {
+      bool ok = live();
+      for (int u = warp - 4; u < nunits && ok; u += kIssuers)
+        ok = tc_issue_unit(tile + (uint32_t)(u >> 1), u & 1, seq0 + (unsigned)u, bop, NB,
+                           u == warp - 4 && tc_prewaited);
+      tc_prewaited = false;
+    }
+    if (warp < 4) {
+      const int q = lane & 7;
+      const int j = (32 * warp + lane) >> 3;  // segment of this lane
+      const int mb = q >> 1;                  // sequence whose sum this lane ends with
+      TcJob jb = job;
+      jb.scale = (mb == 0) ? scale[0] : (mb == 1) ? scale[1] : (mb == 2) ? scale[2] : scale[3];
+      cur_b = mb;
+      for (int t = 0; t < ntiles; ++t) {
+        const unsigned seq = seq0 + 2u * (unsigned)t;
+        bool got = live() && wait_unit(seq) && wait_unit(seq + 1u);
+        got = __all_sync(0xffffffffu, got);
+        if (got && tid == 0) mbar_arrive_cnt(&c.empty[(tile + (uint32_t)t) % kNumSlots], kConsumerWarps);
+        __syncwarp();
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (got) {
+          tc_fence_after_sync();
+#pragma unroll
+          for (int hp = 0; hp < 2; ++hp) {
+            const uint32_t taddr =
+                c.tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)kTmemBufCols * ((seq + (unsigned)hp) % kTmemBufs);
+            uint32_t r[32];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {  // columns 32h .. 32h + 31: sequences 2h, 2h + 1
+              tmem_ld32(taddr + 32u * (uint32_t)h, r);
+              v[2 * h] += sel8(r, q) + sel8(r + 8, q);
+              v[2 * h + 1] += sel8(r + 16, q) + sel8(r + 24, q);
+            }
+          }
+        }
+        tc_fence_before_sync();
+        const float sum = reduce4_oct(v);
+        const float up = __shfl_down_sync(0xffffffffu, sum, 8);
+        int lrow = -1;
+        if ((q & 1) == 0) {
+          if (job.kind == kTcRow)
+            lrow = j;
+          else if ((lane & 8) == 0)
+            lrow = j >> 1;
+        }
+        const int row = job.r0 + t * job.tile_rows + lrow;
+        if (got && lrow >= 0 && row < job.r1) tc_emit(jb, row, sum, up);
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&c.tmem_free[seq % kTmemBufs]);
+          mbar_arrive(&c.tmem_free[(seq + 1u) % kTmemBufs]);
+        }
       }
     }
     tile += (uint32_t)ntiles;
@@ -2165,14 +2283,15 @@ struct Consumer {
   }
 
   // ---------------------------------------------------- batched instance
-  // NB > 1 sequences decoded together (greedy).  A GEMV phase tests its ring
-  // tiles once, runs once per sequence on them and releases them after the
-  // last sequence, so every weight byte is read from HBM once per step for
-  // all sequences; while this CTA works on sequence b the other CTAs'
-  // outputs for sequence b + 1 arrive, so most dataflow waits after the
-  // first sequence find their words already written.  Attention items and
-  // merge tasks are per (sequence, ...); the LM head runs one pass per
-  // sequence over the same rows.
+  // NB > 1 sequences decoded together (greedy).  A GEMV phase stages the
+  // inputs of all NB sequences at once (one poll loop, one barrier) and
+  // makes ONE pass over its ring tiles in which every weight meets all NB
+  // inputs, so every weight byte is read from HBM once per step for all
+  // sequences: q|k|v, gate/up and the LM head (K = 1024, many rows) on the
+  // tensor cores with the NB inputs as the N = 16 NB columns of the B
+  // operand (tc_phase_nb); O and down (a few rows, K = 2048 / 3072) as a
+  // K-split on the CUDA cores (fma_ksplit_nb).  Attention items and merge
+  // tasks are per (sequence, ...).
 
   // Layer-0 input: the embedding row of `tok` into dst; returns its sum of
   // squares (one consumer barrier, reduction slots `red`).
@@ -2199,76 +2318,11 @@ struct Consumer {
 
   // Inputs of a normalized row phase for all NB sequences, staged side by
   // side: raw x_b at sX + b * kHidden (the X, A and ATT regions, 16 KB) and
-  // x_b * w at sU + b * kHidden (the U and x*w regions, 16 KB).
+  // the B operand of the x_b * w in the U and x*w regions (16 KB).
   static_assert(kSmA == kSmX + 4 * kHidden && kSmAtt == kSmA + 4 * kHidden && kSmU == kSmAtt + 4 * kQSize &&
                     kSmXW == kSmU + 4 * kInter,
                 "activation regions are contiguous");
   static_assert(NB * kHidden <= 2 * kHidden + kQSize && NB * kHidden <= kInter + kHidden, "staged inputs fit");
-
-  // Row GEMV of all NB staged inputs in one pass over the phase's tiles:
-  // warp w takes rows w, w + 7, ..., MR at a time, each weight (8 bytes per
-  // lane per j) read once from shared memory and multiplied with the NB
-  // inputs; per row a transposing butterfly leaves sequence b's sum in
-  // lane 8b, which scales it by its own 1/rms and emits it.
-  template <int OUT, int MR>
-  __device__ void fma_rows_nb(bool ok, const float *xw, float scale_mine, int r0, int r1, int tile_rows, int pitch,
-                              unsigned E) {
-    static_assert(NB == 4, "one lane group of 8 per sequence");
-    constexpr bool kGU = (OUT == kOutGU);
-    const int n = r1 - r0;
-    const int mb = lane >> 3;
-    const TcJob job{kTcRow, OUT, r0, r1, tile_rows, scale_mine, E};
-    for (int i0 = warp; ok && i0 < n; i0 += kConsumerWarps * MR) {
-      const uint8_t *rp[MR];
-#pragma unroll
-      for (int r = 0; r < MR; ++r) {
-        const int i = i0 + kConsumerWarps * r;
-        rp[r] = row_ptr(i < n ? i : i0, tile_rows, pitch, 8 * lane);
-      }
-      float acc[MR][NB][2], accu[kGU ? MR : 1][NB][2];
-#pragma unroll
-      for (int r = 0; r < MR; ++r)
-#pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          acc[r][b][0] = acc[r][b][1] = 0.f;
-          accu[kGU ? r : 0][b][0] = accu[kGU ? r : 0][b][1] = 0.f;
-        }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        uint2 w[MR], u[kGU ? MR : 1];
-#pragma unroll
-        for (int r = 0; r < MR; ++r) {
-          w[r] = *reinterpret_cast<const uint2 *>(rp[r] + 256 * j);
-          if (kGU) u[kGU ? r : 0] = *reinterpret_cast<const uint2 *>(rp[r] + 2048 + 256 * j);
-        }
-#pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          const float4 x = reinterpret_cast<const float4 *>(xw + b * kHidden)[lane + 32 * j];
-#pragma unroll
-          for (int r = 0; r < MR; ++r) {
-            dot4(acc[r][b][0], acc[r][b][1], w[r], x);
-            if (kGU) dot4(accu[kGU ? r : 0][b][0], accu[kGU ? r : 0][b][1], u[kGU ? r : 0], x);
-          }
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < MR; ++r) {
-        float v[4], v2[4];
-#pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          v[b] = acc[r][b][0] + acc[r][b][1];
-          v2[b] = kGU ? accu[kGU ? r : 0][b][0] + accu[kGU ? r : 0][b][1] : 0.f;
-        }
-        const float sum = reduce4_transpose(v);  // lane 8b: sequence b
-        const float sum2 = kGU ? reduce4_transpose(v2) : 0.f;
-        const int i = i0 + kConsumerWarps * r;
-        if ((lane & 7) == 0 && i < n) {
-          cur_b = mb;
-          tc_emit(job, r0 + i, sum, sum2);
-        }
-      }
-    }
-  }
 
   // K-split GEMV of NV staged inputs (x_j at xin + j * K, K = 1024 KC;
   // sequences b0 .. b0 + NV - 1) in one pass: the 128-element blocks of K go
@@ -2344,29 +2398,29 @@ struct Consumer {
   __device__ void phase_qkv_nb(unsigned E, unsigned x_flag, const int (&toks)[NB], const __nv_bfloat16 *nw_ptr) {
     const NormPairs nw = nw_pref;
     const Range R = qkv_rows(c.cta, c.ncta), Ro = o_rows(c.cta, c.ncta);
-    const int ntiles = tiles_of(R, kQKVTileRows);
-    const bool tiles = wait_tiles(ntiles);
-    float scale_mine = 0.f;  // 1/rms of this lane's sequence (lane >> 3)
+    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);  // the NB inputs x_b * w (16 KB)
+    tc_prewait(R.begin, R.end, kQKVTileRows);
+    float rstd[NB];
     if (x_flag) {
       float ss[NB];
-      stage_vecs<kHidden, NB, kStageNorm>(c, sX, sU, c.wX, kWordsX, x_flag, kSiteX, red_x, nw_ptr, ss);
+      stage_vecs<kHidden, NB, kStageNormFrag>(c, sX, sU, c.wX, kWordsX, x_flag, kSiteX, red_x, nw_ptr, ss);
 #pragma unroll
-      for (int b = 0; b < NB; ++b)
-        if ((lane >> 3) == b) scale_mine = rsqrtf(ss[b] / (float)kHidden + kRmsEps);
+      for (int b = 0; b < NB; ++b) rstd[b] = rsqrtf(ss[b] / (float)kHidden + kRmsEps);
     } else {
-#pragma unroll 1
+#pragma unroll
       for (int b = 0; b < NB; ++b) {
         // back-to-back embeddings alternate their reduction slots
         const float ss = embed_row(toks[b], sX + b * kHidden, (b & 1) ? red_e : red_x);
-        build_norm_xw(sU + b * kHidden, sX + b * kHidden, nw, tid);
-        if ((lane >> 3) == b) scale_mine = rsqrtf(ss / (float)kHidden + kRmsEps);
+        build_norm_bop_slot<NB>(bop, b, sX + b * kHidden, nw, tid);
+        rstd[b] = rsqrtf(ss / (float)kHidden + kRmsEps);
       }
-      consumer_sync();  // x * w of the embeddings
+      fence_proxy_async_smem();
+      consumer_sync();  // the B operand of the embeddings
     }
     const int no = Ro.end - Ro.begin;
     if (tid < NB * no) sResO[(tid / no) * kMaxResRows + tid % no] = sX[(tid / no) * kHidden + Ro.begin + tid % no];
-    fma_rows_nb<kOutQKV, 4>(tiles, sU, scale_mine, R.begin, R.end, kQKVTileRows, 2048, E);
-    release_tiles(ntiles, tiles);
+    const TcJob job{kTcRow, kOutQKV, R.begin, R.end, kQKVTileRows, 1.f, E};
+    tc_phase_nb(job, bop, rstd);
     consumer_sync();  // the next phase writes its scratch over the staged inputs
   }
 
@@ -2386,18 +2440,16 @@ struct Consumer {
 
   __device__ void phase_gu_nb(unsigned E, const __nv_bfloat16 *nw_ptr) {
     const Range R = gu_rows(c.cta, c.ncta), Rd = d_rows(c.cta, c.ncta);
-    const int ntiles = tiles_of(R, kGUTileRows);
-    const bool tiles = wait_tiles(ntiles);
-    float scale_mine = 0.f;
-    float ss[NB];
-    stage_vecs<kHidden, NB, kStageNorm>(c, sX, sU, c.wA, kWordsA, E, kSiteA, red_x, nw_ptr, ss);
+    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
+    tc_prewait(R.begin, R.end, kGUTileRows);
+    float ss[NB], rstd[NB];
+    stage_vecs<kHidden, NB, kStageNormFrag>(c, sX, sU, c.wA, kWordsA, E, kSiteA, red_x, nw_ptr, ss);
 #pragma unroll
-    for (int b = 0; b < NB; ++b)
-      if ((lane >> 3) == b) scale_mine = rsqrtf(ss[b] / (float)kHidden + kRmsEps);
+    for (int b = 0; b < NB; ++b) rstd[b] = rsqrtf(ss[b] / (float)kHidden + kRmsEps);
     const int nd = Rd.end - Rd.begin;
     if (tid < NB * nd) sResD[(tid / nd) * kMaxResRows + tid % nd] = sX[(tid / nd) * kHidden + Rd.begin + tid % nd];
-    fma_rows_nb<kOutGU, 3>(tiles, sU, scale_mine, R.begin, R.end, kGUTileRows, 4096, E);
-    release_tiles(ntiles, tiles);
+    const TcJob job{kTcGU, kOutGU, R.begin, R.end, kGUTileRows, 1.f, E};
+    tc_phase_nb(job, bop, rstd);
     consumer_sync();  // the next phase stages over the inputs
   }
 
@@ -2423,88 +2475,43 @@ struct Consumer {
     release_tiles(ntiles, tiles);
   }
 
-  // LM head of all NB sequences in one pass over this CTA's vocabulary rows,
-  // on the CUDA cores (the tensor-core LM head takes one vector): the NB
-  // inputs x_b * w (final norm weight) sit side by side in shared memory
-  // (the U and x*w regions, contiguous); as each 16-row tile lands, warp w
-  // takes rows w, w + 7, w + 14 and multiplies every row with all NB
-  // inputs (each weight read once from shared memory), a transposing
-  // butterfly leaves sequence b's row sum in lane 8b, which keeps that
-  // sequence's running argmax.  The weights cross HBM once per step.
+  // LM head of all NB sequences in one pass over this CTA's vocabulary rows
+  // on the tensor cores (tc_phase_nb, the NB final-normed inputs as one B
+  // operand, N = 16 NB): the weights cross HBM once per step for all
+  // sequences.  Reader lane q of a segment keeps the running argmax of
+  // sequence q >> 1 over the rows it emits; per sequence, a butterfly over
+  // the segments of a warp and a pass over the warps in warp order give the
+  // CTA's candidate (largest logit, lowest row on ties).
   __device__ void phase_lm_nb(int step, unsigned E_x, unsigned E) {
-    static_assert(NB == 4, "one lane group of 8 per sequence");
-    static_assert(kSmXW == kSmU + 4 * kInter && NB * kHidden <= kInter + kHidden, "LM-head inputs");
-    const NormPairs nw = nw_pref;  // fetched in the last P5
-    float *sV = sU;                // [NB][kHidden]
-    float rstd_mine = 0.f;         // rstd of this lane's sequence (lane >> 3)
-#pragma unroll 1
-    for (int b = 0; b < NB; ++b) {
-      // alternate reduction slots: back-to-back calls, one barrier each
-      const float ss = stage_vec<kHidden, kStageNorm>(c, sX, reinterpret_cast<uint8_t *>(sV + b * kHidden),
-                                                      c.wX + (size_t)b * kWordsX, E_x, kSiteX,
-                                                      (b & 1) ? red_e : red_lm, nw);
-      if ((lane >> 3) == b) rstd_mine = rsqrtf(ss / (float)kHidden + kRmsEps);
-    }
+    static_assert(NB == 4, "one sequence per lane pair of a segment");
     const Range R = lm_rows(c.cta, c.ncta);
-    const int ntiles = (R.end - R.begin + kLMTileRows - 1) / kLMTileRows;
+    uint8_t *bop = reinterpret_cast<uint8_t *>(sU);
+    tc_prewait(R.begin, R.end, kLMTileRows);
+    float ss[NB], rstd[NB];
+    stage_vecs<kHidden, NB, kStageNormFrag>(c, sX, sU, c.wX, kWordsX, E_x, kSiteX, red_x, p.final_norm, ss);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) rstd[b] = rsqrtf(ss[b] / (float)kHidden + kRmsEps);
     lm_best = -INFINITY;
     lm_best_i = 0x7fffffff;
-    const int mb = lane >> 3;  // sequence whose sums this lane receives
-#pragma unroll 1
-    for (int t = 0; t < ntiles; ++t) {
-      const int r0 = R.begin + t * kLMTileRows;
-      const int n = min(kLMTileRows, R.end - r0);
-      const bool ok = wait_full(c, tile);
-      const uint8_t *tb = slot_ptr(c, tile) + 8 * lane;
-      float acc[3][NB][2];
+    const TcJob job{kTcRow, kOutLM, R.begin, R.end, kLMTileRows, 1.f, E};
+    tc_phase_nb(job, bop, rstd);
+    float best = lm_best;
+    int best_i = lm_best_i;
 #pragma unroll
-      for (int r = 0; r < 3; ++r)
-#pragma unroll
-        for (int b = 0; b < NB; ++b) acc[r][b][0] = acc[r][b][1] = 0.f;
-      if (ok) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uint2 wv[3];
-#pragma unroll
-          for (int r = 0; r < 3; ++r) {
-            const int i = warp + kConsumerWarps * r;
-            wv[r] = *reinterpret_cast<const uint2 *>(tb + (size_t)(i < n ? i : warp) * (kHidden * 2) + 256 * j);
-          }
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            const float4 xv = reinterpret_cast<const float4 *>(sV + b * kHidden)[lane + 32 * j];
-#pragma unroll
-            for (int r = 0; r < 3; ++r) dot4(acc[r][b][0], acc[r][b][1], wv[r], xv);
-          }
-        }
-      }
-      __syncwarp();
-      if (ok && lane == 0) mbar_arrive(&c.empty[tile % kNumSlots]);
-      ++tile;
-#pragma unroll
-      for (int r = 0; r < 3; ++r) {
-        float v[4];
-#pragma unroll
-        for (int b = 0; b < NB; ++b) v[b] = acc[r][b][0] + acc[r][b][1];
-        const float sum = reduce4_transpose(v);  // lane 8b: sequence b (its row order is 2 ((l >> 4) & 1) + ((l >> 3) & 1) = l >> 3)
-        const int i = warp + kConsumerWarps * r;
-        const int row = r0 + i;
-        if (ok && (lane & 7) == 0 && i < n) {
-          const float y = sum * rstd_mine;
-          if (y > lm_best || (y == lm_best && row < lm_best_i)) {
-            lm_best = y;
-            lm_best_i = row;
-          }
-        }
+    for (int o = 8; o < 32; o <<= 1) {  // the warp's segments, same q
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+      if (ov > best || (ov == best && oi < best_i)) {
+        best = ov;
+        best_i = oi;
       }
     }
-    // per sequence: CTA argmax over the warps' lanes 8b
     float *bv = sPart;  // [kConsumerWarps][NB] (the K-split partials are free here)
     int *bi = reinterpret_cast<int *>(sPart + 64);
     static_assert(kConsumerWarps * NB <= 64, "argmax slots");
-    if ((lane & 7) == 0) {
-      bv[warp * NB + mb] = lm_best;
-      bi[warp * NB + mb] = lm_best_i;
+    if (lane < 8 && (lane & 1) == 0) {  // issuer warps: no rows (sentinel index)
+      bv[warp * NB + (lane >> 1)] = best;
+      bi[warp * NB + (lane >> 1)] = best_i;
     }
     consumer_sync();
     if (tid < NB) {

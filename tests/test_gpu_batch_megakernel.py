@@ -1,10 +1,11 @@
 """Batched decode in the persistent kernel (qmk_run_batch, 4 sequences).
 
-The batched instance runs every GEMV phase once per sequence on the same
-weight tiles and gives each sequence its own attention items, so each
-sequence should decode exactly as the single-sequence kernel decodes it
-alone (the attention's position splits differ, hence the margin test), and
-as the oracle does."""
+The batched instance runs every GEMV phase in one pass over the weight
+tiles for all sequences (q|k|v, gate/up and the LM head on the tensor cores
+with the 4 inputs as the MMA's N columns) and gives each sequence its own
+attention items, so each sequence should decode as the single-sequence
+kernel decodes it alone (the attention's position splits and the GEMV
+summation order differ, hence the margin test), and as the oracle does."""
 
 import pytest
 import torch
