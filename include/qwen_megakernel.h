@@ -325,11 +325,17 @@ int qmk_static_scratch_ptrs(int **output_log, QmkStatus **status);
  * are skipped; either sets a bit in *status (device uint32, optional):
  * QMK_BATCH_BAD_TOKEN / QMK_BATCH_BAD_ROW.  A K/V tile copy of the
  * attention that does not complete within 1 s sets QMK_BATCH_TIMEOUT (the
- * outputs of that call are then invalid).  All launches are stream-ordered
- * and capturable in a CUDA graph (no allocation, no host sync). */
+ * outputs of that call are then invalid); if the copies still in flight do
+ * not land within a further 1 s either, QMK_BATCH_COPIES_PENDING is set too:
+ * bulk copies may then still write shared memory after their CTA exited, so
+ * the host should treat the context as suspect (reuse nothing computed on
+ * that stream afterwards, recreate the context).  All launches are
+ * stream-ordered and capturable in a CUDA graph (no allocation, no host
+ * sync). */
 #define QMK_BATCH_BAD_TOKEN 1u
 #define QMK_BATCH_BAD_ROW 2u
 #define QMK_BATCH_TIMEOUT 4u
+#define QMK_BATCH_COPIES_PENDING 8u
 
 typedef struct QmkBatchArgs {
   const void *embed_weight;              /* bf16 [151936, 1024]                 */

@@ -31,6 +31,7 @@ MAX_ROWS = 4096  # QMK_BATCH_MAX_ROWS
 BAD_TOKEN = 1  # QMK_BATCH_BAD_TOKEN
 BAD_ROW = 2  # QMK_BATCH_BAD_ROW
 TIMEOUT = 4  # QMK_BATCH_TIMEOUT
+COPIES_PENDING = 8  # QMK_BATCH_COPIES_PENDING
 MEGAKERNEL_SEQS = 4  # QMK_BATCH_SEQS: sequences of the persistent kernel's batched instance
 
 
@@ -108,6 +109,8 @@ class BatchForward:
                 what.append("row with a sequence or position out of range (skipped)")
             if code & TIMEOUT:
                 what.append("attention K/V copy did not complete within 1 s (outputs invalid)")
+            if code & COPIES_PENDING:
+                what.append("K/V copies still in flight after the drain limit (context suspect: recreate it)")
             raise BatchError("qmk_batch_forward: " + "; ".join(what))
 
 

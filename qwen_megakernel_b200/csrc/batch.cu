@@ -446,8 +446,13 @@ __global__ void __launch_bounds__(256) attention_kernel(
   }
   // After a timeout: bounded wait for the copies still in flight before the
   // CTA (and its shared memory) goes away.
-  if (threadIdx.x == 0)
-    for (int t = pending; t < ntiles && t < pending + kAttStages; ++t) (void)wait_tile(t);
+  // If that wait runs out too, copies may still be landing in this CTA's
+  // shared memory after it exits: a status bit of its own says so.
+  if (threadIdx.x == 0) {
+    bool drained = true;
+    for (int t = pending; t < ntiles && t < pending + kAttStages; ++t) drained = wait_tile(t) && drained;
+    if (!drained && status) atomicOr(status, QMK_BATCH_COPIES_PENDING);
+  }
   // Groups -> warp (same running max in every group): reduce-scatter, then
   // lane (gq, r8) holds head gq & 1, dims [base, base + 8), base = 8 r8 + 64 (gq >> 1).
 #pragma unroll

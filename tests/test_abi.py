@@ -299,3 +299,27 @@ def test_batch_decoder_megakernel_mode_needs_four_sequences():
         BatchDecoder(w, 3, max_seq_len=64, decode="megakernel")
     with pytest.raises(ValueError, match="decode must be"):
         BatchDecoder(w, 4, max_seq_len=64, decode="fast")
+
+
+def test_batch_status_bits_match_header():
+    """The Python decoder of the token-parallel path's status word uses the
+    bit values include/qwen_megakernel.h defines, and every bit has a
+    message in BatchForward.check_status."""
+    from qwen_megakernel_b200 import batch
+
+    defines = dict(re.findall(r"#define\s+(QMK_BATCH_\w+)\s+(\d+)u?", open(HEADER).read()))
+    pairs = {
+        "QMK_BATCH_MAX_ROWS": batch.MAX_ROWS,
+        "QMK_BATCH_BAD_TOKEN": batch.BAD_TOKEN,
+        "QMK_BATCH_BAD_ROW": batch.BAD_ROW,
+        "QMK_BATCH_TIMEOUT": batch.TIMEOUT,
+        "QMK_BATCH_COPIES_PENDING": batch.COPIES_PENDING,
+        "QMK_BATCH_SEQS": batch.MEGAKERNEL_SEQS,
+    }
+    for name, value in pairs.items():
+        assert int(defines[name]) == value, name
+    bits = [batch.BAD_TOKEN, batch.BAD_ROW, batch.TIMEOUT, batch.COPIES_PENDING]
+    assert len(set(bits)) == len(bits) and all(b & (b - 1) == 0 for b in bits)
+    src = open(batch.__file__).read()
+    for name in ("BAD_TOKEN", "BAD_ROW", "TIMEOUT", "COPIES_PENDING"):
+        assert f"code & {name}" in src, name
