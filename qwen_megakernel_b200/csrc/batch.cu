@@ -622,10 +622,15 @@ __global__ void __launch_bounds__(256) softmax_split_kernel(const float *__restr
   const float inv = 1.f / block_sum256(l, red);  // key 0 is always present: sum >= 1
   __nv_bfloat16 *p_hi = P + ((size_t)g * 4 * R + i) * Rp;
   __nv_bfloat16 *p_lo = P + ((size_t)g * 4 * R + 2 * (size_t)R + i) * Rp;
+  // The P V GEMM (causal mode 2, query tiles of at most 128 rows) reads row
+  // r's keys only up to the end of its query tile; with R a multiple of 128
+  // no tile spans two heads' rows, so keys past r's 128-aligned block are
+  // never read and are not written.
+  const int jend = (R % 128 == 0) ? min(R, (r / 128 + 1) * 128) : R;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
     const int j = threadIdx.x + 256 * k;
-    if (j < R) {
+    if (j < jend) {
       const float pv = v[k] * inv;
       const __nv_bfloat16 hb = __float2bfloat16(pv);
       p_hi[j] = hb;
