@@ -19,7 +19,11 @@
 //   * the layer GEMVs run on the CUDA cores straight from the ring tiles (fp32
 //     FMA over bf16 weights, input vector fp32 in shared memory); the LM head,
 //     which streams 311 MB and is bound by HBM, runs on the tensor cores
-//     (tcgen05.mma with TMEM accumulators).
+//     (tcgen05.mma with TMEM accumulators);
+//   * a second instance decodes 4 sequences per step (qmk_run_batch): every
+//     weight tile is read once for all 4, q|k|v, gate/up and the LM head run
+//     on the tensor cores with the sequences as the MMA's N columns, O and
+//     down stay K-splits on the CUDA cores.
 //
 // Numerics follow the reference kernel (fp32 activations and accumulation,
 // bf16 weights, bf16 K/V cache, bf16 cos/sin tables), except that the residual
@@ -668,21 +672,6 @@ __device__ __forceinline__ NormPairs load_norm_pairs(const __nv_bfloat16 *nw, in
     r.w[j] = (q < kHidden / 2) ? __ldg(reinterpret_cast<const unsigned *>(nw) + q) : 0u;
   }
   return r;
-}
-
-// B operand <- x * w (the RMSNorm weight; 1/rms is applied to the GEMV
-// results), fenced for the tensor cores; the caller's next consumer_sync
-// publishes it.  K = 1024.
-__device__ __forceinline__ void build_norm_bop(uint8_t *bop, const float *x, const NormPairs &nw, int tid) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int q = tid + j * kConsumerThreads;
-    if (q < kHidden / 2) {
-      const float2 v = reinterpret_cast<const float2 *>(x)[q];
-      store_bop_pair<1>(bop, 2 * q, v.x * bf_lo(nw.w[j]), v.y * bf_hi(nw.w[j]));
-    }
-  }
-  fence_proxy_async_smem();
 }
 
 // Slot `slot` of a B operand with S inputs side by side (K = 1024 S) <- x * w
