@@ -28,9 +28,9 @@ constexpr int kMaxLayers = 64;
 
 constexpr int kMaxCtas = 160;
 constexpr int kMinCtas = 64;
-// Sequences of the batched instance (qmk_run_batch): every phase runs once
-// per sequence on the same weight tiles; attention items and merge tasks are
-// per (sequence, ...).
+// Sequences of the batched instance (qmk_run_batch): every GEMV phase makes
+// one pass over its weight tiles for all of them; attention items and merge
+// tasks are per (sequence, ...).
 constexpr int kBatchSeqs = 4;
 constexpr int kMaxSeqs = kBatchSeqs;
 constexpr int kMaxSplits = 18;
